@@ -1,0 +1,200 @@
+/* libqwen_cuda -- C ABI of the B200 Qwen3.5 hybrid (Gated DeltaNet + gated attention)
+ * forward pass.
+ *
+ * This is the drop-in boundary under the reference engine's C++ API. Each entry point
+ * names the reference interface it replaces (paths inside the reference project).
+ * The C++ classes of host/ (QwenModel, QwenForward) are thin wrappers over these
+ * calls, and any FFI (ctypes, cgo, JNI) can bind them directly.
+ *
+ * Rules:
+ *  - Every call returns an int status: QWC_OK (0) or a negative QWC_E* code. The
+ *    message of the last failure on a handle is in qwc_last_error(handle); failures
+ *    before a handle exists are in qwc_last_error(NULL).
+ *  - One CUDA stream per handle. A handle is not thread-safe; use one host thread per
+ *    handle (the reference objects are single-threaded as well).
+ *  - Host buffers passed in are owned by the caller and only read/written during the
+ *    call. Device buffers are owned by the handle and allocated once in qwc_create
+ *    (weights, GDN recurrent and conv state, KV cache, scratch). qwc_step and
+ *    qwc_generate_greedy allocate nothing.
+ *  - No C++ or CUDA types cross this boundary; "stream" arguments of the kernel-level
+ *    entry points are cudaStream_t passed as void* (NULL = default stream).
+ */
+#ifndef QWEN_CUDA_H
+#define QWEN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QWC_OK 0
+#define QWC_E_INVALID (-1)     /* bad argument (null pointer, size, token id, ...) */
+#define QWC_E_CUDA (-2)        /* a CUDA runtime call failed */
+#define QWC_E_MISSING (-3)     /* a required tensor is absent from the checkpoint */
+#define QWC_E_SHAPE (-4)       /* a tensor or config value has an unsupported shape */
+#define QWC_E_CONTEXT (-5)     /* position would exceed max_context */
+#define QWC_E_IO (-6)          /* a file could not be read or parsed */
+#define QWC_E_DEVICE (-7)      /* a kernel reported an error (bounded wait expired) */
+#define QWC_E_OOM (-8)         /* device allocation failed */
+
+#define QWC_DTYPE_F32 0
+#define QWC_DTYPE_BF16 1
+
+/* ModelConfig (include/model_config.h:11-63), flattened to plain C. */
+typedef struct {
+    int hidden_size;           /* hidden_size */
+    int n_layers_total;        /* num_hidden_layers */
+    int n_layers_gdn;          /* derived: total - total / interval */
+    int n_layers_attn;         /* derived: total / interval */
+    int gdn_k_heads;           /* linear_num_key_heads */
+    int gdn_v_heads;           /* linear_num_value_heads */
+    int gdn_k_head_dim;        /* linear_key_head_dim */
+    int gdn_v_head_dim;        /* linear_value_head_dim */
+    int gdn_conv_kernel;       /* linear_conv_kernel_dim */
+    int attn_q_heads;          /* num_attention_heads */
+    int attn_kv_heads;         /* num_key_value_heads */
+    int attn_head_dim;         /* head_dim */
+    int ffn_intermediate;      /* intermediate_size */
+    int vocab_size;            /* vocab_size */
+    int native_max_context;    /* max_position_embeddings */
+    int attn_interval;         /* full_attention_interval; layer L is attention iff (L+1)%interval==0 */
+    int tie_word_embeddings;   /* tie_word_embeddings */
+    float rms_norm_eps;        /* rms_norm_eps */
+    float partial_rotary_factor; /* partial_rotary_factor */
+    double rope_theta;         /* rope_theta */
+    int64_t n_params;          /* derived, as load_model_config computes it */
+} qwc_config;
+
+/* One checkpoint tensor as it sits in host memory (a safetensors entry,
+ * include/safetensors_loader.h:26-33). Matrices must be BF16; vectors may be F32 or BF16. */
+typedef struct {
+    const char* name;          /* Hugging Face name, e.g. model.language_model.norm.weight */
+    int dtype;                 /* QWC_DTYPE_F32 or QWC_DTYPE_BF16 */
+    int ndim;
+    int64_t shape[4];
+    const void* data;          /* host pointer, read during qwc_create only */
+} qwc_tensor;
+
+/* MemoryBudget (include/memory_budget.h:6-18): bytes per arena. */
+typedef struct {
+    uint64_t weight_bytes;
+    uint64_t gdn_state_bytes;
+    uint64_t gdn_conv_bytes;
+    uint64_t kv_cache_bytes;
+    uint64_t activation_bytes;
+    uint64_t vision_scratch_bytes;
+} qwc_budget;
+
+typedef struct qwc_handle qwc_handle;
+
+/* ---------------------------------------------------------------- config / budget */
+
+/* load_model_config (src/config_loader.cpp:59-108): fills *cfg from config.json
+ * (text_config preferred); keys that are absent keep the Qwen3.5-0.8B defaults. Returns
+ * QWC_E_IO (with defaults in *cfg) when the file cannot be read. */
+int qwc_load_config(const char* config_json_path, qwc_config* cfg);
+
+/* The ModelConfig defaults (include/model_config.h:11-63). */
+void qwc_default_config(qwc_config* cfg);
+
+/* compute_budget (src/memory_budget.cpp:30-54). */
+int qwc_compute_budget(const qwc_config* cfg, int bytes_per_weight, int max_context,
+                       int kv_bytes_per_elem, int max_vision_tiles, int vit_dim,
+                       qwc_budget* out);
+
+/* solve_max_context (src/memory_budget.cpp:56-81): -1 when the fixed costs do not fit. */
+int64_t qwc_solve_max_context(const qwc_config* cfg, uint64_t ram_budget_bytes,
+                              uint64_t weight_bytes, uint64_t gdn_state_bytes,
+                              uint64_t activation_bytes, uint64_t vision_scratch_bytes,
+                              uint64_t safety_margin_bytes, int kv_bytes_per_elem);
+
+/* ---------------------------------------------------------------- model lifetime */
+
+/* QwenModel::QwenModel (src/qwen_model.cpp:12-96): resolves every weight by name,
+ * uploads them to `device` in the decode layout, and allocates all device arenas once
+ * (sized by the memory equation). kv_dtype: QWC_DTYPE_F32 (the reference's cache
+ * type) or QWC_DTYPE_BF16. Missing tensors -> QWC_E_MISSING with the name in the
+ * error message. */
+int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors,
+               int max_context, int kv_dtype, int device, qwc_handle** out);
+
+/* Convenience: load_model_config + SafeTensors::load_model (main.cpp:21-27) + qwc_create. */
+int qwc_create_from_dir(const char* model_dir, int max_context, int kv_dtype, int device,
+                        qwc_handle** out);
+
+void qwc_destroy(qwc_handle* h);
+
+/* Message of the last failure on h (or of the last handle-less failure if h is NULL). */
+const char* qwc_last_error(const qwc_handle* h);
+
+/* QwenModel::budget (include/qwen_model.h:31): the arenas as planned + allocated. */
+int qwc_get_budget(const qwc_handle* h, qwc_budget* out);
+int qwc_get_config(const qwc_handle* h, qwc_config* out);
+
+/* ---------------------------------------------------------------- decode */
+
+/* QwenModel::reset (src/qwen_model.cpp:98-104): zero KV, GDN and conv state; pos = 0. */
+int qwc_reset(qwc_handle* h);
+
+/* QwenModel::position (include/qwen_model.h:27). */
+int qwc_position(const qwc_handle* h);
+
+/* QwenModel::step (src/qwen_model.cpp:211-239): one token through all layers (one CUDA
+ * graph replay). logits_host: [vocab] floats or NULL; argmax_out: the greedy id
+ * (lowest index among equal maxima) or NULL. */
+int qwc_step(qwc_handle* h, int token, float* logits_host, int* argmax_out);
+
+/* QwenModel::generate_greedy (src/qwen_model.cpp:241-255): reset, feed the prompt one
+ * token at a time, then n_new greedy tokens; the argmax -> next-token feedback stays on
+ * the device. out_tokens: n_new ids. */
+int qwc_generate_greedy(qwc_handle* h, const int* prompt, int n_prompt, int n_new,
+                        int* out_tokens);
+
+/* ---------------------------------------------------------------- prefill */
+
+/* QwenForward::prefill (src/qwen_forward.cpp:154-206): stateless forward pass over
+ * ids[T]; writes T*vocab logits (or only the last row if last_only). The decode state of
+ * h is not touched. */
+int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only);
+
+/* Prefill that also seeds the decode state (the reference equivalent is stepping the
+ * prompt through QwenModel::step, src/qwen_model.cpp:245): resets h, runs ids[T] and
+ * leaves position() == T with KV / GDN / conv state filled. logits_out: the last
+ * position's [vocab] logits, or NULL. */
+int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out);
+
+/* ---------------------------------------------------------------- kernel level */
+
+/* matmul(const WeightView&, ...) (src/forward_pass.cpp:65-75) on device memory:
+ * y[out_dim] = W[out_dim, in_dim](bf16, row-major) . x[in_dim](fp32), fp32 accumulate.
+ * in_dim must be a multiple of 8 and W 16-byte aligned. */
+int qwc_gemv_bf16(const uint16_t* W, const float* x, float* y, int out_dim, int in_dim,
+                  void* stream);
+
+/* The decode GDN mixer core of gdn_step (src/qwen_model.cpp:173-207) for one token on
+ * device memory, as used by step(): conv over the rolling state, SiLU, l2norm(q,k),
+ * gates, delta-rule update of S and o = S^T q (before the gated norm).
+ *   mixed [C] raw conv input (C = 2*KH*DK + VH*DV), a/b [VH] raw gate inputs,
+ *   conv_w [C][K] fp32, neg_exp_A [VH] = -exp(A_log), dt_bias [VH],
+ *   conv_ring [C][K] fp32 rolling state addressed by pos % K (zero at pos 0),
+ *   state [VH][DK][DV] fp32 (the reference's S layout), out [VH][DV].
+ * DK = DV = 128 and K = 4 are supported. */
+int qwc_gdn_decode_step(const float* mixed, const float* a, const float* b,
+                        const float* conv_w, const float* neg_exp_A, const float* dt_bias,
+                        float* conv_ring, float* state, float* out, int KH, int VH, int pos,
+                        void* stream);
+
+/* Attention of one query over a KV cache on device memory (the loop of attn_step,
+ * src/qwen_model.cpp:134-150): q [NQ][HD] (normed and roped), gate [NQ][HD],
+ * K/V cache [NKV][max_ctx][HD] of kv_dtype, positions 0..n_ctx-1; out [NQ][HD] =
+ * softmax(q K^T / sqrt(HD)) V * sigmoid(gate). HD = 256 is supported. */
+int qwc_attention_decode(const float* q, const float* gate, const void* k_cache,
+                         const void* v_cache, int kv_dtype, int NQ, int NKV, int max_ctx,
+                         int n_ctx, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN_CUDA_H */

@@ -1,0 +1,206 @@
+"""ctypes binding of libqwen_cuda's C ABI (include/qwen_cuda.h).
+
+``Model`` mirrors the reference's ``QwenModel`` (``reset``, ``step``, ``position``,
+``generate_greedy``, ``budget``) plus the ``QwenForward::prefill`` semantics
+(``forward_logits``) and the state-seeding ``prefill``. The kernel-level functions
+take device pointers (e.g. ``torch.Tensor.data_ptr()``) and a CUDA stream handle.
+
+Loading fails loudly when the library is not built: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import LIB_PATH
+
+QWC_OK = 0
+ERRORS = {-1: "QWC_E_INVALID", -2: "QWC_E_CUDA", -3: "QWC_E_MISSING", -4: "QWC_E_SHAPE",
+          -5: "QWC_E_CONTEXT", -6: "QWC_E_IO", -7: "QWC_E_DEVICE", -8: "QWC_E_OOM"}
+DTYPE_F32, DTYPE_BF16 = 0, 1
+
+# every symbol include/qwen_cuda.h declares
+EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_solve_max_context",
+           "qwc_create", "qwc_create_from_dir", "qwc_destroy", "qwc_last_error", "qwc_get_budget",
+           "qwc_get_config", "qwc_reset", "qwc_position", "qwc_step", "qwc_generate_greedy",
+           "qwc_forward_logits", "qwc_prefill", "qwc_gemv_bf16", "qwc_gdn_decode_step",
+           "qwc_attention_decode")
+
+
+class qwc_config(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "hidden_size", "n_layers_total", "n_layers_gdn", "n_layers_attn", "gdn_k_heads",
+        "gdn_v_heads", "gdn_k_head_dim", "gdn_v_head_dim", "gdn_conv_kernel", "attn_q_heads",
+        "attn_kv_heads", "attn_head_dim", "ffn_intermediate", "vocab_size", "native_max_context",
+        "attn_interval", "tie_word_embeddings")] + [
+        ("rms_norm_eps", C.c_float), ("partial_rotary_factor", C.c_float),
+        ("rope_theta", C.c_double), ("n_params", C.c_int64)]
+
+
+class qwc_budget(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in (
+        "weight_bytes", "gdn_state_bytes", "gdn_conv_bytes", "kv_cache_bytes",
+        "activation_bytes", "vision_scratch_bytes")]
+
+    def as_dict(self):
+        return {n: int(getattr(self, n)) for n, _ in self._fields_}
+
+
+class qwc_tensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int), ("ndim", C.c_int),
+                ("shape", C.c_int64 * 4), ("data", C.c_void_p)]
+
+
+class QwcError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """The loaded libqwen_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(f"{LIB_PATH} is not built; run __graft_entry__.build()")
+    L = C.CDLL(LIB_PATH)
+    vp, ip, fp = C.c_void_p, C.POINTER(C.c_int), C.c_void_p
+    L.qwc_load_config.argtypes = [C.c_char_p, C.POINTER(qwc_config)]
+    L.qwc_default_config.argtypes = [C.POINTER(qwc_config)]
+    L.qwc_default_config.restype = None
+    L.qwc_compute_budget.argtypes = [C.POINTER(qwc_config), C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, C.POINTER(qwc_budget)]
+    L.qwc_solve_max_context.argtypes = [C.POINTER(qwc_config)] + [C.c_uint64] * 6 + [C.c_int]
+    L.qwc_solve_max_context.restype = C.c_int64
+    L.qwc_create.argtypes = [C.POINTER(qwc_config), C.POINTER(qwc_tensor), C.c_int, C.c_int,
+                             C.c_int, C.c_int, C.POINTER(vp)]
+    L.qwc_create_from_dir.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]
+    L.qwc_destroy.argtypes = [vp]
+    L.qwc_destroy.restype = None
+    L.qwc_last_error.argtypes = [vp]
+    L.qwc_last_error.restype = C.c_char_p
+    L.qwc_get_budget.argtypes = [vp, C.POINTER(qwc_budget)]
+    L.qwc_get_config.argtypes = [vp, C.POINTER(qwc_config)]
+    L.qwc_reset.argtypes = [vp]
+    L.qwc_position.argtypes = [vp]
+    L.qwc_step.argtypes = [vp, C.c_int, fp, ip]
+    L.qwc_generate_greedy.argtypes = [vp, ip, C.c_int, C.c_int, ip]
+    L.qwc_forward_logits.argtypes = [vp, ip, C.c_int, fp, C.c_int]
+    L.qwc_prefill.argtypes = [vp, ip, C.c_int, fp]
+    L.qwc_gemv_bf16.argtypes = [vp, vp, vp, C.c_int, C.c_int, vp]
+    L.qwc_gdn_decode_step.argtypes = [vp] * 9 + [C.c_int, C.c_int, C.c_int, vp]
+    L.qwc_attention_decode.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_int, vp, vp]
+    _lib = L
+    return L
+
+
+def check(rc, handle=None):
+    if rc != QWC_OK:
+        msg = lib().qwc_last_error(handle)
+        raise QwcError(rc, msg.decode() if msg else "")
+    return rc
+
+
+def _iptr(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_int))
+
+
+def load_config(path: str) -> qwc_config:
+    c = qwc_config()
+    check(lib().qwc_load_config(path.encode(), C.byref(c)))
+    return c
+
+
+def compute_budget(cfg: qwc_config, bpw=2, max_context=1024, kv_bytes=4, tiles=4, vit=1024):
+    b = qwc_budget()
+    check(lib().qwc_compute_budget(C.byref(cfg), bpw, max_context, kv_bytes, tiles, vit, C.byref(b)))
+    return b.as_dict()
+
+
+class Model:
+    """One device-resident model + decode state (QwenModel over the C ABI)."""
+
+    def __init__(self, model_dir: str, max_context: int = 4096, kv_dtype: int = DTYPE_F32,
+                 device: int = 0):
+        h = C.c_void_p()
+        check(lib().qwc_create_from_dir(model_dir.encode(), max_context, kv_dtype, device,
+                                        C.byref(h)))
+        self._h = h
+        cfg = qwc_config()
+        check(lib().qwc_get_config(self._h, C.byref(cfg)), self._h)
+        self.cfg = cfg
+        self.vocab = cfg.vocab_size
+        self.max_context = max_context
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().qwc_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def reset(self):
+        check(lib().qwc_reset(self._h), self._h)
+
+    def position(self) -> int:
+        return lib().qwc_position(self._h)
+
+    def budget(self) -> dict:
+        b = qwc_budget()
+        check(lib().qwc_get_budget(self._h, C.byref(b)), self._h)
+        return b.as_dict()
+
+    def step(self, token: int, logits: bool = True):
+        """QwenModel::step: returns (logits[vocab] or None, greedy id)."""
+        lg = np.empty(self.vocab, np.float32) if logits else None
+        am = C.c_int(-1)
+        check(lib().qwc_step(self._h, int(token), lg.ctypes.data if logits else None,
+                             C.byref(am)), self._h)
+        return lg, am.value
+
+    def generate_greedy(self, prompt, n_new: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(n_new, 1), np.int32)
+        check(lib().qwc_generate_greedy(self._h, _iptr(p), len(p), n_new, _iptr(out)), self._h)
+        return out[:n_new] if len(p) else out[:0]
+
+    def forward_logits(self, ids, last_only: bool = False) -> np.ndarray:
+        """QwenForward::prefill semantics (stateless): [T, vocab] logits."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        T = len(ids)
+        lg = np.empty((1 if last_only else T, self.vocab), np.float32)
+        check(lib().qwc_forward_logits(self._h, _iptr(ids), T, lg.ctypes.data,
+                                       1 if last_only else 0), self._h)
+        return lg
+
+    def prefill(self, ids, logits: bool = True):
+        """Prefill that seeds the decode state; returns the last position's logits."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        lg = np.empty(self.vocab, np.float32) if logits else None
+        check(lib().qwc_prefill(self._h, _iptr(ids), len(ids),
+                                lg.ctypes.data if logits else None), self._h)
+        return lg
+
+
+def gemv_bf16(W_ptr, x_ptr, y_ptr, out_dim, in_dim, stream=0):
+    check(lib().qwc_gemv_bf16(W_ptr, x_ptr, y_ptr, out_dim, in_dim, stream))
+
+
+def gdn_decode_step(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state, out, KH, VH,
+                    pos, stream=0):
+    check(lib().qwc_gdn_decode_step(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state,
+                                    out, KH, VH, pos, stream))
+
+
+def attention_decode(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx, n_ctx, out,
+                     stream=0):
+    check(lib().qwc_attention_decode(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx,
+                                     n_ctx, out, stream))

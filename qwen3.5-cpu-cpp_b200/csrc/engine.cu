@@ -1,0 +1,982 @@
+// libqwen_cuda engine: the C ABI of include/qwen_cuda.h.
+//
+// Lifetime (QwenModel::QwenModel, src/qwen_model.cpp:12-96): every weight is resolved
+// by name once, re-laid out for the decode kernels and uploaded into ONE device weight
+// arena; the GDN recurrent state, the GDN conv state, the KV cache and the scratch
+// arena are each one cudaMalloc sized by the memory equation; the decode step is
+// captured once as a CUDA graph. qwc_step / qwc_generate_greedy then only replay the
+// graph (zero allocation per token), with token id, position and the greedy argmax
+// kept on the device.
+#include "qwen_cuda.h"
+#include "kernels.h"
+
+#include <algorithm>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+using namespace qwc;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+__device__ int g_kernel_api_error;  // error word of the kernel-level entry points
+
+struct Layer {
+    int is_attn = 0, idx = 0;
+    const float* in_ln1 = nullptr;   // 1 + input_layernorm.weight
+    const float* post_ln1 = nullptr; // 1 + post_attention_layernorm.weight
+    const uint16_t* w_in = nullptr;  // GDN: [qkv ; z ; b ; a] x H   attn: [q ; k ; v] x H
+    int in_rows = 0;
+    const uint16_t* w_out = nullptr; // GDN out_proj [H][VD]   attn o_proj [H][NQ*HD]
+    int out_in = 0;
+    const uint16_t* w_gu = nullptr;  // [I][2H], row i = [gate_i | up_i]
+    const uint16_t* w_down = nullptr;// [H][I]
+    // GDN
+    const float* conv_w = nullptr;   // [C][4]
+    const float* neg_exp_A = nullptr;// [VH]
+    const float* dt_bias = nullptr;  // [VH]
+    const float* gn_w = nullptr;     // [DV]
+    // attention
+    const float* qn1 = nullptr;      // 1 + q_norm
+    const float* kn1 = nullptr;      // 1 + k_norm
+};
+
+// Where the mutable state of one sequence lives (the handle's decode state, or a
+// temporary one for the stateless forward pass).
+struct StateView {
+    float* gdn_state = nullptr;  // [n_gdn][VH][DK][DV]
+    float* conv_ring = nullptr;  // [n_gdn][C][4]
+    void* kv = nullptr;          // [n_attn][2][NKV][max_ctx][HD]
+    int max_ctx = 0;
+};
+
+}  // namespace
+
+struct qwc_handle {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    qwc_config cfg{};
+    int max_ctx = 0, kv_dtype = QWC_DTYPE_F32, kv_bytes = 4;
+    int H = 0, I = 0, V = 0, L = 0, NQ = 0, NKV = 0, HD = 0, ROT = 0;
+    int KH = 0, VH = 0, DK = 0, DV = 0, KD = 0, VD = 0, C = 0, KER = 0;
+    int n_gdn = 0, n_attn = 0, nsplit = 1;
+    float eps = 1e-6f;
+
+    // arenas
+    uint8_t* w_arena = nullptr;
+    size_t w_bytes = 0;
+    StateView st;
+    size_t gdn_bytes = 0, conv_bytes = 0, kvc_bytes = 0;
+    uint8_t* scratch = nullptr;
+    size_t scratch_bytes = 0;
+
+    std::vector<Layer> layers;
+    const uint16_t* embed = nullptr;
+    const uint16_t* head = nullptr;
+    const float* final_ln1 = nullptr;
+    const double* inv_freq = nullptr;
+
+    // scratch views
+    float *hidden = nullptr, *proj = nullptr, *mix = nullptr, *ffn_h = nullptr, *logits = nullptr;
+    float *am_val = nullptr, *part_o = nullptr, *part_ml = nullptr;
+    int *am_idx = nullptr, *tokens = nullptr, *pos = nullptr, *n_prompt = nullptr, *argmax = nullptr;
+    int* dev_err = nullptr;
+    unsigned *am_counter = nullptr, *attn_counters = nullptr;
+
+    int* h_pin = nullptr;  // pinned host ints for small transfers
+
+    cudaGraphExec_t graph = nullptr;
+    bool use_graph = true, use_pdl = true;
+    int pos_host = 0;
+    qwc_budget budget{};
+    std::string err;
+};
+
+// ------------------------------------------------------------------ error helpers
+static int fail(qwc_handle* h, int code, const std::string& msg) {
+    if (h) h->err = msg;
+    g_last_error = msg;
+    return code;
+}
+#define CU(call)                                                                         \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess)                                                           \
+            return fail(h, QWC_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+static int check_device_error(qwc_handle* h) {
+    int v = 0;
+    CU(cudaMemcpyAsync(&h->h_pin[8], h->dev_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    CU(cudaStreamSynchronize(h->stream));
+    v = h->h_pin[8];
+    if (v != 0) {
+        cudaMemsetAsync(h->dev_err, 0, sizeof(int), h->stream);
+        return fail(h, QWC_E_DEVICE, "device kernel reported error code " + std::to_string(v));
+    }
+    return QWC_OK;
+}
+
+// ------------------------------------------------------------------ config / budget
+extern "C" void qwc_default_config(qwc_config* c) {
+    // ModelConfig defaults (include/model_config.h:11-63)
+    std::memset(c, 0, sizeof(*c));
+    c->hidden_size = 1024;
+    c->n_layers_total = 24;
+    c->n_layers_gdn = 18;
+    c->n_layers_attn = 6;
+    c->gdn_k_heads = 16;
+    c->gdn_v_heads = 16;
+    c->gdn_k_head_dim = 128;
+    c->gdn_v_head_dim = 128;
+    c->gdn_conv_kernel = 4;
+    c->attn_q_heads = 8;
+    c->attn_kv_heads = 2;
+    c->attn_head_dim = 256;
+    c->ffn_intermediate = 3584;
+    c->vocab_size = 248320;
+    c->native_max_context = 262144;
+    c->rms_norm_eps = 1e-6f;
+    c->tie_word_embeddings = 1;
+    c->rope_theta = 10000000.0;
+    c->partial_rotary_factor = 0.25f;
+    c->attn_interval = 4;
+    c->n_params = 800000000LL;
+}
+
+static size_t conv_state_bytes_eq(const qwc_config* c) {
+    // gdn_conv_state_bytes (include/memory_budget.h:23-28)
+    size_t kd = (size_t)c->gdn_k_heads * c->gdn_k_head_dim, vd = (size_t)c->gdn_v_heads * c->gdn_v_head_dim;
+    return (size_t)c->n_layers_gdn * (kd * 2 + vd) * (c->gdn_conv_kernel - 1) * sizeof(float);
+}
+
+extern "C" int qwc_compute_budget(const qwc_config* c, int bpw, int max_context, int kvb,
+                                  int max_vision_tiles, int vit_dim, qwc_budget* out) {
+    if (!c || !out) return fail(nullptr, QWC_E_INVALID, "qwc_compute_budget: null argument");
+    // compute_budget (src/memory_budget.cpp:30-54) and its two estimators (:4-28)
+    out->weight_bytes = (uint64_t)c->n_params * (uint64_t)bpw;
+    out->gdn_state_bytes = (uint64_t)c->n_layers_gdn * c->gdn_v_heads * c->gdn_k_head_dim *
+                           c->gdn_v_head_dim * sizeof(float);
+    out->gdn_conv_bytes = conv_state_bytes_eq(c);
+    out->kv_cache_bytes = (uint64_t)c->n_layers_attn * (uint64_t)max_context * 2 * c->attn_kv_heads *
+                          c->attn_head_dim * kvb;
+    size_t ffn = (size_t)c->ffn_intermediate * sizeof(float) * 2;
+    size_t attn = (size_t)(c->attn_q_heads * c->attn_head_dim + 2 * c->attn_kv_heads * c->attn_head_dim) *
+                  sizeof(float);
+    size_t gdn = (size_t)(3 * c->gdn_v_heads * c->gdn_v_head_dim) * sizeof(float);
+    size_t act = ffn;
+    if (attn > act) act = attn;
+    if (gdn > act) act = gdn;
+    out->activation_bytes = act;
+    const size_t ppt = 256;
+    out->vision_scratch_bytes = (uint64_t)max_vision_tiles * ppt * vit_dim * sizeof(float) +
+                                (uint64_t)ppt * vit_dim * sizeof(float) * 2;
+    return QWC_OK;
+}
+
+extern "C" int64_t qwc_solve_max_context(const qwc_config* c, uint64_t ram, uint64_t wb, uint64_t gb,
+                                         uint64_t ab, uint64_t vb, uint64_t margin, int kvb) {
+    // solve_max_context (src/memory_budget.cpp:56-81)
+    uint64_t fixed = wb + gb + ab + vb + margin;
+    if (fixed >= ram) return -1;
+    uint64_t per_tok = (uint64_t)c->n_layers_attn * 2 * c->attn_kv_heads * c->attn_head_dim * kvb;
+    if (per_tok == 0) return -1;
+    int64_t ctx = (int64_t)((ram - fixed) / per_tok);
+    return ctx < c->native_max_context ? ctx : c->native_max_context;
+}
+
+extern "C" const char* qwc_last_error(const qwc_handle* h) {
+    return h ? h->err.c_str() : g_last_error.c_str();
+}
+
+// ------------------------------------------------------------------ weight upload
+namespace {
+
+struct HostTensor {
+    const qwc_tensor* t;
+    int64_t numel;
+};
+
+struct Builder {
+    qwc_handle* h;
+    std::unordered_map<std::string, HostTensor> by_name;
+    std::string missing;
+
+    const qwc_tensor* find(const std::string& n) {
+        auto it = by_name.find(n);
+        return it == by_name.end() ? nullptr : it->second.t;
+    }
+    const qwc_tensor* need(const std::string& n) {
+        const qwc_tensor* t = find(n);
+        if (!t && missing.empty()) missing = n;
+        return t;
+    }
+};
+
+int64_t numel_of(const qwc_tensor* t) {
+    int64_t n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+    return t->ndim ? n : 0;
+}
+
+float elem_f32(const qwc_tensor* t, int64_t i) {
+    if (t->dtype == QWC_DTYPE_F32) return static_cast<const float*>(t->data)[i];
+    uint32_t u = (uint32_t)static_cast<const uint16_t*>(t->data)[i] << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// A bump allocator over the weight arena: first pass measures, second pass places.
+struct Arena {
+    uint8_t* base = nullptr;
+    size_t off = 0;
+    void* take(size_t bytes) {
+        off = (off + 255) & ~(size_t)255;
+        void* p = base ? base + off : nullptr;
+        off += bytes;
+        return p;
+    }
+};
+
+}  // namespace
+
+static int upload_f32(qwc_handle* h, float* dst, const std::vector<float>& v) {
+    CU(cudaMemcpy(dst, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return QWC_OK;
+}
+
+// Copies a BF16 matrix [rows][cols] into dst with destination row pitch `dpitch` elements.
+static int upload_mat(qwc_handle* h, uint16_t* dst, size_t dpitch, const qwc_tensor* t, int64_t rows,
+                      int64_t cols) {
+    if (t->dtype != QWC_DTYPE_BF16)
+        return fail(h, QWC_E_SHAPE, std::string("matrix ") + t->name + " must be BF16");
+    if (numel_of(t) != rows * cols)
+        return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected shape");
+    CU(cudaMemcpy2D(dst, dpitch * 2, t->data, cols * 2, cols * 2, rows, cudaMemcpyHostToDevice));
+    return QWC_OK;
+}
+
+static int vec_f32(qwc_handle* h, const qwc_tensor* t, int64_t n, std::vector<float>& out, float add = 0.f) {
+    if (numel_of(t) != n) return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected size");
+    out.resize(n);
+    for (int64_t i = 0; i < n; ++i) out[i] = add == 0.f ? elem_f32(t, i) : (add + elem_f32(t, i));
+    return QWC_OK;
+}
+
+// Resolve, lay out and upload all weights. With arena.base == nullptr only measures.
+static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
+    const bool doit = a.base != nullptr;
+    const int H = h->H, I = h->I;
+    const std::string LM = "model.language_model.";
+    int ai = 0, gi = 0;
+    h->layers.assign(h->L, Layer());
+    std::vector<float> tmp;
+    for (int L = 0; L < h->L; ++L) {
+        Layer& lw = h->layers[L];
+        const std::string P = LM + "layers." + std::to_string(L) + ".";
+        const qwc_tensor* iln = b.need(P + "input_layernorm.weight");
+        const qwc_tensor* pln = b.need(P + "post_attention_layernorm.weight");
+        const qwc_tensor* gp = b.need(P + "mlp.gate_proj.weight");
+        const qwc_tensor* up = b.need(P + "mlp.up_proj.weight");
+        const qwc_tensor* dp = b.need(P + "mlp.down_proj.weight");
+        lw.in_ln1 = (const float*)a.take((size_t)H * 4);
+        lw.post_ln1 = (const float*)a.take((size_t)H * 4);
+        lw.w_gu = (const uint16_t*)a.take((size_t)I * 2 * H * 2);
+        lw.w_down = (const uint16_t*)a.take((size_t)H * I * 2);
+        const bool attn = (L + 1) % h->cfg.attn_interval == 0;
+        lw.is_attn = attn ? 1 : 0;
+        if (attn) {
+            lw.idx = ai++;
+            const std::string A = P + "self_attn.";
+            const qwc_tensor* q = b.need(A + "q_proj.weight");
+            const qwc_tensor* k = b.need(A + "k_proj.weight");
+            const qwc_tensor* v = b.need(A + "v_proj.weight");
+            const qwc_tensor* o = b.need(A + "o_proj.weight");
+            const qwc_tensor* qn = b.need(A + "q_norm.weight");
+            const qwc_tensor* kn = b.need(A + "k_norm.weight");
+            const int qr = 2 * h->NQ * h->HD, kr = h->NKV * h->HD;
+            lw.in_rows = qr + 2 * kr;
+            lw.w_in = (const uint16_t*)a.take((size_t)lw.in_rows * H * 2);
+            lw.out_in = h->NQ * h->HD;
+            lw.w_out = (const uint16_t*)a.take((size_t)H * lw.out_in * 2);
+            lw.qn1 = (const float*)a.take((size_t)h->HD * 4);
+            lw.kn1 = (const float*)a.take((size_t)h->HD * 4);
+            if (doit && b.missing.empty()) {
+                uint16_t* wi = const_cast<uint16_t*>(lw.w_in);
+                int rc;
+                if ((rc = upload_mat(h, wi, H, q, qr, H))) return rc;
+                if ((rc = upload_mat(h, wi + (size_t)qr * H, H, k, kr, H))) return rc;
+                if ((rc = upload_mat(h, wi + (size_t)(qr + kr) * H, H, v, kr, H))) return rc;
+                if ((rc = upload_mat(h, const_cast<uint16_t*>(lw.w_out), lw.out_in, o, H, lw.out_in))) return rc;
+                if ((rc = vec_f32(h, qn, h->HD, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.qn1), tmp))) return rc;
+                if ((rc = vec_f32(h, kn, h->HD, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.kn1), tmp))) return rc;
+            }
+        } else {
+            lw.idx = gi++;
+            const std::string G = P + "linear_attn.";
+            const qwc_tensor* qkv = b.need(G + "in_proj_qkv.weight");
+            const qwc_tensor* z = b.need(G + "in_proj_z.weight");
+            const qwc_tensor* bb = b.need(G + "in_proj_b.weight");
+            const qwc_tensor* aa = b.need(G + "in_proj_a.weight");
+            const qwc_tensor* cw = b.need(G + "conv1d.weight");
+            const qwc_tensor* dt = b.need(G + "dt_bias");
+            const qwc_tensor* al = b.need(G + "A_log");
+            const qwc_tensor* gn = b.need(G + "norm.weight");
+            const qwc_tensor* op = b.need(G + "out_proj.weight");
+            lw.in_rows = h->C + h->VD + 2 * h->VH;
+            lw.w_in = (const uint16_t*)a.take((size_t)lw.in_rows * H * 2);
+            lw.out_in = h->VD;
+            lw.w_out = (const uint16_t*)a.take((size_t)H * h->VD * 2);
+            lw.conv_w = (const float*)a.take((size_t)h->C * 4 * 4);
+            lw.neg_exp_A = (const float*)a.take((size_t)h->VH * 4);
+            lw.dt_bias = (const float*)a.take((size_t)h->VH * 4);
+            lw.gn_w = (const float*)a.take((size_t)h->DV * 4);
+            if (doit && b.missing.empty()) {
+                uint16_t* wi = const_cast<uint16_t*>(lw.w_in);
+                int rc;
+                if ((rc = upload_mat(h, wi, H, qkv, h->C, H))) return rc;
+                if ((rc = upload_mat(h, wi + (size_t)h->C * H, H, z, h->VD, H))) return rc;
+                if ((rc = upload_mat(h, wi + (size_t)(h->C + h->VD) * H, H, bb, h->VH, H))) return rc;
+                if ((rc = upload_mat(h, wi + (size_t)(h->C + h->VD + h->VH) * H, H, aa, h->VH, H))) return rc;
+                if ((rc = upload_mat(h, const_cast<uint16_t*>(lw.w_out), h->VD, op, H, h->VD))) return rc;
+                if ((rc = vec_f32(h, cw, (int64_t)h->C * h->KER, tmp))) return rc;
+                if ((rc = upload_f32(h, const_cast<float*>(lw.conv_w), tmp))) return rc;
+                // -exp(A_log) with the host expf, as the reference evaluates it
+                if ((rc = vec_f32(h, al, h->VH, tmp))) return rc;
+                for (auto& x : tmp) x = -std::exp(x);
+                if ((rc = upload_f32(h, const_cast<float*>(lw.neg_exp_A), tmp))) return rc;
+                if ((rc = vec_f32(h, dt, h->VH, tmp)) || (rc = upload_f32(h, const_cast<float*>(lw.dt_bias), tmp))) return rc;
+                if ((rc = vec_f32(h, gn, h->DV, tmp)) || (rc = upload_f32(h, const_cast<float*>(lw.gn_w), tmp))) return rc;
+            }
+        }
+        if (doit && b.missing.empty()) {
+            int rc;
+            if ((rc = vec_f32(h, iln, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.in_ln1), tmp))) return rc;
+            if ((rc = vec_f32(h, pln, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.post_ln1), tmp))) return rc;
+            uint16_t* gu = const_cast<uint16_t*>(lw.w_gu);
+            if ((rc = upload_mat(h, gu, 2 * (size_t)H, gp, I, H))) return rc;
+            if ((rc = upload_mat(h, gu + H, 2 * (size_t)H, up, I, H))) return rc;
+            if ((rc = upload_mat(h, const_cast<uint16_t*>(lw.w_down), I, dp, H, I))) return rc;
+        }
+    }
+    const qwc_tensor* emb = b.need(LM + "embed_tokens.weight");
+    const qwc_tensor* fn = b.need(LM + "norm.weight");
+    // dedicated lm_head if present, else the tied embedding (src/qwen_model.cpp:67-69)
+    const qwc_tensor* lmh = b.find("lm_head.weight");
+    if (!lmh) lmh = b.find(LM + "lm_head.weight");
+    h->embed = (const uint16_t*)a.take((size_t)h->V * H * 2);
+    h->head = lmh ? (const uint16_t*)a.take((size_t)h->V * H * 2) : h->embed;
+    h->final_ln1 = (const float*)a.take((size_t)H * 4);
+    h->inv_freq = (const double*)a.take((size_t)(h->ROT / 2 + 1) * 8);
+    if (doit && b.missing.empty()) {
+        int rc;
+        if (emb->ndim != 2 || emb->shape[1] != H || emb->shape[0] < h->V)
+            return fail(h, QWC_E_SHAPE, "embed_tokens.weight rows < vocab_size or width != hidden_size");
+        if ((rc = upload_mat(h, const_cast<uint16_t*>(h->embed), H, emb, h->V, H) )) {
+            // the embedding may hold more rows than vocab_size: upload only vocab_size rows
+            if (emb->dtype != QWC_DTYPE_BF16) return rc;
+            CU(cudaMemcpy(const_cast<uint16_t*>(h->embed), emb->data, (size_t)h->V * H * 2, cudaMemcpyHostToDevice));
+        }
+        if (lmh) {
+            if (lmh->dtype != QWC_DTYPE_BF16 || lmh->ndim != 2 || lmh->shape[1] != H || lmh->shape[0] < h->V)
+                return fail(h, QWC_E_SHAPE, "lm_head.weight must be BF16 [>=vocab, hidden]");
+            CU(cudaMemcpy(const_cast<uint16_t*>(h->head), lmh->data, (size_t)h->V * H * 2, cudaMemcpyHostToDevice));
+        }
+        if ((rc = vec_f32(h, fn, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(h->final_ln1), tmp))) return rc;
+        std::vector<double> invf(h->ROT / 2 + 1, 0.0);
+        for (int i = 0; i < h->ROT / 2; ++i) invf[i] = std::pow(h->cfg.rope_theta, -(double)(2 * i) / h->ROT);
+        CU(cudaMemcpy(const_cast<double*>(h->inv_freq), invf.data(), invf.size() * 8, cudaMemcpyHostToDevice));
+    }
+    if (!b.missing.empty()) return fail(h, QWC_E_MISSING, "[qwen] missing weight: " + b.missing);
+    return QWC_OK;
+}
+
+// ------------------------------------------------------------------ the decode step
+static GemvParams gp_base(qwc_handle* h) {
+    GemvParams p;
+    p.eps = h->eps;
+    p.dev_err = h->dev_err;
+    return p;
+}
+
+// Enqueue one decode step (embedding -> layers -> norm -> lm_head + argmax) on h->stream.
+static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
+    const int H = h->H;
+    bool first = true;
+    auto PDL = [&]() { bool r = pdl && !first; first = false; return r; };
+    const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
+    for (int L = 0; L < h->L; ++L) {
+        const Layer& lw = h->layers[L];
+        // mixer input projection with the input RMSNorm (and the embedding at layer 0)
+        GemvParams p = gp_base(h);
+        p.W = lw.w_in;
+        p.rows = lw.in_rows;
+        p.in_dim = H;
+        p.x_len = H;
+        p.x = h->hidden;
+        p.norm_w = lw.in_ln1;
+        p.y = h->proj;
+        int pro = PRO_RMSNORM;
+        if (L == 0) {
+            pro = PRO_EMBED_RMSNORM;
+            p.embed = h->embed;
+            p.tokens = h->tokens;
+            p.pos = h->pos;
+            p.vocab = h->V;
+            p.hidden_out = h->hidden;
+        }
+        CU(launch_gemv(pro, EPI_STORE, p, gemv_grid(p.rows), h->stream, PDL()));
+        if (lw.is_attn) {
+            AttnDecodeParams a;
+            a.proj = h->proj;
+            a.qn1 = lw.qn1;
+            a.kn1 = lw.kn1;
+            a.inv_freq = h->inv_freq;
+            uint8_t* kvl = static_cast<uint8_t*>(sv.kv) + kv_layer * lw.idx;
+            a.k_cache = kvl;
+            a.v_cache = kvl + kv_layer / 2;
+            a.kv_bf16 = h->kv_dtype == QWC_DTYPE_BF16;
+            a.max_ctx = sv.max_ctx;
+            a.pos_ptr = h->pos;
+            a.part_o = h->part_o;
+            a.part_ml = h->part_ml;
+            a.counters = h->attn_counters;
+            a.out = h->mix;
+            a.NQ = h->NQ;
+            a.NKV = h->NKV;
+            a.rot = h->ROT;
+            a.nsplit = h->nsplit;
+            a.eps = h->eps;
+            CU(launch_attn_decode(a, h->stream, PDL()));
+            GemvParams o = gp_base(h);
+            o.W = lw.w_out;
+            o.rows = H;
+            o.in_dim = lw.out_in;
+            o.x_len = lw.out_in;
+            o.x = h->mix;
+            o.y = h->hidden;
+            CU(launch_gemv(PRO_PLAIN, EPI_RESIDUAL, o, gemv_grid(H), h->stream, PDL()));
+        } else {
+            GdnDecodeParams g;
+            g.mixed = h->proj;
+            g.b = h->proj + h->C + h->VD;
+            g.a = h->proj + h->C + h->VD + h->VH;
+            g.conv_w = lw.conv_w;
+            g.neg_exp_A = lw.neg_exp_A;
+            g.dt_bias = lw.dt_bias;
+            g.conv_ring = sv.conv_ring + (size_t)lw.idx * h->C * 4;
+            g.state = sv.gdn_state + (size_t)lw.idx * h->VH * h->DK * h->DV;
+            g.out = h->mix;
+            g.pos_ptr = h->pos;
+            g.KH = h->KH;
+            g.VH = h->VH;
+            CU(launch_gdn_decode(g, h->stream, PDL()));
+            GemvParams o = gp_base(h);
+            o.W = lw.w_out;
+            o.rows = H;
+            o.in_dim = h->VD;
+            o.x_len = h->VD;
+            o.x = h->mix;
+            o.z = h->proj + h->C;
+            o.norm_w = lw.gn_w;
+            o.gn_dim = h->DV;
+            o.y = h->hidden;
+            CU(launch_gemv(PRO_GATED_NORM, EPI_RESIDUAL, o, gemv_grid(H), h->stream, PDL()));
+        }
+        // FFN: post-attention RMSNorm + gate/up + SwiGLU, then down + residual
+        GemvParams f = gp_base(h);
+        f.W = lw.w_gu;
+        f.rows = h->I;
+        f.in_dim = 2 * H;
+        f.x_len = H;
+        f.x = h->hidden;
+        f.norm_w = lw.post_ln1;
+        f.y = h->ffn_h;
+        CU(launch_gemv(PRO_RMSNORM, EPI_SWIGLU, f, gemv_grid(h->I), h->stream, PDL()));
+        GemvParams d = gp_base(h);
+        d.W = lw.w_down;
+        d.rows = H;
+        d.in_dim = h->I;
+        d.x_len = h->I;
+        d.x = h->ffn_h;
+        d.y = h->hidden;
+        CU(launch_gemv(PRO_PLAIN, EPI_RESIDUAL, d, gemv_grid(H), h->stream, PDL()));
+    }
+    GemvParams o = gp_base(h);
+    o.W = h->head;
+    o.rows = h->V;
+    o.in_dim = H;
+    o.x_len = H;
+    o.x = h->hidden;
+    o.norm_w = h->final_ln1;
+    o.y = h->logits;
+    o.am_val = h->am_val;
+    o.am_idx = h->am_idx;
+    o.am_counter = h->am_counter;
+    o.argmax_out = h->argmax;
+    o.tokens_out = h->tokens;
+    o.n_prompt = h->n_prompt;
+    o.pos_inout = h->pos;
+    o.max_ctx = sv.max_ctx;
+    CU(launch_gemv(PRO_RMSNORM, EPI_ARGMAX, o, gemv_grid(h->V), h->stream, PDL()));
+    return QWC_OK;
+}
+
+static int build_graph(qwc_handle* h) {
+    if (h->graph) {
+        cudaGraphExecDestroy(h->graph);
+        h->graph = nullptr;
+    }
+    if (!h->use_graph) return QWC_OK;
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(h, h->st, h->use_pdl);
+    cudaError_t e = cudaStreamEndCapture(h->stream, &g);
+    if (rc != QWC_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(h, QWC_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&h->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(h, QWC_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+static int run_step(qwc_handle* h) {
+    if (h->graph) {
+        CU(cudaGraphLaunch(h->graph, h->stream));
+        return QWC_OK;
+    }
+    return enqueue_step(h, h->st, h->use_pdl);
+}
+
+// ------------------------------------------------------------------ create / destroy
+static int validate_config(qwc_handle* h, const qwc_config* c) {
+    if (c->hidden_size <= 0 || c->hidden_size % 8) return fail(h, QWC_E_SHAPE, "hidden_size must be a positive multiple of 8");
+    if (c->gdn_k_head_dim != 128 || c->gdn_v_head_dim != 128)
+        return fail(h, QWC_E_SHAPE, "GDN head dims other than 128 are not supported");
+    if (c->gdn_conv_kernel != 4) return fail(h, QWC_E_SHAPE, "GDN conv kernel other than 4 is not supported");
+    if (c->attn_head_dim != 256) return fail(h, QWC_E_SHAPE, "attention head_dim other than 256 is not supported");
+    if (c->attn_kv_heads <= 0 || c->attn_q_heads % c->attn_kv_heads)
+        return fail(h, QWC_E_SHAPE, "num_attention_heads must be a multiple of num_key_value_heads");
+    const int grp = c->attn_q_heads / c->attn_kv_heads;
+    if (grp != 1 && grp != 2 && grp != 4 && grp != 8) return fail(h, QWC_E_SHAPE, "GQA group must be 1, 2, 4 or 8");
+    if (c->gdn_k_heads <= 0 || c->gdn_v_heads % c->gdn_k_heads)
+        return fail(h, QWC_E_SHAPE, "linear_num_value_heads must be a multiple of linear_num_key_heads");
+    if (c->ffn_intermediate <= 0 || c->ffn_intermediate % 8) return fail(h, QWC_E_SHAPE, "intermediate_size must be a multiple of 8");
+    if (c->attn_interval <= 0 || c->n_layers_total <= 0) return fail(h, QWC_E_SHAPE, "bad layer layout");
+    const int rot = (int)(c->attn_head_dim * c->partial_rotary_factor);
+    if (rot < 0 || rot > c->attn_head_dim || rot % 2) return fail(h, QWC_E_SHAPE, "bad partial_rotary_factor");
+    if (c->vocab_size <= 0) return fail(h, QWC_E_SHAPE, "bad vocab_size");
+    return QWC_OK;
+}
+
+extern "C" void qwc_destroy(qwc_handle* h) {
+    if (!h) return;
+    cudaSetDevice(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->graph) cudaGraphExecDestroy(h->graph);
+    cudaFree(h->w_arena);
+    cudaFree(h->st.gdn_state);
+    cudaFree(h->st.conv_ring);
+    cudaFree(h->st.kv);
+    cudaFree(h->scratch);
+    if (h->h_pin) cudaFreeHost(h->h_pin);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
+                          int kv_dtype, int device, qwc_handle** out) {
+    if (!cfg || !out || (!tensors && n_tensors > 0) || max_context <= 0)
+        return fail(nullptr, QWC_E_INVALID, "qwc_create: invalid argument");
+    if (kv_dtype != QWC_DTYPE_F32 && kv_dtype != QWC_DTYPE_BF16)
+        return fail(nullptr, QWC_E_INVALID, "qwc_create: kv_dtype must be F32 or BF16");
+    *out = nullptr;
+    qwc_handle* h = new qwc_handle();
+    h->device = device;
+    h->cfg = *cfg;
+    int rc = validate_config(h, cfg);
+    if (rc) { g_last_error = h->err; delete h; return rc; }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        delete h;
+        return fail(nullptr, QWC_E_CUDA, "cudaSetDevice failed");
+    }
+    const char* ng = std::getenv("QWC_NO_GRAPH");
+    h->use_graph = !(ng && ng[0] == '1');
+    const char* np = std::getenv("QWC_NO_PDL");
+    h->use_pdl = !(np && np[0] == '1');
+    h->max_ctx = max_context;
+    h->kv_dtype = kv_dtype;
+    h->kv_bytes = kv_dtype == QWC_DTYPE_BF16 ? 2 : 4;
+    h->H = cfg->hidden_size;
+    h->I = cfg->ffn_intermediate;
+    h->V = cfg->vocab_size;
+    h->L = cfg->n_layers_total;
+    h->NQ = cfg->attn_q_heads;
+    h->NKV = cfg->attn_kv_heads;
+    h->HD = cfg->attn_head_dim;
+    h->ROT = (int)(h->HD * cfg->partial_rotary_factor);
+    h->KH = cfg->gdn_k_heads;
+    h->VH = cfg->gdn_v_heads;
+    h->DK = cfg->gdn_k_head_dim;
+    h->DV = cfg->gdn_v_head_dim;
+    h->KD = h->KH * h->DK;
+    h->VD = h->VH * h->DV;
+    h->C = 2 * h->KD + h->VD;
+    h->KER = cfg->gdn_conv_kernel;
+    h->eps = cfg->rms_norm_eps;
+    h->n_attn = h->L / cfg->attn_interval;
+    h->n_gdn = h->L - h->n_attn;
+    h->cfg.n_layers_attn = h->n_attn;
+    h->cfg.n_layers_gdn = h->n_gdn;
+
+    Builder b;
+    b.h = h;
+    for (int i = 0; i < n_tensors; ++i) {
+        if (!tensors[i].name || !tensors[i].data) continue;
+        b.by_name[tensors[i].name] = HostTensor{&tensors[i], numel_of(&tensors[i])};
+    }
+    // pass 1: measure
+    Arena meas;
+    rc = place_weights(h, b, meas);
+    if (rc) { g_last_error = h->err; delete h; return rc; }
+    h->w_bytes = meas.off;
+
+    auto bail = [&](int code) { g_last_error = h->err; qwc_destroy(h); return code; };
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(h, QWC_E_CUDA, "cudaStreamCreate failed"));
+    if (cudaMalloc(&h->w_arena, h->w_bytes) != cudaSuccess)
+        return bail(fail(h, QWC_E_OOM, "weight arena allocation failed"));
+    Arena real;
+    real.base = h->w_arena;
+    rc = place_weights(h, b, real);
+    if (rc) return bail(rc);
+
+    // state arenas, sized by the memory equation (compute_budget with bpw 2)
+    qwc_compute_budget(&h->cfg, 2, max_context, h->kv_bytes, 4, 1024, &h->budget);
+    h->gdn_bytes = h->budget.gdn_state_bytes;
+    h->kvc_bytes = h->budget.kv_cache_bytes;
+    // conv state: a ring of K slots per channel (the equation counts K-1)
+    h->conv_bytes = (size_t)h->n_gdn * h->C * 4 * sizeof(float);
+    h->st.max_ctx = max_context;
+    if (h->gdn_bytes && cudaMalloc(&h->st.gdn_state, h->gdn_bytes) != cudaSuccess)
+        return bail(fail(h, QWC_E_OOM, "GDN state allocation failed"));
+    if (h->conv_bytes && cudaMalloc(&h->st.conv_ring, h->conv_bytes) != cudaSuccess)
+        return bail(fail(h, QWC_E_OOM, "conv state allocation failed"));
+    if (h->kvc_bytes && cudaMalloc(&h->st.kv, h->kvc_bytes) != cudaSuccess)
+        return bail(fail(h, QWC_E_OOM, "KV cache allocation failed"));
+
+    // scratch arena
+    h->nsplit = attn_nsplit_for(max_context);
+    const int grp = h->NQ / h->NKV;
+    Arena s;
+    auto carve = [&](size_t bytes) { return s.take(bytes); };
+    const int proj_n = std::max(h->C + h->VD + 2 * h->VH, 2 * h->NQ * h->HD + 2 * h->NKV * h->HD);
+    const int nsm = num_sms();
+    struct { void** p; size_t bytes; } plan[] = {
+        {(void**)&h->hidden, (size_t)h->H * 4},
+        {(void**)&h->proj, (size_t)proj_n * 4},
+        {(void**)&h->mix, (size_t)std::max(h->VD, h->NQ * h->HD) * 4},
+        {(void**)&h->ffn_h, (size_t)h->I * 4},
+        {(void**)&h->logits, (size_t)h->V * 4},
+        {(void**)&h->am_val, (size_t)nsm * 4},
+        {(void**)&h->am_idx, (size_t)nsm * 4},
+        {(void**)&h->am_counter, 16},
+        {(void**)&h->attn_counters, (size_t)h->NKV * 4},
+        {(void**)&h->part_o, (size_t)h->NKV * h->nsplit * grp * h->HD * 4},
+        {(void**)&h->part_ml, (size_t)h->NKV * h->nsplit * grp * 2 * 4},
+        {(void**)&h->tokens, (size_t)(max_context + 1) * 4},
+        {(void**)&h->pos, 16},
+        {(void**)&h->n_prompt, 16},
+        {(void**)&h->argmax, 16},
+        {(void**)&h->dev_err, 16},
+    };
+    for (auto& e : plan) carve(e.bytes);
+    h->scratch_bytes = s.off;
+    if (cudaMalloc(&h->scratch, h->scratch_bytes) != cudaSuccess)
+        return bail(fail(h, QWC_E_OOM, "scratch allocation failed"));
+    s.base = h->scratch;
+    s.off = 0;
+    for (auto& e : plan) *e.p = carve(e.bytes);
+    if (cudaMemset(h->scratch, 0, h->scratch_bytes) != cudaSuccess)
+        return bail(fail(h, QWC_E_CUDA, "scratch memset failed"));
+    if (cudaMallocHost(&h->h_pin, 64 * sizeof(int)) != cudaSuccess)
+        return bail(fail(h, QWC_E_OOM, "pinned host allocation failed"));
+    // reconcile the activation arena with the real allocation (qwen_model.cpp:84-87)
+    h->budget.activation_bytes = h->scratch_bytes;
+    h->budget.vision_scratch_bytes = 0;
+
+    rc = qwc_reset(h);
+    if (rc) return bail(rc);
+    rc = build_graph(h);
+    if (rc) return bail(rc);
+    *out = h;
+    return QWC_OK;
+}
+
+// ------------------------------------------------------------------ decode API
+extern "C" int qwc_reset(qwc_handle* h) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_reset: null handle");
+    CU(cudaSetDevice(h->device));
+    // QwenModel::reset (src/qwen_model.cpp:98-104): zero every cache and the position
+    if (h->gdn_bytes) CU(cudaMemsetAsync(h->st.gdn_state, 0, h->gdn_bytes, h->stream));
+    if (h->conv_bytes) CU(cudaMemsetAsync(h->st.conv_ring, 0, h->conv_bytes, h->stream));
+    if (h->kvc_bytes) CU(cudaMemsetAsync(h->st.kv, 0, h->kvc_bytes, h->stream));
+    CU(cudaMemsetAsync(h->pos, 0, sizeof(int), h->stream));
+    CU(cudaStreamSynchronize(h->stream));
+    h->pos_host = 0;
+    return QWC_OK;
+}
+
+extern "C" int qwc_position(const qwc_handle* h) { return h ? h->pos_host : -1; }
+
+extern "C" int qwc_step(qwc_handle* h, int token, float* logits_host, int* argmax_out) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_step: null handle");
+    if (token < 0 || token >= h->V) return fail(h, QWC_E_INVALID, "qwc_step: token id out of range");
+    if (h->pos_host >= h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_step: position would exceed max_context");
+    CU(cudaSetDevice(h->device));
+    // the token goes to tokens[pos]; n_prompt = max_ctx keeps the argmax from writing tokens
+    h->h_pin[0] = token;
+    h->h_pin[1] = h->max_ctx;
+    CU(cudaMemcpyAsync(h->tokens + h->pos_host, &h->h_pin[0], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    CU(cudaMemcpyAsync(h->n_prompt, &h->h_pin[1], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    int rc = run_step(h);
+    if (rc) return rc;
+    if (logits_host)
+        CU(cudaMemcpyAsync(logits_host, h->logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost, h->stream));
+    CU(cudaMemcpyAsync(&h->h_pin[2], h->argmax, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    rc = check_device_error(h);  // synchronises
+    if (rc) return rc;
+    h->pos_host++;
+    if (argmax_out) *argmax_out = h->h_pin[2];
+    return QWC_OK;
+}
+
+extern "C" int qwc_generate_greedy(qwc_handle* h, const int* prompt, int n_prompt, int n_new, int* out_tokens) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_generate_greedy: null handle");
+    if (n_prompt < 0 || n_new < 0 || (n_prompt > 0 && !prompt) || (n_new > 0 && !out_tokens))
+        return fail(h, QWC_E_INVALID, "qwc_generate_greedy: invalid argument");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_generate_greedy: token id out of range");
+    if ((long)n_prompt + n_new > h->max_ctx)
+        return fail(h, QWC_E_CONTEXT, "qwc_generate_greedy: prompt + n_new exceeds max_context");
+    int rc = qwc_reset(h);
+    if (rc) return rc;
+    if (n_prompt == 0) return QWC_OK;  // the reference produces nothing without a prompt
+    CU(cudaMemcpyAsync(h->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, h->stream));
+    h->h_pin[3] = n_prompt;
+    CU(cudaMemcpyAsync(h->n_prompt, &h->h_pin[3], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    for (int i = 0; i < n_prompt + n_new; ++i) {
+        rc = run_step(h);
+        if (rc) return rc;
+    }
+    if (n_new > 0)
+        CU(cudaMemcpyAsync(out_tokens, h->tokens + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, h->stream));
+    rc = check_device_error(h);
+    if (rc) return rc;
+    h->pos_host = n_prompt + n_new;
+    return QWC_OK;
+}
+
+extern "C" int qwc_get_budget(const qwc_handle* h, qwc_budget* out) {
+    if (!h || !out) return fail(nullptr, QWC_E_INVALID, "qwc_get_budget: null argument");
+    *out = h->budget;
+    return QWC_OK;
+}
+
+extern "C" int qwc_get_config(const qwc_handle* h, qwc_config* out) {
+    if (!h || !out) return fail(nullptr, QWC_E_INVALID, "qwc_get_config: null argument");
+    *out = h->cfg;
+    return QWC_OK;
+}
+
+// ------------------------------------------------------------------ prefill (stepping)
+// First implementation: the prompt goes through the decode step one token at a time,
+// exactly as the reference's generate_greedy feeds it (src/qwen_model.cpp:245).
+extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_prefill: null handle");
+    if (T <= 0 || !ids) return fail(h, QWC_E_INVALID, "qwc_prefill: empty prompt");
+    if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_prefill: T exceeds max_context");
+    for (int i = 0; i < T; ++i)
+        if (ids[i] < 0 || ids[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_prefill: token id out of range");
+    int rc = qwc_reset(h);
+    if (rc) return rc;
+    CU(cudaMemcpyAsync(h->tokens, ids, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
+    h->h_pin[4] = h->max_ctx;
+    CU(cudaMemcpyAsync(h->n_prompt, &h->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    for (int i = 0; i < T; ++i) {
+        rc = run_step(h);
+        if (rc) return rc;
+    }
+    if (logits_out) CU(cudaMemcpyAsync(logits_out, h->logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost, h->stream));
+    rc = check_device_error(h);
+    if (rc) return rc;
+    h->pos_host = T;
+    return QWC_OK;
+}
+
+// QwenForward::prefill semantics: stateless. A temporary state of T positions is
+// allocated for the call; the handle's decode state and position are untouched.
+extern "C" int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_forward_logits: null handle");
+    if (T <= 0 || !ids || !logits_out) return fail(h, QWC_E_INVALID, "qwc_forward_logits: invalid argument");
+    for (int i = 0; i < T; ++i)
+        if (ids[i] < 0 || ids[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_forward_logits: token id out of range");
+    CU(cudaSetDevice(h->device));
+    StateView tv;
+    tv.max_ctx = T;
+    const size_t gb = h->gdn_bytes, cb = h->conv_bytes;
+    const size_t kb = (size_t)h->n_attn * 2 * h->NKV * (size_t)T * h->HD * h->kv_bytes;
+    if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_forward_logits: T exceeds max_context");
+    if (gb && cudaMalloc(&tv.gdn_state, gb) != cudaSuccess) return fail(h, QWC_E_OOM, "forward state allocation failed");
+    if (cb && cudaMalloc(&tv.conv_ring, cb) != cudaSuccess) { cudaFree(tv.gdn_state); return fail(h, QWC_E_OOM, "forward state allocation failed"); }
+    if (kb && cudaMalloc(&tv.kv, kb) != cudaSuccess) { cudaFree(tv.gdn_state); cudaFree(tv.conv_ring); return fail(h, QWC_E_OOM, "forward state allocation failed"); }
+    int rc = QWC_OK;
+    // the handle's token buffer and position are borrowed and restored afterwards
+    do {
+        if (gb && cudaMemsetAsync(tv.gdn_state, 0, gb, h->stream) != cudaSuccess) { rc = fail(h, QWC_E_CUDA, "memset"); break; }
+        if (cb && cudaMemsetAsync(tv.conv_ring, 0, cb, h->stream) != cudaSuccess) { rc = fail(h, QWC_E_CUDA, "memset"); break; }
+        std::vector<int> saved_tokens((size_t)h->max_ctx + 1);
+        cudaMemcpyAsync(saved_tokens.data(), h->tokens, saved_tokens.size() * 4, cudaMemcpyDeviceToHost, h->stream);
+        cudaMemcpyAsync(&h->h_pin[10], h->pos, sizeof(int), cudaMemcpyDeviceToHost, h->stream);
+        cudaMemcpyAsync(&h->h_pin[11], h->n_prompt, sizeof(int), cudaMemcpyDeviceToHost, h->stream);
+        cudaStreamSynchronize(h->stream);
+        const int saved_pos = h->h_pin[10], saved_np = h->h_pin[11];
+        cudaMemcpyAsync(h->tokens, ids, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream);
+        h->h_pin[12] = 0;
+        h->h_pin[13] = h->max_ctx;
+        cudaMemcpyAsync(h->pos, &h->h_pin[12], sizeof(int), cudaMemcpyHostToDevice, h->stream);
+        cudaMemcpyAsync(h->n_prompt, &h->h_pin[13], sizeof(int), cudaMemcpyHostToDevice, h->stream);
+        for (int t = 0; t < T && rc == QWC_OK; ++t) {
+            rc = enqueue_step(h, tv, h->use_pdl);
+            if (rc) break;
+            if (!last_only || t == T - 1) {
+                float* dst = logits_out + (last_only ? 0 : (size_t)t * h->V);
+                if (cudaMemcpyAsync(dst, h->logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess)
+                    rc = fail(h, QWC_E_CUDA, "logits copy failed");
+            }
+        }
+        cudaMemcpyAsync(h->tokens, saved_tokens.data(), saved_tokens.size() * 4, cudaMemcpyHostToDevice, h->stream);
+        h->h_pin[10] = saved_pos;
+        h->h_pin[11] = saved_np;
+        cudaMemcpyAsync(h->pos, &h->h_pin[10], sizeof(int), cudaMemcpyHostToDevice, h->stream);
+        cudaMemcpyAsync(h->n_prompt, &h->h_pin[11], sizeof(int), cudaMemcpyHostToDevice, h->stream);
+        int rc2 = check_device_error(h);
+        if (rc == QWC_OK) rc = rc2;
+    } while (0);
+    cudaStreamSynchronize(h->stream);
+    cudaFree(tv.gdn_state);
+    cudaFree(tv.conv_ring);
+    cudaFree(tv.kv);
+    return rc;
+}
+
+// ------------------------------------------------------------------ kernel-level API
+static int* kernel_api_err() {
+    int* p = nullptr;
+    if (cudaGetSymbolAddress((void**)&p, g_kernel_api_error) != cudaSuccess) return nullptr;
+    return p;
+}
+
+extern "C" int qwc_gemv_bf16(const uint16_t* W, const float* x, float* y, int out_dim, int in_dim, void* stream) {
+    if (!W || !x || !y || out_dim <= 0 || in_dim <= 0 || in_dim % 8)
+        return fail(nullptr, QWC_E_INVALID, "qwc_gemv_bf16: invalid argument");
+    GemvParams p;
+    p.W = W;
+    p.rows = out_dim;
+    p.in_dim = in_dim;
+    p.x_len = in_dim;
+    p.x = x;
+    p.y = y;
+    p.dev_err = kernel_api_err();
+    cudaError_t e = launch_gemv(PRO_PLAIN, EPI_STORE, p, gemv_grid(out_dim), (cudaStream_t)stream, false);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gemv_bf16: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+extern "C" int qwc_gdn_decode_step(const float* mixed, const float* a, const float* b, const float* conv_w,
+                                   const float* neg_exp_A, const float* dt_bias, float* conv_ring, float* state,
+                                   float* out, int KH, int VH, int pos, void* stream) {
+    if (!mixed || !a || !b || !conv_w || !neg_exp_A || !dt_bias || !conv_ring || !state || !out || KH <= 0 ||
+        VH <= 0 || VH % KH || pos < 0)
+        return fail(nullptr, QWC_E_INVALID, "qwc_gdn_decode_step: invalid argument");
+    GdnDecodeParams p;
+    p.mixed = mixed;
+    p.a = a;
+    p.b = b;
+    p.conv_w = conv_w;
+    p.neg_exp_A = neg_exp_A;
+    p.dt_bias = dt_bias;
+    p.conv_ring = conv_ring;
+    p.state = state;
+    p.out = out;
+    p.pos_val = pos;
+    p.KH = KH;
+    p.VH = VH;
+    cudaError_t e = launch_gdn_decode(p, (cudaStream_t)stream, false);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gdn_decode_step: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+namespace {
+struct AttnOpScratch {
+    int device = -1;
+    float* part_o = nullptr;
+    float* part_ml = nullptr;
+    unsigned* counters = nullptr;
+    size_t cap_o = 0;
+};
+thread_local AttnOpScratch g_attn_op;
+}  // namespace
+
+extern "C" int qwc_attention_decode(const float* q, const float* gate, const void* k_cache, const void* v_cache,
+                                    int kv_dtype, int NQ, int NKV, int max_ctx, int n_ctx, float* out, void* stream) {
+    if (!q || !gate || !k_cache || !v_cache || !out || NKV <= 0 || NQ % NKV || n_ctx <= 0 || n_ctx > max_ctx ||
+        (kv_dtype != QWC_DTYPE_F32 && kv_dtype != QWC_DTYPE_BF16))
+        return fail(nullptr, QWC_E_INVALID, "qwc_attention_decode: invalid argument");
+    AttnDecodeParams p;
+    p.q_in = q;
+    p.gate_in = gate;
+    p.k_cache = const_cast<void*>(k_cache);
+    p.v_cache = const_cast<void*>(v_cache);
+    p.kv_bf16 = kv_dtype == QWC_DTYPE_BF16;
+    p.max_ctx = max_ctx;
+    p.n_ctx_val = n_ctx;
+    p.NQ = NQ;
+    p.NKV = NKV;
+    p.nsplit = attn_nsplit_for(n_ctx);
+    p.out = out;
+    const int grp = NQ / NKV;
+    const size_t need_o = (size_t)NKV * p.nsplit * grp * 256;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    AttnOpScratch& s = g_attn_op;
+    if (s.device != dev || s.cap_o < need_o) {
+        // per-thread split-K workspace, grown on demand and kept for later calls
+        if (s.part_o) { cudaFree(s.part_o); cudaFree(s.part_ml); cudaFree(s.counters); }
+        s = AttnOpScratch();
+        if (cudaMalloc(&s.part_o, need_o * 4) != cudaSuccess || cudaMalloc(&s.part_ml, need_o / 256 * 2 * 4) != cudaSuccess ||
+            cudaMalloc(&s.counters, 64 * 4) != cudaSuccess)
+            return fail(nullptr, QWC_E_OOM, "qwc_attention_decode: workspace allocation failed");
+        cudaMemset(s.counters, 0, 64 * 4);
+        s.device = dev;
+        s.cap_o = need_o;
+    }
+    if (NKV > 64) return fail(nullptr, QWC_E_INVALID, "qwc_attention_decode: too many kv heads");
+    p.part_o = s.part_o;
+    p.part_ml = s.part_ml;
+    p.counters = s.counters;
+    cudaError_t e = launch_attn_decode(p, (cudaStream_t)stream, false);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_attention_decode: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}

@@ -1,0 +1,110 @@
+// Internal launch interface of the sm_100a kernels (not part of the C ABI).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qwc {
+
+// ------------------------------------------------------------------ GEMV family
+// y = W . x with W bf16 [rows][in_dim] row-major, x fp32, fp32 accumulation: the
+// reference's matmul(WeightView) (src/forward_pass.cpp:44-75), streamed from HBM by
+// 1-D bulk TMA into a shared-memory ring, with the neighbouring elementwise work of
+// the decode step fused as a prologue (how x is formed) and an epilogue (where the
+// row results go).
+enum GemvPro : int {
+    PRO_PLAIN = 0,        // x = x_in
+    PRO_RMSNORM = 1,      // x = rmsnorm(x_in) * (1 + w)            (forward_pass.cpp:77-84)
+    PRO_EMBED_RMSNORM = 2,// x_in = embedding row of tokens[*pos]; CTA 0 stores it in hidden
+    PRO_GATED_NORM = 3,   // x = w * (o * rsqrt(mean_head(o^2)+eps)) * silu(z)  (:86-93)
+};
+enum GemvEpi : int {
+    EPI_STORE = 0,        // y[r] = acc
+    EPI_RESIDUAL = 1,     // y[r] += acc                               (qwen_model.cpp:223,232)
+    EPI_SWIGLU = 2,       // row r = [gate_r | up_r] (2*x_len long): y[r] = silu(g)*u (:227-231)
+    EPI_ARGMAX = 3,       // y[r] = acc (logits) + greedy argmax over all rows (:249-251)
+};
+
+struct GemvParams {
+    const uint16_t* W = nullptr;
+    int rows = 0;
+    int in_dim = 0;          // row length in elements
+    int x_len = 0;           // length of x (in_dim, or in_dim/2 for EPI_SWIGLU)
+    const float* x = nullptr;
+    const float* norm_w = nullptr;  // PRO_RMSNORM: (1+w) [x_len]; PRO_GATED_NORM: w [gn_dim]
+    const float* z = nullptr;       // PRO_GATED_NORM: gate input [x_len]
+    int gn_dim = 128;
+    float eps = 1e-6f;
+    // PRO_EMBED_RMSNORM
+    const uint16_t* embed = nullptr;
+    const int* tokens = nullptr;    // token at position p is tokens[p]
+    const int* pos = nullptr;
+    int vocab = 0;
+    float* hidden_out = nullptr;
+    // output
+    float* y = nullptr;
+    // EPI_ARGMAX
+    float* am_val = nullptr;        // [gridDim] per-CTA partials
+    int* am_idx = nullptr;
+    unsigned* am_counter = nullptr; // zero between launches (the last CTA resets it)
+    int* argmax_out = nullptr;      // final id
+    int* tokens_out = nullptr;      // if non-null: tokens_out[*pos + 1] = id when *pos+1 >= *n_prompt
+    const int* n_prompt = nullptr;
+    int* pos_inout = nullptr;       // if non-null: ++*pos_inout by the last CTA
+    int max_ctx = 0;
+    int slots_per_warp = 6;         // ring depth (set by the launcher)
+    int* dev_err = nullptr;         // device error word (bounded waits, bad token)
+};
+
+size_t gemv_smem_bytes(const GemvParams& p);
+cudaError_t launch_gemv(int pro, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl);
+int gemv_grid(int rows);
+
+// ------------------------------------------------------------------ GDN decode
+// One token of the Gated DeltaNet mixer core (qwen_model.cpp:173-207): causal conv over
+// the rolling state + SiLU, l2norm(q,k), gates, delta-rule update, o = S^T q.
+struct GdnDecodeParams {
+    const float* mixed = nullptr;   // [C] = [q KD | k KD | v VD]
+    const float* a = nullptr;       // [VH]
+    const float* b = nullptr;       // [VH]
+    const float* conv_w = nullptr;  // [C][4]
+    const float* neg_exp_A = nullptr;  // [VH]
+    const float* dt_bias = nullptr;    // [VH]
+    float* conv_ring = nullptr;     // [C][4], slot pos % 4 receives the new input
+    float* state = nullptr;         // [VH][DK][DV]
+    float* out = nullptr;           // [VH][DV]
+    const int* pos_ptr = nullptr;   // device position (or nullptr: use pos_val)
+    int pos_val = 0;
+    int KH = 0, VH = 0;
+};
+cudaError_t launch_gdn_decode(const GdnDecodeParams& p, cudaStream_t s, bool pdl);
+
+// ------------------------------------------------------------------ attention decode
+// Split-K flash decode over the KV cache with the q/k norm + partial RoPE + KV append
+// of attn_step (qwen_model.cpp:118-150) fused in, and the sigmoid output gate applied by
+// the CTA that combines the splits.
+struct AttnDecodeParams {
+    const float* proj = nullptr;    // decode: [NQ][2*HD] ([q|gate] per head), [NKV][HD] k, [NKV][HD] v
+    const float* q_in = nullptr;    // op mode: q [NQ][HD] (normed+roped); proj == nullptr
+    const float* gate_in = nullptr; // op mode: gate [NQ][HD]
+    const float* qn1 = nullptr;     // (1+w) q_norm [HD]
+    const float* kn1 = nullptr;     // (1+w) k_norm [HD]
+    const double* inv_freq = nullptr;  // [rot/2] theta^(-2i/rot)
+    void* k_cache = nullptr;        // [NKV][max_ctx][HD]
+    void* v_cache = nullptr;
+    int kv_bf16 = 0;
+    int max_ctx = 0;
+    const int* pos_ptr = nullptr;   // decode: position of the new token (n_ctx = pos+1)
+    int n_ctx_val = 0;              // op mode: number of cached positions
+    float* part_o = nullptr;        // [NKV][nsplit][GRP][HD]
+    float* part_ml = nullptr;       // [NKV][nsplit][GRP][2]
+    unsigned* counters = nullptr;   // [NKV], zero between launches
+    float* out = nullptr;           // [NQ][HD]
+    int NQ = 0, NKV = 0, rot = 64, nsplit = 1;
+    float eps = 1e-6f;
+};
+cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t s, bool pdl);
+int attn_nsplit_for(int max_ctx);
+
+int num_sms();
+
+}  // namespace qwc

@@ -1,0 +1,99 @@
+"""Kernel-level parity on the GPU through the C ABI, against the CPU oracle.
+
+Tolerances: the kernels accumulate in fp32 in a different order than the oracle, so
+results agree to a few ulp-scale relative errors; rel_l2 <= 1e-5 is required."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("out_dim,in_dim", [(1, 8), (7, 256), (1024, 1024), (8224, 1024),
+                                            (1024, 2048), (1024, 3584), (2048, 6144),
+                                            (3000, 520), (151936, 1024)])
+def test_gemv_matches_oracle(pkg, oracle, out_dim, in_dim):
+    rng = np.random.default_rng(out_dim * 7 + in_dim)
+    W = pkg.synth.f32_to_bf16_bits(rng.standard_normal((out_dim, in_dim), dtype=np.float32) * 0.02)
+    x = rng.standard_normal(in_dim, dtype=np.float32)
+    want = np.empty(out_dim, np.float32)
+    oracle.orc_lib().orc_matmul_bf16(W, x, want, out_dim, in_dim)
+    Wd, xd = dev(W.view(np.int16)), dev(x)
+    yd = torch.full((out_dim,), float("nan"), device="cuda")
+    pkg.abi.gemv_bf16(Wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), out_dim, in_dim)
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, want) < TOL
+
+
+@pytest.mark.parametrize("KH,VH", [(16, 16), (2, 4)])
+def test_gdn_decode_step_matches_oracle(pkg, oracle, KH, VH):
+    DK = DV = 128
+    C = 2 * KH * DK + VH * DV
+    T = 6
+    rng = np.random.default_rng(KH + VH)
+    mixed = rng.standard_normal((T, C), dtype=np.float32)
+    a = rng.standard_normal((T, VH), dtype=np.float32)
+    b = rng.standard_normal((T, VH), dtype=np.float32)
+    conv_w = (rng.standard_normal((C, 4), dtype=np.float32) * 0.1).astype(np.float32)
+    A_log = rng.uniform(0, np.log(16), VH).astype(np.float32)
+    dt = np.ones(VH, np.float32)
+    state = (rng.standard_normal((VH, DK, DV), dtype=np.float32) * 0.1).astype(np.float32)
+    cs = np.zeros((C, 3), np.float32)
+    want = np.empty((T, VH, DV), np.float32)
+    st_want = state.copy()
+    oracle.orc_lib().orc_gdn_core(T, KH, VH, DK, DV, 4, mixed, conv_w, a, b, A_log, dt, st_want, cs, want)
+
+    neg = (-np.exp(A_log)).astype(np.float32)
+    d_conv_w, d_neg, d_dt = dev(conv_w), dev(neg), dev(dt)
+    d_ring = torch.zeros((C, 4), device="cuda")
+    d_state = dev(state)
+    d_out = torch.empty((VH, DV), device="cuda")
+    got = np.empty((T, VH, DV), np.float32)
+    for t in range(T):
+        dm, da, db = dev(mixed[t]), dev(a[t]), dev(b[t])
+        pkg.abi.gdn_decode_step(dm.data_ptr(), da.data_ptr(), db.data_ptr(), d_conv_w.data_ptr(),
+                                d_neg.data_ptr(), d_dt.data_ptr(), d_ring.data_ptr(),
+                                d_state.data_ptr(), d_out.data_ptr(), KH, VH, t)
+        torch.cuda.synchronize()
+        got[t] = d_out.cpu().numpy()
+    assert rel_l2(got, want) < TOL
+    assert rel_l2(d_state.cpu().numpy(), st_want) < TOL
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+@pytest.mark.parametrize("n_ctx", [1, 63, 64, 65, 1000, 4099])
+def test_attention_decode_matches_oracle(pkg, oracle, kv_dtype, n_ctx):
+    NQ, NKV, HD = 8, 2, 256
+    max_ctx = n_ctx + 5
+    rng = np.random.default_rng(n_ctx)
+    q = rng.standard_normal((NQ, HD), dtype=np.float32) * 0.1
+    gate = rng.standard_normal((NQ, HD), dtype=np.float32)
+    K = rng.standard_normal((NKV, max_ctx, HD), dtype=np.float32)
+    V = rng.standard_normal((NKV, max_ctx, HD), dtype=np.float32)
+    if kv_dtype == 1:  # the oracle sees the bf16-rounded cache
+        Kb, Vb = pkg.synth.f32_to_bf16_bits(K), pkg.synth.f32_to_bf16_bits(V)
+        K, V = pkg.synth.bf16_bits_to_f32(Kb), pkg.synth.bf16_bits_to_f32(Vb)
+        dK, dV = dev(Kb.view(np.int16)), dev(Vb.view(np.int16))
+    else:
+        dK, dV = dev(K), dev(V)
+    kc = np.ascontiguousarray(K[:, :n_ctx].transpose(1, 0, 2))
+    vc = np.ascontiguousarray(V[:, :n_ctx].transpose(1, 0, 2))
+    want = np.empty((NQ, HD), np.float32)
+    oracle.orc_lib().orc_attention(NQ, NKV, HD, n_ctx, np.ascontiguousarray(q), gate, kc, vc, want)
+    dq, dg = dev(q), dev(gate)
+    dout = torch.empty((NQ, HD), device="cuda")
+    for _ in range(2):  # second call reuses the split-K workspace / counters
+        pkg.abi.attention_decode(dq.data_ptr(), dg.data_ptr(), dK.data_ptr(), dV.data_ptr(), kv_dtype,
+                                 NQ, NKV, max_ctx, n_ctx, dout.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_l2(dout.cpu().numpy(), want) < TOL

@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Decode benchmark of the B200 Qwen3.5 hybrid forward pass.
+
+Workload: the 0.8B-shaped seeded model, a 32-token random prompt and
+128 greedy tokens, i.e. exactly QwenModel::generate_greedy (src/qwen_model.cpp:241-255):
+160 single-token decode steps. One bench "step" is one such generation; the metric is
+decode tokens per second (step() calls per second, prompt tokens included, as the
+reference processes its prompt one token at a time).
+
+  value      device time of K generations with the prompt already in HBM (CUDA events
+             on the engine's stream; max over ranks); inputs (1.31 GB of weights per
+             token) are far larger than the 126 MB L2, so no flush is needed.
+  e2e        the same through the C ABI call qwc_generate_greedy with host buffers:
+             prompt H2D, reset, 160 graph replays, token ids D2H, all in the timed region.
+  roofline   the dominant kernel class of the step, timed live per launch (eager step,
+             CUDA events) against MEASURED_PEAKS.json's HBM copy bandwidth.
+  cpu_baseline  the reference engine itself (oracle/_ref: its own sources, built here)
+             on this host's cores, one full generation.
+
+--impl reference times the reference's CPU generate_greedy on the same workload.
+Multi-GPU: single-sequence decode does not shard; N ranks run N independent replicas
+(weak scaling), value = total tokens/s over all ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_PROMPT, N_NEW = 32, 128
+SHAPE = "qwen3.5-0.8b-shaped"
+METRIC = "decode tok/s"
+UNIT = "tok/s"
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+RANK, WORLD, LOCAL_RANK = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+HOST_CORES = os.cpu_count() or 1
+os.environ.setdefault("OMP_NUM_THREADS", str(HOST_CORES))  # before any OpenMP library loads
+
+
+def workload_config(args):
+    return {"workload": "configs[0]: qwen3.5-0.8b-shaped greedy decode", "model": SHAPE,
+            "prompt_tokens": N_PROMPT, "new_tokens": N_NEW,
+            "tokens_per_step": N_PROMPT + N_NEW, "global_batch": 1,
+            "seq_len": N_PROMPT + N_NEW, "kv_cache": "fp32", "parallelism": f"replicas{args.gpus}",
+            "l2": "inputs larger than L2 (1.31 GB of weights streamed per token)"}
+
+
+def model_dir():
+    base = os.environ.get("QWC_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "qwc_models"))
+    return os.path.join(base, f"{SHAPE}-s0")
+
+
+def ensure_model(pkg):
+    return pkg.synth.write_model(pkg.synth.SHAPES[SHAPE], model_dir(), seed=0)
+
+
+def decode_bytes_per_token(cfg, ctx):
+    """Algorithmic HBM bytes of one decode token at context length ctx (fp32 KV)."""
+    H, I, V = cfg.hidden_size, cfg.ffn_intermediate, cfg.vocab_size
+    L = cfg.n_layers_total
+    n_attn = L // cfg.attn_interval
+    n_gdn = L - n_attn
+    KD = cfg.gdn_k_heads * cfg.gdn_k_head_dim
+    VD = cfg.gdn_v_heads * cfg.gdn_v_head_dim
+    C = 2 * KD + VD
+    NQ, NKV, HD = cfg.attn_q_heads, cfg.attn_kv_heads, cfg.attn_head_dim
+    w = 0
+    w += n_gdn * ((C + VD + 2 * cfg.gdn_v_heads) * H + H * VD) * 2
+    w += n_attn * ((2 * NQ * HD + 2 * NKV * HD) * H + H * NQ * HD) * 2
+    w += L * 3 * H * I * 2
+    w += V * H * 2 + H * 2  # lm_head (tied embedding read in full) + embedding row
+    small = L * 2 * H * 4 + n_gdn * (C * 4 * 4 + 3 * cfg.gdn_v_heads * 4 + 128 * 4) + n_attn * 2 * HD * 4
+    state = n_gdn * cfg.gdn_v_heads * cfg.gdn_k_head_dim * cfg.gdn_v_head_dim * 4 * 2
+    conv = n_gdn * C * (16 + 4)  # ring: read 16 B, write 4 B per channel
+    kv = n_attn * (ctx * NKV * HD * 4 * 2 + 2 * NKV * HD * 4)
+    return w + small + state + conv + kv
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.path = tempfile.mktemp(prefix="qwc_clocks_", suffix=".csv")
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons, power = [], None, set(), []
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline(d, prompt, n_new):
+    """The reference engine (oracle/_ref) on this host's cores: one full generation."""
+    from oracle import bindings
+    cores = int(os.environ.get("OMP_NUM_THREADS", HOST_CORES))
+    if bindings.ref_available():
+        ref, kind = bindings.RefModel(d, len(prompt) + n_new + 2), "reference"
+        secs, toks = ref.time_generate(prompt, n_new)
+    else:
+        ref, kind = bindings.OracleModel(d, len(prompt) + n_new + 2), "port"
+        t0 = time.perf_counter()
+        toks = ref.generate_greedy(prompt, n_new)
+        secs = time.perf_counter() - t0
+    n = len(prompt) + n_new
+    return {"value": round(n / secs, 3), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"one generate_greedy: {len(prompt)} prompt + {n_new} new tokens "
+                      f"({n} step() calls, {secs:.2f} s)"}, toks
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU generate_greedy, rank 0 only."""
+    if RANK != 0:
+        return 0
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from oracle import bindings
+    d = ensure_model(pkg)
+    prompt = pkg.synth.random_prompt(pkg.synth.SHAPES[SHAPE].vocab_size, N_PROMPT, seed=1234)
+    if bindings.ref_available():
+        ref, kind = bindings.RefModel(d, N_PROMPT + N_NEW + 2), "reference"
+    else:
+        ref, kind = bindings.OracleModel(d, N_PROMPT + N_NEW + 2), "port"
+    # each step: one generation, shortened when many steps are asked for so the whole
+    # run stays within a few minutes
+    n_new = N_NEW if args.steps + args.warmup <= 12 else max(8, N_NEW * 12 // (args.steps + args.warmup))
+
+    def one():
+        t0 = time.perf_counter()
+        ref.generate_greedy(prompt, n_new)
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        one()
+    secs = sum(one() for _ in range(args.steps))
+    toks = args.steps * (N_PROMPT + n_new)
+    val = toks / secs
+    cores = int(os.environ.get("OMP_NUM_THREADS", HOST_CORES))
+    line = {"metric": METRIC, "value": round(val, 3), "unit": UNIT, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000 * secs / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": round(val, 3), "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": f"{args.steps} x generate_greedy({N_PROMPT} prompt + {n_new} new)"},
+            "e2e": {"value": round(val, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import __graft_entry__
+    torch.cuda.set_device(LOCAL_RANK)
+    dist = None
+    if WORLD > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", LOCAL_RANK))
+    pkg = __graft_entry__.load_package()
+    if RANK == 0:
+        ensure_model(pkg)
+    if dist:
+        dist.barrier()
+    d = ensure_model(pkg)
+    shape = pkg.synth.SHAPES[SHAPE]
+    prompt = pkg.synth.random_prompt(shape.vocab_size, N_PROMPT, seed=1234)
+    max_ctx = N_PROMPT + N_NEW + 16
+    m = pkg.abi.Model(d, max_context=max_ctx, device=LOCAL_RANK)
+    stream = torch.cuda.ExternalStream(m.stream())
+    n_tok = N_PROMPT + N_NEW
+
+    # ---- value: device-resident generations
+    m.set_prompt(prompt)
+    for _ in range(args.warmup):
+        m.enqueue_greedy(N_PROMPT, N_NEW)
+    ref_tokens = m.read_tokens(N_PROMPT, N_NEW)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_index = LOCAL_RANK
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v for v in vis.split(",") if v.strip()]
+        if LOCAL_RANK < len(ids) and ids[LOCAL_RANK].strip().isdigit():
+            gpu_index = int(ids[LOCAL_RANK])
+    with ClockSampler(gpu_index) as clocks:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            m.enqueue_greedy(N_PROMPT, N_NEW)
+        e1.record(stream)
+        stream.synchronize()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    dev_ms = e0.elapsed_time(e1)
+    got = m.read_tokens(N_PROMPT, N_NEW)
+    assert np.array_equal(got, ref_tokens), "generations differ between runs"
+    if dist:
+        t = torch.tensor([dev_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms = float(t.item())
+    total_tokens = WORLD * args.steps * n_tok
+    value = total_tokens / (dev_ms / 1000.0)
+    clk = clocks.summary()
+
+    # ---- e2e: the C ABI call with host buffers (H2D prompt, D2H ids inside the timed region)
+    for _ in range(2):
+        out = m.generate_greedy(prompt, N_NEW)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = m.generate_greedy(prompt, N_NEW)
+    e1.record(stream)
+    stream.synchronize()
+    wall = time.perf_counter() - w0
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    assert np.array_equal(out, ref_tokens), "e2e generation differs from the device-resident one"
+    e2e = {"value": round(WORLD * args.steps * n_tok / (e2e_ms / 1000.0), 2), "unit": UNIT,
+           "h2d_bytes_per_step": N_PROMPT * 4, "d2h_bytes_per_step": N_NEW * 4 + 4,
+           "wall_clock_value": round(WORLD * args.steps * n_tok / wall, 2)}
+
+    # ---- live per-kernel timing of eager steps -> roofline of the dominant kernel class
+    m.generate_greedy(prompt, 8)  # position 40, mid-workload context
+    prof = []
+    for _ in range(4):
+        prof += m.profile_step()
+    launches_per_step = len(prof) // 4
+    by_kind = {}
+    for k, ms, b in prof:
+        e = by_kind.setdefault(k, [0.0, 0, 0])
+        e[0] += ms
+        e[1] += b
+        e[2] += 1
+    dom = max(by_kind, key=lambda k: by_kind[k][0])
+    dms, dbytes, dn = by_kind[dom]
+    peak, peak_src = measured_peaks()
+    achieved = (dbytes / dn) / (dms / dn / 1000.0) / 1e9
+    tot_ms = sum(v[0] for v in by_kind.values())
+    share = {k: round(v[0] / tot_ms, 4) for k, v in by_kind.items()}
+    kernel_gbs = {k: round((v[1] / v[2]) / (v[0] / v[2] / 1000.0) / 1e9, 1) for k, v in by_kind.items()}
+
+    # step-level HBM roofline of the timed workload (context grows over the generation)
+    cfg = m.cfg
+    step_bytes = sum(decode_bytes_per_token(cfg, ctx) for ctx in range(1, n_tok + 1))
+    step_gbs = step_bytes / ((dev_ms / args.steps) / 1000.0) / 1e9
+
+    line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": WORLD,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args),
+            "roofline": {"bound": "hbm", "kernel": f"k_gemv ({dom})", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": peak_src, "traffic": None,
+                         "bytes_per_launch": int(dbytes / dn), "avg_launch_ms": round(dms / dn, 5),
+                         "timing": "eager launches, CUDA events per launch"},
+            "step_roofline": {"bytes_per_token": int(step_bytes / n_tok),
+                              "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                              "frac": round(step_gbs / peak, 4), "peak_source": peak_src},
+            "kernel_share": share, "kernel_gbs": kernel_gbs,
+            "eager_step_ms": round(tot_ms / 4, 4),
+            "e2e": e2e, "gpu_launches": int(args.steps * n_tok * launches_per_step),
+            "clocks": clk}
+    if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
+        cb, toks = cpu_baseline(d, prompt, N_NEW)
+        cb["tokens_match"] = bool(np.array_equal(np.asarray(toks[:N_NEW]), ref_tokens))
+        line["cpu_baseline"] = cb
+    m.close()
+    if RANK == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(args.warmup, 3)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

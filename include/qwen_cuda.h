@@ -165,6 +165,37 @@ int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* logits_out, 
  * position's [vocab] logits, or NULL. */
 int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out);
 
+/* ---------------------------------------------------------------- measurement */
+/* No reference counterpart: hooks for timing the decode path without host round trips. */
+
+/* The handle's CUDA stream (cudaStream_t as void*): record events on it to time work. */
+void* qwc_stream(const qwc_handle* h);
+
+/* Upload prompt ids to the device token buffer (synchronises). */
+int qwc_set_prompt(qwc_handle* h, const int* prompt, int n_prompt);
+
+/* Enqueue, without any host synchronisation, the device work of a greedy generation
+ * whose n_prompt ids are already on the device (qwc_set_prompt): reset the state, then
+ * n_prompt + n_new decode steps. Read the ids back with qwc_read_tokens. */
+int qwc_enqueue_greedy(qwc_handle* h, int n_prompt, int n_new);
+
+/* Copy device token ids [start, start+n) to host memory (synchronises; checks the
+ * device error word). Position `start + i` holds the id fed at that position. */
+int qwc_read_tokens(qwc_handle* h, int start, int n, int* out);
+
+/* Runs ONE decode step eagerly (no graph, no programmatic launch) at the current
+ * position with the token id already at that position, timing every kernel with CUDA
+ * events. For each launch i < cap: kind[i] (QWC_K_*), ms[i], bytes[i] (algorithmic HBM
+ * bytes of that launch). Returns the number of launches (>= 0) or an error code. */
+#define QWC_K_MIX_IN 0      /* norm + mixer input projection GEMV */
+#define QWC_K_GDN 1         /* GDN conv + delta-rule recurrence */
+#define QWC_K_ATTN 2        /* attention (norm/rope/append + split-K) */
+#define QWC_K_MIX_OUT 3     /* mixer output projection GEMV + residual */
+#define QWC_K_GATE_UP 4     /* norm + gate/up GEMV + SwiGLU */
+#define QWC_K_DOWN 5        /* down GEMV + residual */
+#define QWC_K_LM_HEAD 6     /* final norm + lm_head GEMV + argmax */
+int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* bytes);
+
 /* ---------------------------------------------------------------- kernel level */
 
 /* matmul(const WeightView&, ...) (src/forward_pass.cpp:65-75) on device memory:

@@ -25,8 +25,11 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_solve_max_context",
            "qwc_create", "qwc_create_from_dir", "qwc_destroy", "qwc_last_error", "qwc_get_budget",
            "qwc_get_config", "qwc_reset", "qwc_position", "qwc_step", "qwc_generate_greedy",
-           "qwc_forward_logits", "qwc_prefill", "qwc_gemv_bf16", "qwc_gdn_decode_step",
-           "qwc_attention_decode")
+           "qwc_forward_logits", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
+           "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_gemv_bf16",
+           "qwc_gdn_decode_step", "qwc_attention_decode")
+KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
+                6: "lm_head"}
 
 
 class qwc_config(C.Structure):
@@ -93,6 +96,12 @@ def lib():
     L.qwc_generate_greedy.argtypes = [vp, ip, C.c_int, C.c_int, ip]
     L.qwc_forward_logits.argtypes = [vp, ip, C.c_int, fp, C.c_int]
     L.qwc_prefill.argtypes = [vp, ip, C.c_int, fp]
+    L.qwc_stream.argtypes = [vp]
+    L.qwc_stream.restype = C.c_void_p
+    L.qwc_set_prompt.argtypes = [vp, ip, C.c_int]
+    L.qwc_enqueue_greedy.argtypes = [vp, C.c_int, C.c_int]
+    L.qwc_read_tokens.argtypes = [vp, C.c_int, C.c_int, ip]
+    L.qwc_profile_step.argtypes = [vp, C.c_int, ip, C.POINTER(C.c_float), C.POINTER(C.c_int64)]
     L.qwc_gemv_bf16.argtypes = [vp, vp, vp, C.c_int, C.c_int, vp]
     L.qwc_gdn_decode_step.argtypes = [vp] * 9 + [C.c_int, C.c_int, C.c_int, vp]
     L.qwc_attention_decode.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -180,6 +189,36 @@ class Model:
         check(lib().qwc_forward_logits(self._h, _iptr(ids), T, lg.ctypes.data,
                                        1 if last_only else 0), self._h)
         return lg
+
+    # ---- measurement hooks (no reference counterpart)
+    def stream(self) -> int:
+        return lib().qwc_stream(self._h)
+
+    def set_prompt(self, prompt):
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        check(lib().qwc_set_prompt(self._h, _iptr(p), len(p)), self._h)
+
+    def enqueue_greedy(self, n_prompt: int, n_new: int):
+        check(lib().qwc_enqueue_greedy(self._h, n_prompt, n_new), self._h)
+
+    def read_tokens(self, start: int, n: int) -> np.ndarray:
+        out = np.zeros(max(n, 1), np.int32)
+        check(lib().qwc_read_tokens(self._h, start, n, _iptr(out)), self._h)
+        return out[:n]
+
+    def profile_step(self, cap: int = 512):
+        """One eager decode step at the current position with per-launch CUDA-event
+        timings: list of (kind, ms, algorithmic bytes)."""
+        kind = np.zeros(cap, np.int32)
+        ms = np.zeros(cap, np.float32)
+        by = np.zeros(cap, np.int64)
+        n = lib().qwc_profile_step(self._h, cap, _iptr(kind),
+                                   ms.ctypes.data_as(C.POINTER(C.c_float)),
+                                   by.ctypes.data_as(C.POINTER(C.c_int64)))
+        if n < 0:
+            check(n, self._h)
+        n = min(n, cap)
+        return [(KERNEL_KINDS[int(kind[i])], float(ms[i]), int(by[i])) for i in range(n)]
 
     def prefill(self, ids, logits: bool = True):
         """Prefill that seeds the decode state; returns the last position's logits."""

@@ -407,11 +407,33 @@ static GemvParams gp_base(qwc_handle* h) {
     return p;
 }
 
+// Optional per-launch timing of an eager step (qwc_profile_step).
+struct StepProfile {
+    int cap = 0, n = 0;
+    std::vector<cudaEvent_t> ev;  // ev[0] before the first launch, ev[i+1] after launch i
+    std::vector<int> kind;
+    std::vector<int64_t> bytes;
+};
+
 // Enqueue one decode step (embedding -> layers -> norm -> lm_head + argmax) on h->stream.
-static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
+static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfile* prof = nullptr,
+                        int pos_for_bytes = 0) {
     const int H = h->H;
     bool first = true;
     auto PDL = [&]() { bool r = pdl && !first; first = false; return r; };
+    auto rec = [&](int kind, int64_t bytes) -> int {
+        if (!prof) return QWC_OK;
+        if (prof->n < prof->cap) {
+            CU(cudaEventRecord(prof->ev[prof->n + 1], h->stream));
+            prof->kind[prof->n] = kind;
+            prof->bytes[prof->n] = bytes;
+        }
+        prof->n++;
+        return QWC_OK;
+    };
+    if (prof) CU(cudaEventRecord(prof->ev[0], h->stream));
+    int rc;
+    const int64_t kvb = h->kv_bytes;
     const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
     for (int L = 0; L < h->L; ++L) {
         const Layer& lw = h->layers[L];
@@ -434,6 +456,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
             p.hidden_out = h->hidden;
         }
         CU(launch_gemv(pro, EPI_STORE, p, gemv_grid(p.rows), h->stream, PDL()));
+        if ((rc = rec(QWC_K_MIX_IN, (int64_t)p.rows * H * 2 + (int64_t)H * 8 + (int64_t)p.rows * 4))) return rc;
         if (lw.is_attn) {
             AttnDecodeParams a;
             a.proj = h->proj;
@@ -456,6 +479,9 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
             a.nsplit = h->nsplit;
             a.eps = h->eps;
             CU(launch_attn_decode(a, h->stream, PDL()));
+            if ((rc = rec(QWC_K_ATTN, (int64_t)(pos_for_bytes + 1) * h->NKV * h->HD * kvb * 2 +
+                                          (int64_t)lw.in_rows * 4 + (int64_t)h->NQ * h->HD * 4)))
+                return rc;
             GemvParams o = gp_base(h);
             o.W = lw.w_out;
             o.rows = H;
@@ -464,6 +490,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
             o.x = h->mix;
             o.y = h->hidden;
             CU(launch_gemv(PRO_PLAIN, EPI_RESIDUAL, o, gemv_grid(H), h->stream, PDL()));
+            if ((rc = rec(QWC_K_MIX_OUT, (int64_t)H * lw.out_in * 2 + (int64_t)lw.out_in * 4 + (int64_t)H * 8))) return rc;
         } else {
             GdnDecodeParams g;
             g.mixed = h->proj;
@@ -479,6 +506,9 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
             g.KH = h->KH;
             g.VH = h->VH;
             CU(launch_gdn_decode(g, h->stream, PDL()));
+            if ((rc = rec(QWC_K_GDN, (int64_t)h->VH * h->DK * h->DV * 8 + (int64_t)h->C * (16 + 4 + 16 + 4) +
+                                         (int64_t)h->VD * 4)))
+                return rc;
             GemvParams o = gp_base(h);
             o.W = lw.w_out;
             o.rows = H;
@@ -490,6 +520,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
             o.gn_dim = h->DV;
             o.y = h->hidden;
             CU(launch_gemv(PRO_GATED_NORM, EPI_RESIDUAL, o, gemv_grid(H), h->stream, PDL()));
+            if ((rc = rec(QWC_K_MIX_OUT, (int64_t)H * h->VD * 2 + (int64_t)h->VD * 8 + (int64_t)H * 8))) return rc;
         }
         // FFN: post-attention RMSNorm + gate/up + SwiGLU, then down + residual
         GemvParams f = gp_base(h);
@@ -501,6 +532,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
         f.norm_w = lw.post_ln1;
         f.y = h->ffn_h;
         CU(launch_gemv(PRO_RMSNORM, EPI_SWIGLU, f, gemv_grid(h->I), h->stream, PDL()));
+        if ((rc = rec(QWC_K_GATE_UP, (int64_t)h->I * 2 * H * 2 + (int64_t)H * 8 + (int64_t)h->I * 4))) return rc;
         GemvParams d = gp_base(h);
         d.W = lw.w_down;
         d.rows = H;
@@ -509,6 +541,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
         d.x = h->ffn_h;
         d.y = h->hidden;
         CU(launch_gemv(PRO_PLAIN, EPI_RESIDUAL, d, gemv_grid(H), h->stream, PDL()));
+        if ((rc = rec(QWC_K_DOWN, (int64_t)H * h->I * 2 + (int64_t)h->I * 4 + (int64_t)H * 8))) return rc;
     }
     GemvParams o = gp_base(h);
     o.W = h->head;
@@ -527,6 +560,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl) {
     o.pos_inout = h->pos;
     o.max_ctx = sv.max_ctx;
     CU(launch_gemv(PRO_RMSNORM, EPI_ARGMAX, o, gemv_grid(h->V), h->stream, PDL()));
+    if ((rc = rec(QWC_K_LM_HEAD, (int64_t)h->V * H * 2 + (int64_t)H * 8 + (int64_t)h->V * 4))) return rc;
     return QWC_OK;
 }
 
@@ -879,6 +913,73 @@ extern "C" int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* l
     cudaFree(tv.conv_ring);
     cudaFree(tv.kv);
     return rc;
+}
+
+// ------------------------------------------------------------------ measurement API
+extern "C" void* qwc_stream(const qwc_handle* h) { return h ? (void*)h->stream : nullptr; }
+
+extern "C" int qwc_set_prompt(qwc_handle* h, const int* prompt, int n_prompt) {
+    if (!h || n_prompt <= 0 || !prompt || n_prompt > h->max_ctx) return fail(h, QWC_E_INVALID, "qwc_set_prompt: invalid argument");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_set_prompt: token id out of range");
+    CU(cudaSetDevice(h->device));
+    CU(cudaMemcpyAsync(h->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, h->stream));
+    CU(cudaStreamSynchronize(h->stream));
+    return QWC_OK;
+}
+
+extern "C" int qwc_enqueue_greedy(qwc_handle* h, int n_prompt, int n_new) {
+    if (!h || n_prompt <= 0 || n_new < 0) return fail(h, QWC_E_INVALID, "qwc_enqueue_greedy: invalid argument");
+    if ((long)n_prompt + n_new > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_enqueue_greedy: exceeds max_context");
+    if (h->gdn_bytes) CU(cudaMemsetAsync(h->st.gdn_state, 0, h->gdn_bytes, h->stream));
+    if (h->conv_bytes) CU(cudaMemsetAsync(h->st.conv_ring, 0, h->conv_bytes, h->stream));
+    if (h->kvc_bytes) CU(cudaMemsetAsync(h->st.kv, 0, h->kvc_bytes, h->stream));
+    CU(cudaMemsetAsync(h->pos, 0, sizeof(int), h->stream));
+    h->h_pin[5] = n_prompt;
+    CU(cudaMemcpyAsync(h->n_prompt, &h->h_pin[5], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    for (int i = 0; i < n_prompt + n_new; ++i) {
+        int rc = run_step(h);
+        if (rc) return rc;
+    }
+    h->pos_host = n_prompt + n_new;
+    return QWC_OK;
+}
+
+extern "C" int qwc_read_tokens(qwc_handle* h, int start, int n, int* out) {
+    if (!h || start < 0 || n < 0 || (n > 0 && !out) || (long)start + n > h->max_ctx + 1)
+        return fail(h, QWC_E_INVALID, "qwc_read_tokens: invalid argument");
+    if (n > 0) CU(cudaMemcpyAsync(out, h->tokens + start, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream));
+    return check_device_error(h);
+}
+
+extern "C" int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* bytes) {
+    if (!h || cap < 0 || (cap > 0 && (!kind || !ms || !bytes))) return fail(h, QWC_E_INVALID, "qwc_profile_step: invalid argument");
+    if (h->pos_host >= h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_profile_step: context full");
+    CU(cudaSetDevice(h->device));
+    StepProfile prof;
+    prof.cap = cap;
+    prof.ev.resize((size_t)cap + 1);
+    prof.kind.resize((size_t)cap);
+    prof.bytes.resize((size_t)cap);
+    for (auto& e : prof.ev) CU(cudaEventCreate(&e));
+    h->h_pin[6] = h->max_ctx;
+    int rc = QWC_OK;
+    if (cudaMemcpyAsync(h->n_prompt, &h->h_pin[6], sizeof(int), cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
+        rc = fail(h, QWC_E_CUDA, "qwc_profile_step: copy failed");
+    if (rc == QWC_OK) rc = enqueue_step(h, h->st, false, &prof, h->pos_host);
+    if (rc == QWC_OK) rc = check_device_error(h);
+    int n = std::min(prof.n, cap);
+    for (int i = 0; i < n && rc == QWC_OK; ++i) {
+        float t = 0.f;
+        cudaEventElapsedTime(&t, prof.ev[i], prof.ev[i + 1]);
+        kind[i] = prof.kind[i];
+        ms[i] = t;
+        bytes[i] = prof.bytes[i];
+    }
+    for (auto& e : prof.ev) cudaEventDestroy(e);
+    if (rc != QWC_OK) return rc;
+    h->pos_host++;
+    return prof.n;
 }
 
 // ------------------------------------------------------------------ kernel-level API

@@ -225,6 +225,26 @@ int qwc_attention_decode(const float* q, const float* gate, const void* k_cache,
                          const void* v_cache, int kv_dtype, int NQ, int NKV, int max_ctx,
                          int n_ctx, float* out, void* stream);
 
+/* No counterpart in the reference. Same computation and arguments as
+ * qwc_attention_decode, for callers that must not allocate device memory while they
+ * run: a plugin whose host application owns all device memory through its own pool, or
+ * a latency-critical loop that cannot afford cudaMalloc's implicit synchronisation.
+ * qwc_attention_decode grows a per-thread split-K workspace with cudaMalloc on first
+ * use; this variant instead uses a fixed 4 MiB array in device global memory that the
+ * library reserves on every GPU that loads it (held until the process exits), and calls
+ * no cudaMalloc, cudaFree or other allocating routine.
+ *  - Limit: the workspace, 256 B + NQ * nsplit * 1032 B (nsplit = number of context
+ *    splits, at most 296 on a B200, about n_ctx / 64), must fit 4 MiB; larger requests
+ *    return QWC_E_INVALID with the sizes in qwc_last_error(NULL). NKV <= 64.
+ *  - The first call on each device looks up the array's device address (with that
+ *    device current); make that first call before any stream capture.
+ *  - Every call on a device shares the one array: calls that overlap on the GPU (on
+ *    different streams, or from different host threads) race and give wrong results.
+ *    The split counters are cleared on `stream` at the start of each call. */
+int qwc_attention_decode_noalloc(const float* q, const float* gate, const void* k_cache,
+                                 const void* v_cache, int kv_dtype, int NQ, int NKV,
+                                 int max_ctx, int n_ctx, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -239,6 +239,16 @@ def gdn_decode_step(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state, o
                                     out, KH, VH, pos, stream))
 
 
+def attention_decode_noalloc(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx, n_ctx,
+                             out, stream=0):
+    """qwc_attention_decode_noalloc: same result as attention_decode, with its split-K
+    workspace in the library's fixed device array instead of a cudaMalloc'd one."""
+    L = lib()
+    fn = L.qwc_attention_decode_noalloc
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_void_p, C.c_void_p]
+    check(fn(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx, n_ctx, out, stream))
+
+
 def attention_decode(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx, n_ctx, out,
                      stream=0):
     check(lib().qwc_attention_decode(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx,

@@ -192,6 +192,10 @@ extern "C" int64_t qwc_solve_max_context(const qwc_config* c, uint64_t ram, uint
     return ctx < c->native_max_context ? ctx : c->native_max_context;
 }
 
+namespace qwc {
+void set_api_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace qwc
+
 extern "C" const char* qwc_last_error(const qwc_handle* h) {
     return h ? h->err.c_str() : g_last_error.c_str();
 }

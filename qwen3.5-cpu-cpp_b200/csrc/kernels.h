@@ -107,4 +107,7 @@ int attn_nsplit_for(int max_ctx);
 
 int num_sms();
 
+// Records a handle-less failure message (what qwc_last_error(NULL) returns).
+void set_api_error(const char* msg);
+
 }  // namespace qwc

@@ -196,6 +196,18 @@ int qwc_read_tokens(qwc_handle* h, int start, int n, int* out);
 #define QWC_K_LM_HEAD 6     /* final norm + lm_head GEMV + argmax */
 int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* bytes);
 
+/* Runs ONE step of the persistent decode kernel (the one the CUDA graph replays) eagerly
+ * at the current position, recording device timestamps (ns) per CTA and phase. out
+ * receives: [0] grid size G, [1] phase count P, [2..2+P) the QWC_K_* kind of each phase,
+ * then G*P*8 values, CTA-major, phase-minor: stamps of phase start, barrier passed,
+ * GEMV prologue done, phase end; then for GEMV phases the ns spent waiting on weight
+ * slots and the slot count, for attention phases stamps after its prologue, main loop,
+ * warp merge and split combine.
+ * Returns the number of int64 values needed (when cap is too small nothing runs), or an
+ * error code (QWC_E_INVALID when the persistent kernel is not in use). Allocates a
+ * temporary device buffer. */
+int qwc_trace_step(qwc_handle* h, int cap, int64_t* out);
+
 /* ---------------------------------------------------------------- kernel level */
 
 /* matmul(const WeightView&, ...) (src/forward_pass.cpp:65-75) on device memory:

@@ -26,7 +26,8 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_create", "qwc_create_from_dir", "qwc_destroy", "qwc_last_error", "qwc_get_budget",
            "qwc_get_config", "qwc_reset", "qwc_position", "qwc_step", "qwc_generate_greedy",
            "qwc_forward_logits", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
-           "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_gemv_bf16",
+           "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
+           "qwc_gemv_bf16",
            "qwc_gdn_decode_step", "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
                 6: "lm_head"}
@@ -102,6 +103,7 @@ def lib():
     L.qwc_enqueue_greedy.argtypes = [vp, C.c_int, C.c_int]
     L.qwc_read_tokens.argtypes = [vp, C.c_int, C.c_int, ip]
     L.qwc_profile_step.argtypes = [vp, C.c_int, ip, C.POINTER(C.c_float), C.POINTER(C.c_int64)]
+    L.qwc_trace_step.argtypes = [vp, C.c_int, C.POINTER(C.c_int64)]
     L.qwc_gemv_bf16.argtypes = [vp, vp, vp, C.c_int, C.c_int, vp]
     L.qwc_gdn_decode_step.argtypes = [vp] * 9 + [C.c_int, C.c_int, C.c_int, vp]
     L.qwc_attention_decode.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -219,6 +221,22 @@ class Model:
             check(n, self._h)
         n = min(n, cap)
         return [(KERNEL_KINDS[int(kind[i])], float(ms[i]), int(by[i])) for i in range(n)]
+
+    def trace_step(self):
+        """One eager step of the persistent decode kernel with device timestamps.
+        Returns (kinds[P], stamps[G, P, 8]) or None when that kernel is not in use."""
+        need = lib().qwc_trace_step(self._h, 0, None)
+        if need < 0:
+            if need == -1:
+                return None
+            check(need, self._h)
+        buf = np.zeros(need, np.int64)
+        rc = lib().qwc_trace_step(self._h, need, buf.ctypes.data_as(C.POINTER(C.c_int64)))
+        if rc < 0:
+            check(rc, self._h)
+        G, P = int(buf[0]), int(buf[1])
+        kinds = [KERNEL_KINDS[int(k)] for k in buf[2:2 + P]]
+        return kinds, buf[2 + P:].reshape(G, P, 8)
 
     def prefill(self, ids, logits: bool = True):
         """Prefill that seeds the decode state; returns the last position's logits."""

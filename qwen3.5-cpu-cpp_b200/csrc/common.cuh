@@ -17,6 +17,7 @@ enum DevError : int {
     DEV_BAD_TOKEN = 4,            // token id out of range at the embedding
     DEV_BAD_POS = 5,              // position beyond the KV cache
     DEV_PREFILL_TIMEOUT = 6,
+    DEV_STEP_BARRIER_TIMEOUT = 7, // a persistent-step CTA waited too long for the grid
 };
 
 __device__ __forceinline__ void post_error(int* flag, int code) {
@@ -101,6 +102,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// As bulk_g2s, with an L2 cache-policy hint (e.g. evict-first for streamed weights).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+        "[%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// L2 policy: lines brought in under it are the first candidates for eviction.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
 // Hint: pull [src, src+bytes) into L2 (no completion to wait on).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
@@ -128,4 +144,23 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
+}  // namespace qwc
+
+namespace qwc {
+// Loads n floats (n % 4 == 0, 16-byte aligned) with up to kMaxV float4 per thread issued
+// before any is used, so the whole vector costs one memory round trip instead of one per
+// loop iteration. Returns false (nothing loaded) if n exceeds 4*kMaxV*nthreads.
+template <int kMaxV>
+__device__ __forceinline__ bool load_vec4(const float* __restrict__ src, int n, int t, int nthreads,
+                                          float4 (&r)[kMaxV]) {
+    const int n4 = n >> 2;
+    if (n4 > kMaxV * nthreads) return false;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+    for (int k = 0; k < kMaxV; ++k) {
+        const int i = t + k * nthreads;
+        r[k] = i < n4 ? s4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return true;
+}
 }  // namespace qwc

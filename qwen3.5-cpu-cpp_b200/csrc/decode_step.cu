@@ -1,0 +1,720 @@
+// Persistent decode-step kernel: one launch runs a whole QwenModel::step()
+// (src/qwen_model.cpp:211-239) -- embedding, every layer, final norm, lm_head and the
+// greedy argmax -- as a sequence of phases separated by grid-wide barriers.
+//
+// Why: at batch 1 every projection is a small GEMV (1-17 MB). As separate kernels each
+// one pays a launch plus several dependent memory round trips after its input is ready,
+// and can keep only ~64 KB of weights in flight per SM in registers. Here one CTA per SM
+// lives for the whole step, and every warp streams the weight rows it owns -- for the
+// current GEMV phase and, ahead of time, for the following ones -- through its own ring
+// of 4 KB shared-memory slots filled by 1-D bulk TMA copies (cp.async.bulk; eight
+// issuing warps per SM with 4 KB copies sustain ~6.4 TB/s). Before blocking on a phase
+// barrier a warp tops its ring up, so HBM keeps streaming while the grid waits, while
+// the GDN recurrence and the attention run, and while activations are exchanged.
+// Weights never depend on activations; only x (the GEMV input vector) and the small
+// mixer phases wait for the barrier.
+//
+// Phase types (descriptors built once on the host, in global memory, staged per phase
+// in shared memory):
+//   GEMV  y = W x with the fused prologues/epilogues of the GEMV family (kernels.h);
+//         rows split into NC balanced CTA ranges, each into 8 balanced warp ranges;
+//         a warp's range is one contiguous byte stream consumed in 512 B groups.
+//   GDN   the recurrent mixer core (gdn_body.cuh), one (value head, 16-column) item per
+//         CTA on warps 0-3; the state slice is loaded before the barrier.
+//   ATTN  split-K decode attention (attn_body.cuh), one (kv head, split) item per CTA.
+// Each phase body is a separate non-inlined function so that it gets its own register
+// allocation (one inlined body would spill the others' hot loops).
+//
+// Barrier: every CTA adds 1 to a 64-bit arrival counter after a phase; phase p may start
+// when the counter reaches p * NC. The last CTA to finish the step resets it. All waits
+// are bounded (they post an error code and stop the step instead of hanging), and the
+// kernel is launched cooperatively, so all CTAs are co-resident.
+#include "attn_body.cuh"
+#include "gdn_body.cuh"
+
+#include <algorithm>
+#include <type_traits>
+
+namespace qwc {
+
+constexpr int kSW = 8;                 // warps per CTA
+constexpr int kSThreads = kSW * 32;
+constexpr int kChunkBytes = 4096;      // one ring slot = one bulk copy
+constexpr int kGroupBytes = 512;       // 32 lanes x 16 B
+constexpr int kGroupsPerChunk = kChunkBytes / kGroupBytes;
+constexpr int kMaxSlots = 8;
+
+// Compact per-phase stream description kept in shared memory for the issue cursor.
+struct PhaseBrief {
+    const uint16_t* W;  // nullptr: not a GEMV phase
+    int rows, in_dim;
+};
+
+// Per-warp ring cursors, kept in shared memory between phases.
+struct RingState {
+    const uint8_t* src;   // start of this warp's rows in the phase being issued
+    long long off;        // bytes of that range already issued
+    long long bytes;      // size of that range (-1: not computed yet)
+    int ip;               // phase being issued
+    int issued;           // chunks issued so far
+    int islot;            // slot of the next chunk to issue
+    int consumed;         // chunks consumed so far
+    int cslot;            // slot of the next chunk to consume
+    uint32_t cpar;        // mbarrier parity of that slot
+};
+
+// Block-shared bookkeeping of the step kernel.
+struct StepShared {
+    uint8_t* ring;        // [kSW][nslot][kChunkBytes]
+    float* xs;            // GEMV input vector
+    uint64_t* full;       // [kSW][nslot] mbarriers
+    PhaseBrief* brief;    // [nphases]
+    StepPhase* ph;        // staged descriptor of the current phase
+    RingState rings[kSW];
+    double red_d[kSW];
+    float rv[kSW];
+    int ri[kSW];
+    int s_last;
+    int abort;            // CTA-uniform: an error was posted
+};
+
+struct StepSmem {
+    size_t ring, xs, bars, brief, phase, total;
+};
+static __host__ __device__ inline StepSmem step_smem_plan(int nslot, int xs_max, int nphases) {
+    StepSmem s;
+    s.ring = 0;
+    s.xs = (size_t)kSW * nslot * kChunkBytes;
+    s.bars = s.xs + (((size_t)xs_max * 4 + 127) / 128) * 128;
+    s.brief = s.bars + (((size_t)kSW * nslot * 8 + 15) / 16) * 16;
+    s.phase = s.brief + (((size_t)nphases * sizeof(PhaseBrief) + 127) / 128) * 128;
+    s.total = s.phase + ((sizeof(StepPhase) + 127) / 128) * 128;
+    return s;
+}
+
+// rows [a, b) of warp w in CTA c for a GEMV phase
+__device__ __forceinline__ void warp_rows(int rows, int c, int nc, int w, int& a, int& b) {
+    const int r0 = (int)((long long)rows * c / nc), r1 = (int)((long long)rows * (c + 1) / nc);
+    const int nr = r1 - r0;
+    a = r0 + (int)((long long)nr * w / kSW);
+    b = r0 + (int)((long long)nr * (w + 1) / kSW);
+}
+
+// dot of 8 bf16 weights (one uint4) with 8 fp32 x values in shared memory
+__device__ __forceinline__ float dot8s(uint4 w, const float* x, float acc) {
+    const float4 x0 = *reinterpret_cast<const float4*>(x);
+    const float4 x1 = *reinterpret_cast<const float4*>(x + 4);
+    acc = fmaf(bf16lo(w.x), x0.x, acc);
+    acc = fmaf(bf16hi(w.x), x0.y, acc);
+    acc = fmaf(bf16lo(w.y), x0.z, acc);
+    acc = fmaf(bf16hi(w.y), x0.w, acc);
+    acc = fmaf(bf16lo(w.z), x1.x, acc);
+    acc = fmaf(bf16hi(w.z), x1.y, acc);
+    acc = fmaf(bf16lo(w.w), x1.z, acc);
+    acc = fmaf(bf16hi(w.w), x1.w, acc);
+    return acc;
+}
+
+__device__ __forceinline__ bool step_aborted(const StepParams& sp) {
+    return *reinterpret_cast<const volatile int*>(sp.dev_err) != 0;
+}
+
+__device__ __forceinline__ void trace_mark(const StepParams& sp, int c, int p, int k) {
+    if (sp.trace && threadIdx.x == 0)
+        sp.trace[((size_t)c * sp.nphases + p) * 8 + k] = (long long)globaltimer_ns();
+}
+
+// Issue bulk copies of this warp's weight stream (register copy r of its cursors) until
+// `limit` chunks are issued. All lanes run it (uniform values); lane 31 issues.
+__device__ __forceinline__ void ring_issue(RingState& r, const StepShared& S, const StepParams& sp, int c,
+                                           int nc, int limit) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nslot = sp.nslot;
+    uint8_t* my_ring = S.ring + (size_t)warp * nslot * kChunkBytes;
+    uint64_t* my_full = S.full + warp * nslot;
+    while (r.issued < limit) {
+        while (r.ip < sp.nphases) {
+            if (r.bytes < 0) {
+                const PhaseBrief bf = S.brief[r.ip];
+                if (bf.W) {
+                    int a, b;
+                    warp_rows(bf.rows, c, nc, warp, a, b);
+                    r.bytes = (long long)(b - a) * bf.in_dim * 2;
+                    r.src = reinterpret_cast<const uint8_t*>(bf.W + (size_t)a * bf.in_dim);
+                } else {
+                    r.bytes = 0;
+                }
+                r.off = 0;
+            }
+            if (r.off < r.bytes) break;
+            ++r.ip;
+            r.bytes = -1;
+        }
+        if (r.ip >= sp.nphases) return;
+        const uint32_t len = (uint32_t)min((long long)kChunkBytes, r.bytes - r.off);
+        const int slot = r.islot;
+        if (++r.islot == nslot) r.islot = 0;
+        if (lane == 31) {
+            // Lane 31 issues, so that the lane-0 threads that fence and signal the grid
+            // barriers never have bulk copies of their own in flight.
+            // The slot was last read through the generic proxy by this warp.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(&my_full[slot], len);
+            // weights are read once per step: evict them first, keep activations, KV rows
+            // and partial results resident in L2
+            bulk_g2s_hint(my_ring + (size_t)slot * kChunkBytes, r.src + r.off, len, &my_full[slot],
+                          l2_policy_evict_first());
+        }
+        r.off += len;
+        ++r.issued;
+    }
+}
+
+__device__ __noinline__ void ring_topup(StepShared& S, const StepParams sp, int c, int nc) {
+    const int warp = threadIdx.x >> 5;
+    RingState r = S.rings[warp];
+    ring_issue(r, S, sp, c, nc, r.consumed + sp.nslot);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) S.rings[warp] = r;
+    __syncwarp();
+}
+
+// Grid barrier: all CTAs finished phase p-1. Leaves S.abort CTA-uniform.
+__device__ __noinline__ void grid_wait(StepShared& S, const StepParams sp, int p, int c, int nc) {
+    const int tid = threadIdx.x;
+    if (tid == 0 && p > 0) {
+        const unsigned long long target = (unsigned long long)p * nc;
+        const volatile unsigned long long* ctr = sp.bar;
+        if (*ctr < target) {
+            // Poll with a short sleep: ~150 CTAs spinning back-to-back on one L2 line
+            // would delay the arrivals (and every atomic near that line) they wait for.
+            const unsigned long long t0 = globaltimer_ns();
+            while (*ctr < target) {
+                __nanosleep(100);
+                if (step_aborted(sp)) break;
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    post_error(sp.dev_err, DEV_STEP_BARRIER_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    if (tid == 0) S.abort = step_aborted(sp) ? 1 : 0;
+    __syncthreads();
+    trace_mark(sp, c, p, 1);
+}
+
+// ---------------------------------------------------------------------- GEMV phase
+__device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int p, int c, int nc) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const StepPhase& ph = *S.ph;
+    const int pro = ph.pro, epi = ph.epi;
+    const int xlen = ph.g.x_len, in = ph.g.in_dim;
+    float* const y = ph.g.y;
+    float* const xs = S.xs;
+    const float eps = ph.g.eps;
+
+    // ---- prologue: x into shared memory, every load issued before any use
+    if (pro == PRO_GATED_NORM) {
+        // one warp per head of gn_dim values: w * (o * inv_head) * silu(z)
+        const int D = ph.g.gn_dim, nh = xlen / D;
+        const float* x0 = ph.g.x;
+        const float* z0 = ph.g.z;
+        const float* nw = ph.g.norm_w;
+        for (int h = warp; h < nh; h += kSW) {
+            const float* o = x0 + (size_t)h * D;
+            const float* zz = z0 + (size_t)h * D;
+            float ov[4], zv[4], wv4[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = lane + 32 * k;
+                const bool in_r = i < D;
+                ov[k] = in_r ? o[i] : 0.f;
+                zv[k] = in_r ? zz[i] : 0.f;
+                wv4[k] = in_r ? nw[i] : 0.f;
+            }
+            double ss = 0.0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ss += (double)ov[k] * ov[k];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            const float inv = 1.0f / sqrtf((float)(ss / D) + eps);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = lane + 32 * k;
+                if (i < D) xs[(size_t)h * D + i] = wv4[k] * (ov[k] * inv) * silu_f(zv[k]);
+            }
+        }
+        __syncthreads();
+    } else {
+        const float* src = ph.g.x;
+        if (pro == PRO_EMBED_RMSNORM) {
+            int tok = ph.g.tokens[*ph.g.pos];
+            if (tok < 0 || tok >= ph.g.vocab) {
+                if (tid == 0) post_error(sp.dev_err, DEV_BAD_TOKEN);
+                tok = 0;
+            }
+            const uint16_t* erow = ph.g.embed + (size_t)tok * xlen;
+            float* hout = ph.g.hidden_out;
+            for (int i = tid; i < xlen; i += kSThreads) {
+                const float v = __uint_as_float((uint32_t)erow[i] << 16);
+                xs[i] = v;
+                if (c == 0) hout[i] = v;
+            }
+            __syncthreads();
+            src = xs;
+        }
+        // x (and the norm weight) in registers: one round trip per 4096 elements
+        constexpr int kV = 4;
+        const int n4 = xlen >> 2;
+        float4* xs4 = reinterpret_cast<float4*>(xs);
+        if (pro == PRO_PLAIN) {
+            for (int base = 0; base < n4; base += kV * kSThreads) {
+                float4 xv[kV];
+                load_vec4<kV>(src + 4 * base, 4 * min(n4 - base, kV * kSThreads), tid, kSThreads, xv);
+#pragma unroll
+                for (int k = 0; k < kV; ++k) {
+                    const int i = base + tid + k * kSThreads;
+                    if (i < n4) xs4[i] = xv[k];
+                }
+            }
+        } else {  // RMSNORM (xlen <= 4096: checked when the phases are built)
+            float4 xv[kV], wv[kV];
+            load_vec4<kV>(src, xlen, tid, kSThreads, xv);
+            load_vec4<kV>(ph.g.norm_w, xlen, tid, kSThreads, wv);
+            double ss = 0.0;
+#pragma unroll
+            for (int k = 0; k < kV; ++k)
+                ss += (double)xv[k].x * xv[k].x + (double)xv[k].y * xv[k].y + (double)xv[k].z * xv[k].z +
+                      (double)xv[k].w * xv[k].w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) S.red_d[warp] = ss;
+            __syncthreads();
+            ss = 0.0;
+#pragma unroll
+            for (int w = 0; w < kSW; ++w) ss += S.red_d[w];
+            const float inv = 1.0f / sqrtf((float)(ss / xlen) + eps);
+#pragma unroll
+            for (int k = 0; k < kV; ++k) {
+                const int i = tid + k * kSThreads;
+                if (i < n4) {
+                    float4 v = xv[k];
+                    v.x = v.x * inv * wv[k].x;
+                    v.y = v.y * inv * wv[k].y;
+                    v.z = v.z * inv * wv[k].z;
+                    v.w = v.w * inv * wv[k].w;
+                    xs4[i] = v;
+                }
+            }
+        }
+        __syncthreads();
+    }
+    trace_mark(sp, c, p, 2);
+
+    // ---- this warp's weight stream
+    int a, b;
+    warp_rows(ph.g.rows, c, nc, warp, a, b);
+    const int bytes = (b - a) * in * 2;
+    RingState r = S.rings[warp];
+    const int nslot = sp.nslot;
+    const uint8_t* my_ring = S.ring + (size_t)warp * nslot * kChunkBytes;
+    uint64_t* my_full = S.full + warp * nslot;
+    float best = -INFINITY;
+    int best_idx = 0x7fffffff;
+    int row = a;
+    int res_base = a;
+    float res = 0.f;
+    if (epi == EPI_RESIDUAL) res = (a + lane < b) ? y[a + lane] : 0.f;
+    long long waited_ns = 0;
+    int nchunks = 0;
+
+    // epilogue of one finished row (lane 0 stores); residuals prefetched 32 rows at a time
+    auto finish_row = [&](auto epi_tag, float sum, float su) {
+        constexpr int EPI = decltype(epi_tag)::value;
+        float resv = 0.f;
+        if constexpr (EPI == EPI_RESIDUAL) {
+            if (row - res_base >= 32) {
+                res_base += 32;
+                res = (res_base + lane < b) ? y[res_base + lane] : 0.f;
+            }
+            resv = __shfl_sync(0xffffffffu, res, row - res_base);
+        }
+        if (lane == 0) {
+            if constexpr (EPI == EPI_STORE) y[row] = sum;
+            else if constexpr (EPI == EPI_RESIDUAL) y[row] = resv + sum;
+            else if constexpr (EPI == EPI_SWIGLU) y[row] = silu_f(sum) * su;
+            else {
+                y[row] = sum;
+                if (sum > best) { best = sum; best_idx = row; }
+            }
+        }
+        ++row;
+    };
+    auto next_chunk = [&](const uint4*& wv) -> bool {
+        const unsigned long long tw = sp.trace ? globaltimer_ns() : 0ull;
+        if (!mbar_wait_bounded(&my_full[r.cslot], r.cpar, sp.dev_err, DEV_GEMV_FULL_TIMEOUT)) return false;
+        if (sp.trace) {
+            waited_ns += (long long)(globaltimer_ns() - tw);
+            ++nchunks;
+        }
+        wv = reinterpret_cast<const uint4*>(my_ring + (size_t)r.cslot * kChunkBytes);
+        return true;
+    };
+    auto release_chunk = [&]() {
+        ++r.consumed;
+        if (++r.cslot == nslot) { r.cslot = 0; r.cpar ^= 1u; }
+        __syncwarp();
+        ring_issue(r, S, sp, c, nc, r.consumed + nslot);
+    };
+    // Specialised stream: GPR groups per row, x (XG groups) in registers. Chunks hold 8
+    // groups and start on a row boundary (GPR divides 8), so each group's x slice,
+    // gate/up half and row end are compile-time.
+    auto stream_fast = [&](auto epi_tag, auto gpr_tag, auto xg_tag) {
+        constexpr int EPI = decltype(epi_tag)::value;
+        constexpr int GPR = decltype(gpr_tag)::value;
+        constexpr int XG = decltype(xg_tag)::value;
+        float xr[XG][8];
+#pragma unroll
+        for (int k = 0; k < XG; ++k) {
+            const float4 v0 = *reinterpret_cast<const float4*>(xs + k * 256 + lane * 8);
+            const float4 v1 = *reinterpret_cast<const float4*>(xs + k * 256 + lane * 8 + 4);
+            xr[k][0] = v0.x; xr[k][1] = v0.y; xr[k][2] = v0.z; xr[k][3] = v0.w;
+            xr[k][4] = v1.x; xr[k][5] = v1.y; xr[k][6] = v1.z; xr[k][7] = v1.w;
+        }
+        float acc = 0.f, acc_u = 0.f;
+        for (int off = 0; off < bytes; off += kChunkBytes) {
+            const uint4* wv;
+            if (!next_chunk(wv)) return;
+            const int ng = min(kChunkBytes, bytes - off) / kGroupBytes;
+            uint4 w[kGroupsPerChunk];
+#pragma unroll
+            for (int gi = 0; gi < kGroupsPerChunk; ++gi)
+                w[gi] = gi < ng ? wv[gi * 32 + lane] : make_uint4(0u, 0u, 0u, 0u);
+            float pt[kGroupsPerChunk];
+#pragma unroll
+            for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
+                const float* xx = xr[gi % XG];
+                float d = 0.f;
+                d = fmaf(bf16lo(w[gi].x), xx[0], d);
+                d = fmaf(bf16hi(w[gi].x), xx[1], d);
+                d = fmaf(bf16lo(w[gi].y), xx[2], d);
+                d = fmaf(bf16hi(w[gi].y), xx[3], d);
+                d = fmaf(bf16lo(w[gi].z), xx[4], d);
+                d = fmaf(bf16hi(w[gi].z), xx[5], d);
+                d = fmaf(bf16lo(w[gi].w), xx[6], d);
+                d = fmaf(bf16hi(w[gi].w), xx[7], d);
+                pt[gi] = d;
+            }
+#pragma unroll
+            for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
+                if (gi < ng) {
+                    const int qq = gi % GPR;  // position of the group in its row
+                    if (EPI == EPI_SWIGLU && qq >= XG) acc_u += pt[gi];
+                    else acc += pt[gi];
+                    if (qq == GPR - 1) {
+                        const float sum = warp_sum(acc);
+                        const float su = EPI == EPI_SWIGLU ? warp_sum(acc_u) : 0.f;
+                        finish_row(epi_tag, sum, su);
+                        acc = 0.f;
+                        acc_u = 0.f;
+                    }
+                }
+            }
+            release_chunk();
+        }
+    };
+    // Generic stream: x from shared memory, row position tracked at run time.
+    auto stream_generic = [&](auto epi_tag) {
+        constexpr int EPI = decltype(epi_tag)::value;
+        const int gpr = in >> 8;
+        int q = 0;
+        float acc = 0.f, acc_u = 0.f;
+        for (int off = 0; off < bytes; off += kChunkBytes) {
+            const uint4* wv;
+            if (!next_chunk(wv)) return;
+            const int ng = min(kChunkBytes, bytes - off) / kGroupBytes;
+#pragma unroll 4
+            for (int gi = 0; gi < ng; ++gi) {
+                const uint4 w = wv[gi * 32 + lane];
+                const int col = q * 256 + lane * 8;
+                if (EPI == EPI_SWIGLU && col >= xlen) acc_u = dot8s(w, xs + (col - xlen), acc_u);
+                else acc = dot8s(w, xs + col, acc);
+                if (q == gpr - 1) {
+                    const float sum = warp_sum(acc);
+                    const float su = EPI == EPI_SWIGLU ? warp_sum(acc_u) : 0.f;
+                    finish_row(epi_tag, sum, su);
+                    acc = 0.f;
+                    acc_u = 0.f;
+                    q = 0;
+                } else {
+                    ++q;
+                }
+            }
+            release_chunk();
+        }
+    };
+    using I4 = std::integral_constant<int, 4>;
+    using I8 = std::integral_constant<int, 8>;
+    const int gpr = in >> 8, xg = xlen >> 8;
+    auto run = [&](auto epi_tag) {
+        constexpr int EPI = decltype(epi_tag)::value;
+        if constexpr (EPI == EPI_SWIGLU) {
+            if (gpr == 8 && xg == 4) stream_fast(epi_tag, I8{}, I4{});
+            else stream_generic(epi_tag);
+        } else {
+            if (gpr == 4 && xg == 4) stream_fast(epi_tag, I4{}, I4{});
+            else stream_generic(epi_tag);
+        }
+    };
+    if (epi == EPI_STORE) run(std::integral_constant<int, EPI_STORE>{});
+    else if (epi == EPI_RESIDUAL) run(std::integral_constant<int, EPI_RESIDUAL>{});
+    else if (epi == EPI_SWIGLU) run(std::integral_constant<int, EPI_SWIGLU>{});
+    else run(std::integral_constant<int, EPI_ARGMAX>{});
+    __syncwarp();
+    if (lane == 0) S.rings[warp] = r;
+    if (sp.trace && tid == 0) {
+        sp.trace[((size_t)c * sp.nphases + p) * 8 + 4] = waited_ns;
+        sp.trace[((size_t)c * sp.nphases + p) * 8 + 5] = nchunks;
+    }
+
+    if (epi == EPI_ARGMAX) {
+        // CTA argmax (larger wins, ties -> lower index), then the grid ticket
+        const GemvParams& g = ph.g;
+        if (lane == 0) { S.rv[warp] = best; S.ri[warp] = best_idx; }
+        __syncthreads();
+        if (tid == 0) {
+            float bv = S.rv[0];
+            int bi = S.ri[0];
+            for (int w = 1; w < kSW; ++w)
+                if (S.rv[w] > bv || (S.rv[w] == bv && S.ri[w] < bi)) { bv = S.rv[w]; bi = S.ri[w]; }
+            g.am_val[c] = bv;
+            g.am_idx[c] = bi;
+            __threadfence();
+            S.s_last = (atomicAdd(g.am_counter, 1u) == (unsigned)nc - 1) ? 1 : 0;
+        }
+        __syncthreads();
+        if (S.s_last) {
+            __threadfence();
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int k = tid; k < nc; k += kSThreads) {
+                const float v = __ldcg(&g.am_val[k]);
+                const int i = __ldcg(&g.am_idx[k]);
+                if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            __syncthreads();
+            if (lane == 0) { S.rv[warp] = bv; S.ri[warp] = bi; }
+            __syncthreads();
+            if (tid == 0) {
+                bv = S.rv[0];
+                bi = S.ri[0];
+                for (int w = 1; w < kSW; ++w)
+                    if (S.rv[w] > bv || (S.rv[w] == bv && S.ri[w] < bi)) { bv = S.rv[w]; bi = S.ri[w]; }
+                if (bi == 0x7fffffff) bi = 0;
+                if (g.argmax_out) *g.argmax_out = bi;
+                if (g.pos_inout) {
+                    const int pos = *g.pos_inout;
+                    if (g.tokens_out && pos + 1 < g.max_ctx && pos + 1 >= *g.n_prompt) g.tokens_out[pos + 1] = bi;
+                    *g.pos_inout = pos + 1;
+                }
+                *g.am_counter = 0u;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------- GDN phase
+// Warps 0-3 run the item (state slice loaded before the barrier); all threads take
+// part in the barrier.
+__device__ __noinline__ void gdn_phase(StepShared& S, const StepParams sp, int p, int c, int nc) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const GdnDecodeParams& d = S.ph->d;
+    const int items = d.VH * (128 / 16);
+    bool waited = false;
+    if (warp < 4) {
+        for (int it = c; it < items; it += nc) {
+            const int vh = it >> 3, vs = it & 7;
+            if (!waited) {
+                gdn_decode_item(d, vh, vs, tid, [&] { grid_wait(S, sp, p, c, nc); });
+                waited = true;
+            } else {
+                gdn_decode_item(d, vh, vs, tid, [] {});
+            }
+        }
+    }
+    if (warp >= 4 || c >= items) grid_wait(S, sp, p, c, nc);
+}
+
+// ---------------------------------------------------------------------- attention phase
+template <int GRP>
+__device__ __noinline__ void attn_phase(StepShared& S, const StepParams sp, int p, int c, int nc) {
+    const AttnDecodeParams at = S.ph->a;
+    const int items = at.NKV * at.nsplit;
+    long long* marks = sp.trace ? sp.trace + ((size_t)c * sp.nphases + p) * 8 + 4 : nullptr;
+    for (int it = c; it < items; it += nc) attn_decode_item<GRP>(at, it % at.NKV, it / at.NKV, marks);
+}
+
+__device__ __noinline__ void ring_drain(StepShared& S, const StepParams sp) {
+    // Every issued copy has been consumed on the normal path; after an error, wait
+    // (bounded) for the copies still in flight before the CTA may exit.
+    const int warp = threadIdx.x >> 5;
+    RingState r = S.rings[warp];
+    uint64_t* my_full = S.full + warp * sp.nslot;
+    bool ok = true;
+    for (int k = r.consumed; k < r.issued && ok; ++k) {
+        ok = mbar_wait_bounded(&my_full[r.cslot], r.cpar, sp.dev_err, DEV_GEMV_DRAIN_TIMEOUT);
+        if (++r.cslot == sp.nslot) { r.cslot = 0; r.cpar ^= 1u; }
+    }
+}
+
+template <int GRP>
+__global__ void __launch_bounds__(kSThreads, 1) k_decode_step(const StepParams sp) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ StepShared S;
+    const int tid = threadIdx.x;
+    const int c = blockIdx.x, nc = gridDim.x;
+    const StepSmem plan = step_smem_plan(sp.nslot, sp.xs_max, sp.nphases);
+
+    if (tid == 0) {
+        S.ring = smem;
+        S.xs = reinterpret_cast<float*>(smem + plan.xs);
+        S.full = reinterpret_cast<uint64_t*>(smem + plan.bars);
+        S.brief = reinterpret_cast<PhaseBrief*>(smem + plan.brief);
+        S.ph = reinterpret_cast<StepPhase*>(smem + plan.phase);
+        S.abort = 0;
+    }
+    if (tid < kSW) {
+        RingState r;
+        r.src = nullptr;
+        r.off = 0;
+        r.bytes = -1;
+        r.ip = 0;
+        r.issued = 0;
+        r.islot = 0;
+        r.consumed = 0;
+        r.cslot = 0;
+        r.cpar = 0;
+        S.rings[tid] = r;
+    }
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.bars);
+    if (tid < kSW * sp.nslot) mbar_init(&full[tid], 1);
+    if (tid == 0) fence_mbar_init();
+    PhaseBrief* brief = reinterpret_cast<PhaseBrief*>(smem + plan.brief);
+    for (int q = tid; q < sp.nphases; q += kSThreads) {
+        const StepPhase& g = sp.phases[q];
+        PhaseBrief bf;
+        bf.W = g.type == PH_GEMV ? g.g.W : nullptr;
+        bf.rows = g.g.rows;
+        bf.in_dim = g.g.in_dim;
+        brief[q] = bf;
+    }
+    __syncthreads();
+
+    StepPhase* ph = reinterpret_cast<StepPhase*>(smem + plan.phase);
+    for (int p = 0; p < sp.nphases; ++p) {
+        trace_mark(sp, c, p, 0);
+        // stage this phase's descriptor (the previous phase ended with a CTA barrier)
+        {
+            const int4* src = reinterpret_cast<const int4*>(sp.phases + p);
+            int4* dst = reinterpret_cast<int4*>(ph);
+            for (int q = tid; q < (int)(sizeof(StepPhase) / 16); q += kSThreads) dst[q] = src[q];
+        }
+        ring_topup(S, sp, c, nc);  // keep HBM busy across the barrier
+        __syncthreads();
+        const int type = ph->type;
+        if (type == PH_GDN) {
+            gdn_phase(S, sp, p, c, nc);
+        } else {
+            grid_wait(S, sp, p, c, nc);
+            if (type == PH_ATTN) attn_phase<GRP>(S, sp, p, c, nc);
+            else if (!S.abort) gemv_phase(S, sp, p, c, nc);
+        }
+        trace_mark(sp, c, p, 3);
+        if (p + 1 < sp.nphases) {
+            __syncthreads();  // (also ends every read of the staged descriptor)
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(sp.bar, 1ull);
+            }
+        }
+    }
+    ring_drain(S, sp);
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(sp.done, 1u) == (unsigned)nc - 1) {  // last CTA of the step
+            *sp.bar = 0ull;
+            *sp.done = 0u;
+        }
+    }
+}
+
+size_t step_smem_bytes(int nslot, int xs_max, int nphases) { return step_smem_plan(nslot, xs_max, nphases).total; }
+
+int step_slots(int xs_max, int grp, int nphases) {
+    // static shared memory: StepShared + the attention body (grows with the GQA group)
+    const size_t static_bytes = sizeof(StepShared) + (size_t)grp * 1024 + 2048 + 8192 + 2048 + 1024;
+    const size_t budget = 227 * 1024 - static_bytes;
+    int n = kMaxSlots;
+    while (n > 2 && step_smem_plan(n, xs_max, nphases).total > budget) --n;
+    return n;
+}
+
+template <int GRP>
+static cudaError_t launch_step_t(const StepParams& sp, int grid, cudaStream_t s) {
+    const size_t smem = step_smem_bytes(sp.nslot, sp.xs_max, sp.nphases);
+    auto kern = k_decode_step<GRP>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kSThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, sp);
+}
+
+cudaError_t launch_decode_step(const StepParams& sp, int grp, int grid, cudaStream_t s) {
+    switch (grp) {
+        case 1: return launch_step_t<1>(sp, grid, s);
+        case 2: return launch_step_t<2>(sp, grid, s);
+        case 4: return launch_step_t<4>(sp, grid, s);
+        case 8: return launch_step_t<8>(sp, grid, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int GRP>
+static int max_grid_t(size_t smem) {
+    int per_sm = 0;
+    cudaFuncSetAttribute(k_decode_step<GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_step<GRP>, kSThreads, smem) != cudaSuccess)
+        return 0;
+    return per_sm >= 1 ? num_sms() : 0;  // one CTA per SM
+}
+
+int decode_step_max_grid(int grp, int nslot, int xs_max, int nphases) {
+    const size_t smem = step_smem_bytes(nslot, xs_max, nphases);
+    switch (grp) {
+        case 1: return max_grid_t<1>(smem);
+        case 2: return max_grid_t<2>(smem);
+        case 4: return max_grid_t<4>(smem);
+        case 8: return max_grid_t<8>(smem);
+        default: return 0;
+    }
+}
+
+}  // namespace qwc

@@ -81,7 +81,7 @@ struct qwc_handle {
     const uint16_t* embed = nullptr;
     const uint16_t* head = nullptr;
     const float* final_ln1 = nullptr;
-    const double* inv_freq = nullptr;
+    const float* rope_cs = nullptr;  // [max_ctx][rot/2][2] RoPE cos/sin per position
 
     // scratch views
     float *hidden = nullptr, *proj = nullptr, *mix = nullptr, *ffn_h = nullptr, *logits = nullptr;
@@ -91,6 +91,14 @@ struct qwc_handle {
     unsigned *am_counter = nullptr, *attn_counters = nullptr;
 
     int* h_pin = nullptr;  // pinned host ints for small transfers
+
+    // persistent decode-step kernel (step_grid == 0: per-kernel path)
+    StepParams step;
+    StepPhase* step_phases = nullptr;  // device array
+    int step_grid = 0;
+    std::vector<int> step_kinds;  // QWC_K_* of each phase
+    unsigned long long* step_bar = nullptr;
+    unsigned* step_done = nullptr;
 
     cudaGraphExec_t graph = nullptr;
     bool use_graph = true, use_pdl = true;
@@ -379,7 +387,7 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
     h->embed = (const uint16_t*)a.take((size_t)h->V * H * 2);
     h->head = lmh ? (const uint16_t*)a.take((size_t)h->V * H * 2) : h->embed;
     h->final_ln1 = (const float*)a.take((size_t)H * 4);
-    h->inv_freq = (const double*)a.take((size_t)(h->ROT / 2 + 1) * 8);
+    h->rope_cs = (const float*)a.take((size_t)h->max_ctx * (h->ROT / 2) * 2 * 4 + 16);
     if (doit && b.missing.empty()) {
         int rc;
         if (emb->ndim != 2 || emb->shape[1] != H || emb->shape[0] < h->V)
@@ -395,9 +403,21 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
             CU(cudaMemcpy(const_cast<uint16_t*>(h->head), lmh->data, (size_t)h->V * H * 2, cudaMemcpyHostToDevice));
         }
         if ((rc = vec_f32(h, fn, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(h->final_ln1), tmp))) return rc;
-        std::vector<double> invf(h->ROT / 2 + 1, 0.0);
-        for (int i = 0; i < h->ROT / 2; ++i) invf[i] = std::pow(h->cfg.rope_theta, -(double)(2 * i) / h->ROT);
-        CU(cudaMemcpy(const_cast<double*>(h->inv_freq), invf.data(), invf.size() * 8, cudaMemcpyHostToDevice));
+        // RoPE table, exactly as apply_rope evaluates it (src/forward_pass.cpp:102-112):
+        // inv_freq and the angle in double, cos/sin in double, rounded to float.
+        const int half = h->ROT / 2;
+        if (half > 0) {
+            std::vector<double> invf(half);
+            for (int i = 0; i < half; ++i) invf[i] = std::pow(h->cfg.rope_theta, -(double)(2 * i) / h->ROT);
+            std::vector<float> tab((size_t)h->max_ctx * half * 2);
+            for (int pp = 0; pp < h->max_ctx; ++pp)
+                for (int i = 0; i < half; ++i) {
+                    const double ang = (double)pp * invf[i];
+                    tab[((size_t)pp * half + i) * 2] = (float)std::cos(ang);
+                    tab[((size_t)pp * half + i) * 2 + 1] = (float)std::sin(ang);
+                }
+            CU(cudaMemcpy(const_cast<float*>(h->rope_cs), tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+        }
     }
     if (!b.missing.empty()) return fail(h, QWC_E_MISSING, "[qwen] missing weight: " + b.missing);
     return QWC_OK;
@@ -419,26 +439,23 @@ struct StepProfile {
     std::vector<int64_t> bytes;
 };
 
-// Enqueue one decode step (embedding -> layers -> norm -> lm_head + argmax) on h->stream.
-static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfile* prof = nullptr,
-                        int pos_for_bytes = 0) {
+// The decode step as a list of phases (one per kernel of the per-kernel path, one per
+// grid-barrier phase of the persistent kernel), with the profiling kind of each.
+static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std::vector<StepPhase>& out,
+                        std::vector<int>& kinds) {
     const int H = h->H;
-    bool first = true;
-    auto PDL = [&]() { bool r = pdl && !first; first = false; return r; };
-    auto rec = [&](int kind, int64_t bytes) -> int {
-        if (!prof) return QWC_OK;
-        if (prof->n < prof->cap) {
-            CU(cudaEventRecord(prof->ev[prof->n + 1], h->stream));
-            prof->kind[prof->n] = kind;
-            prof->bytes[prof->n] = bytes;
-        }
-        prof->n++;
-        return QWC_OK;
-    };
-    if (prof) CU(cudaEventRecord(prof->ev[0], h->stream));
-    int rc;
-    const int64_t kvb = h->kv_bytes;
+    out.clear();
+    kinds.clear();
     const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
+    auto gemv = [&](int pro, int epi, const GemvParams& g, int kind) {
+        StepPhase ph;
+        ph.type = PH_GEMV;
+        ph.pro = pro;
+        ph.epi = epi;
+        ph.g = g;
+        out.push_back(ph);
+        kinds.push_back(kind);
+    };
     for (int L = 0; L < h->L; ++L) {
         const Layer& lw = h->layers[L];
         // mixer input projection with the input RMSNorm (and the embedding at layer 0)
@@ -459,14 +476,15 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
             p.vocab = h->V;
             p.hidden_out = h->hidden;
         }
-        CU(launch_gemv(pro, EPI_STORE, p, gemv_grid(p.rows), h->stream, PDL()));
-        if ((rc = rec(QWC_K_MIX_IN, (int64_t)p.rows * H * 2 + (int64_t)H * 8 + (int64_t)p.rows * 4))) return rc;
+        gemv(pro, EPI_STORE, p, QWC_K_MIX_IN);
         if (lw.is_attn) {
-            AttnDecodeParams a;
+            StepPhase ph;
+            ph.type = PH_ATTN;
+            AttnDecodeParams& a = ph.a;
             a.proj = h->proj;
             a.qn1 = lw.qn1;
             a.kn1 = lw.kn1;
-            a.inv_freq = h->inv_freq;
+            a.rope_cs = h->rope_cs;
             uint8_t* kvl = static_cast<uint8_t*>(sv.kv) + kv_layer * lw.idx;
             a.k_cache = kvl;
             a.v_cache = kvl + kv_layer / 2;
@@ -480,12 +498,10 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
             a.NQ = h->NQ;
             a.NKV = h->NKV;
             a.rot = h->ROT;
-            a.nsplit = h->nsplit;
+            a.nsplit = attn_nsplit;
             a.eps = h->eps;
-            CU(launch_attn_decode(a, h->stream, PDL()));
-            if ((rc = rec(QWC_K_ATTN, (int64_t)(pos_for_bytes + 1) * h->NKV * h->HD * kvb * 2 +
-                                          (int64_t)lw.in_rows * 4 + (int64_t)h->NQ * h->HD * 4)))
-                return rc;
+            out.push_back(ph);
+            kinds.push_back(QWC_K_ATTN);
             GemvParams o = gp_base(h);
             o.W = lw.w_out;
             o.rows = H;
@@ -493,10 +509,11 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
             o.x_len = lw.out_in;
             o.x = h->mix;
             o.y = h->hidden;
-            CU(launch_gemv(PRO_PLAIN, EPI_RESIDUAL, o, gemv_grid(H), h->stream, PDL()));
-            if ((rc = rec(QWC_K_MIX_OUT, (int64_t)H * lw.out_in * 2 + (int64_t)lw.out_in * 4 + (int64_t)H * 8))) return rc;
+            gemv(PRO_PLAIN, EPI_RESIDUAL, o, QWC_K_MIX_OUT);
         } else {
-            GdnDecodeParams g;
+            StepPhase ph;
+            ph.type = PH_GDN;
+            GdnDecodeParams& g = ph.d;
             g.mixed = h->proj;
             g.b = h->proj + h->C + h->VD;
             g.a = h->proj + h->C + h->VD + h->VH;
@@ -509,10 +526,8 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
             g.pos_ptr = h->pos;
             g.KH = h->KH;
             g.VH = h->VH;
-            CU(launch_gdn_decode(g, h->stream, PDL()));
-            if ((rc = rec(QWC_K_GDN, (int64_t)h->VH * h->DK * h->DV * 8 + (int64_t)h->C * (16 + 4 + 16 + 4) +
-                                         (int64_t)h->VD * 4)))
-                return rc;
+            out.push_back(ph);
+            kinds.push_back(QWC_K_GDN);
             GemvParams o = gp_base(h);
             o.W = lw.w_out;
             o.rows = H;
@@ -523,8 +538,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
             o.norm_w = lw.gn_w;
             o.gn_dim = h->DV;
             o.y = h->hidden;
-            CU(launch_gemv(PRO_GATED_NORM, EPI_RESIDUAL, o, gemv_grid(H), h->stream, PDL()));
-            if ((rc = rec(QWC_K_MIX_OUT, (int64_t)H * h->VD * 2 + (int64_t)h->VD * 8 + (int64_t)H * 8))) return rc;
+            gemv(PRO_GATED_NORM, EPI_RESIDUAL, o, QWC_K_MIX_OUT);
         }
         // FFN: post-attention RMSNorm + gate/up + SwiGLU, then down + residual
         GemvParams f = gp_base(h);
@@ -535,8 +549,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
         f.x = h->hidden;
         f.norm_w = lw.post_ln1;
         f.y = h->ffn_h;
-        CU(launch_gemv(PRO_RMSNORM, EPI_SWIGLU, f, gemv_grid(h->I), h->stream, PDL()));
-        if ((rc = rec(QWC_K_GATE_UP, (int64_t)h->I * 2 * H * 2 + (int64_t)H * 8 + (int64_t)h->I * 4))) return rc;
+        gemv(PRO_RMSNORM, EPI_SWIGLU, f, QWC_K_GATE_UP);
         GemvParams d = gp_base(h);
         d.W = lw.w_down;
         d.rows = H;
@@ -544,8 +557,7 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
         d.x_len = h->I;
         d.x = h->ffn_h;
         d.y = h->hidden;
-        CU(launch_gemv(PRO_PLAIN, EPI_RESIDUAL, d, gemv_grid(H), h->stream, PDL()));
-        if ((rc = rec(QWC_K_DOWN, (int64_t)H * h->I * 2 + (int64_t)h->I * 4 + (int64_t)H * 8))) return rc;
+        gemv(PRO_PLAIN, EPI_RESIDUAL, d, QWC_K_DOWN);
     }
     GemvParams o = gp_base(h);
     o.W = h->head;
@@ -563,8 +575,55 @@ static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfil
     o.n_prompt = h->n_prompt;
     o.pos_inout = h->pos;
     o.max_ctx = sv.max_ctx;
-    CU(launch_gemv(PRO_RMSNORM, EPI_ARGMAX, o, gemv_grid(h->V), h->stream, PDL()));
-    if ((rc = rec(QWC_K_LM_HEAD, (int64_t)h->V * H * 2 + (int64_t)H * 8 + (int64_t)h->V * 4))) return rc;
+    gemv(PRO_RMSNORM, EPI_ARGMAX, o, QWC_K_LM_HEAD);
+}
+
+// Algorithmic HBM bytes of one phase at position `pos` (for qwc_profile_step).
+static int64_t phase_bytes(const qwc_handle* h, const StepPhase& ph, int pos) {
+    if (ph.type == PH_GEMV) {
+        const GemvParams& g = ph.g;
+        return (int64_t)g.rows * g.in_dim * 2 + (int64_t)g.x_len * 8 +
+               (int64_t)g.rows * (ph.epi == EPI_RESIDUAL ? 8 : 4);
+    }
+    if (ph.type == PH_GDN)
+        return (int64_t)h->VH * h->DK * h->DV * 8 + (int64_t)h->C * (16 + 4 + 16 + 4) + (int64_t)h->VD * 4;
+    return (int64_t)(pos + 1) * h->NKV * h->HD * h->kv_bytes * 2 + (int64_t)(2 * h->NQ * h->HD + 2 * h->NKV * h->HD) * 4 +
+           (int64_t)h->NQ * h->HD * 4;
+}
+
+// Enqueue one decode step as separate kernels (embedding -> layers -> lm_head + argmax).
+static int enqueue_step(qwc_handle* h, const StateView& sv, bool pdl, StepProfile* prof = nullptr,
+                        int pos_for_bytes = 0) {
+    std::vector<StepPhase> phases;
+    std::vector<int> kinds;
+    make_phases(h, sv, h->nsplit, phases, kinds);
+    if (prof) CU(cudaEventRecord(prof->ev[0], h->stream));
+    for (size_t i = 0; i < phases.size(); ++i) {
+        const StepPhase& ph = phases[i];
+        const bool use_pdl = pdl && i > 0;
+        if (ph.type == PH_GEMV) {
+            const int per_sm = ph.epi == EPI_ARGMAX ? 2 : 1;
+            CU(launch_gemv(ph.pro, ph.epi, ph.g, gemv_grid(ph.g.rows, per_sm), h->stream, use_pdl));
+        } else if (ph.type == PH_GDN) {
+            CU(launch_gdn_decode(ph.d, h->stream, use_pdl));
+        } else {
+            CU(launch_attn_decode(ph.a, h->stream, use_pdl));
+        }
+        if (prof) {
+            if (prof->n < prof->cap) {
+                CU(cudaEventRecord(prof->ev[prof->n + 1], h->stream));
+                prof->kind[prof->n] = kinds[i];
+                prof->bytes[prof->n] = phase_bytes(h, ph, pos_for_bytes);
+            }
+            prof->n++;
+        }
+    }
+    return QWC_OK;
+}
+
+// One launch of the persistent decode-step kernel.
+static int enqueue_persistent(qwc_handle* h) {
+    CU(launch_decode_step(h->step, h->NQ / h->NKV, h->step_grid, h->stream));
     return QWC_OK;
 }
 
@@ -576,7 +635,7 @@ static int build_graph(qwc_handle* h) {
     if (!h->use_graph) return QWC_OK;
     cudaGraph_t g = nullptr;
     CU(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(h, h->st, h->use_pdl);
+    int rc = h->step_grid > 0 ? enqueue_persistent(h) : enqueue_step(h, h->st, h->use_pdl);
     cudaError_t e = cudaStreamEndCapture(h->stream, &g);
     if (rc != QWC_OK) {
         if (g) cudaGraphDestroy(g);
@@ -594,7 +653,42 @@ static int run_step(qwc_handle* h) {
         CU(cudaGraphLaunch(h->graph, h->stream));
         return QWC_OK;
     }
-    return enqueue_step(h, h->st, h->use_pdl);
+    return h->step_grid > 0 ? enqueue_persistent(h) : enqueue_step(h, h->st, h->use_pdl);
+}
+
+// Choose the persistent decode-step kernel when the shapes allow it (every GEMV input
+// length a multiple of 256, one co-resident CTA per SM) unless QWC_DECODE=kernels.
+static int setup_persistent(qwc_handle* h) {
+    h->step_grid = 0;
+    const char* mode = std::getenv("QWC_DECODE");
+    if (mode && std::string(mode) == "kernels") return QWC_OK;
+    const int grp = h->NQ / h->NKV;
+    if (h->H % 256 || h->I % 256 || h->VD % 256 || (h->NQ * h->HD) % 256 || h->H > 4096) return QWC_OK;
+    const int xs_max = std::max({h->H, h->I, h->VD, h->NQ * h->HD});
+    const int grid0 = num_sms();
+    // attention items are spread one per CTA: at most grid / NKV splits
+    const int nsplit = std::max(1, std::min(h->nsplit, grid0 / h->NKV));
+    std::vector<StepPhase> phases;
+    make_phases(h, h->st, nsplit, phases, h->step_kinds);
+    const int np = (int)phases.size();
+    // Ring depth: two or three 4 KB slots per warp (64-96 KB per SM) already sustain
+    // full HBM bandwidth; deeper rings only queue latency-critical loads (barrier polls,
+    // activations, KV rows) behind prefetched weights.
+    int nslot = std::min(step_slots(xs_max, grp, np), 3);
+    if (const char* e = std::getenv("QWC_STEP_SLOTS")) nslot = std::max(2, std::min(step_slots(xs_max, grp, np), std::atoi(e)));
+    const int grid = decode_step_max_grid(grp, nslot, xs_max, np);
+    if (grid <= 0) return QWC_OK;
+    CU(cudaMalloc(&h->step_phases, phases.size() * sizeof(StepPhase)));
+    CU(cudaMemcpy(h->step_phases, phases.data(), phases.size() * sizeof(StepPhase), cudaMemcpyHostToDevice));
+    h->step.phases = h->step_phases;
+    h->step.nphases = (int)phases.size();
+    h->step.bar = h->step_bar;
+    h->step.done = h->step_done;
+    h->step.dev_err = h->dev_err;
+    h->step.nslot = nslot;
+    h->step.xs_max = xs_max;
+    h->step_grid = grid;
+    return QWC_OK;
 }
 
 // ------------------------------------------------------------------ create / destroy
@@ -628,6 +722,7 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     cudaFree(h->st.conv_ring);
     cudaFree(h->st.kv);
     cudaFree(h->scratch);
+    cudaFree(h->step_phases);
     if (h->h_pin) cudaFreeHost(h->h_pin);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
@@ -720,7 +815,7 @@ extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int 
     Arena s;
     auto carve = [&](size_t bytes) { return s.take(bytes); };
     const int proj_n = std::max(h->C + h->VD + 2 * h->VH, 2 * h->NQ * h->HD + 2 * h->NKV * h->HD);
-    const int nsm = num_sms();
+    const int nsm = gemv_grid(h->V, 2);  // CTAs of the lm_head GEMV: one argmax partial each
     struct { void** p; size_t bytes; } plan[] = {
         {(void**)&h->hidden, (size_t)h->H * 4},
         {(void**)&h->proj, (size_t)proj_n * 4},
@@ -738,6 +833,9 @@ extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int 
         {(void**)&h->n_prompt, 16},
         {(void**)&h->argmax, 16},
         {(void**)&h->dev_err, 16},
+        // grid-barrier counters on their own 4 KB lines, away from the other counters
+        {(void**)&h->step_bar, 4096},
+        {(void**)&h->step_done, 4096},
     };
     for (auto& e : plan) carve(e.bytes);
     h->scratch_bytes = s.off;
@@ -756,7 +854,16 @@ extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int 
 
     rc = qwc_reset(h);
     if (rc) return bail(rc);
+    rc = setup_persistent(h);
+    if (rc) return bail(rc);
     rc = build_graph(h);
+    if (rc && h->step_grid > 0) {
+        // the persistent kernel could not be captured: use the per-kernel path
+        std::fprintf(stderr, "[qwc] persistent decode step unavailable (%s); using separate kernels\n",
+                     h->err.c_str());
+        h->step_grid = 0;
+        rc = build_graph(h);
+    }
     if (rc) return bail(rc);
     *out = h;
     return QWC_OK;
@@ -771,6 +878,8 @@ extern "C" int qwc_reset(qwc_handle* h) {
     if (h->conv_bytes) CU(cudaMemsetAsync(h->st.conv_ring, 0, h->conv_bytes, h->stream));
     if (h->kvc_bytes) CU(cudaMemsetAsync(h->st.kv, 0, h->kvc_bytes, h->stream));
     CU(cudaMemsetAsync(h->pos, 0, sizeof(int), h->stream));
+    if (h->step_bar) CU(cudaMemsetAsync(h->step_bar, 0, 16, h->stream));
+    if (h->step_done) CU(cudaMemsetAsync(h->step_done, 0, 16, h->stream));
     CU(cudaStreamSynchronize(h->stream));
     h->pos_host = 0;
     return QWC_OK;
@@ -984,6 +1093,39 @@ extern "C" int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, in
     if (rc != QWC_OK) return rc;
     h->pos_host++;
     return prof.n;
+}
+
+extern "C" int qwc_trace_step(qwc_handle* h, int cap, int64_t* out) {
+    if (!h || cap < 0 || (cap > 0 && !out)) return fail(h, QWC_E_INVALID, "qwc_trace_step: invalid argument");
+    if (h->step_grid <= 0) return fail(h, QWC_E_INVALID, "qwc_trace_step: the persistent decode step is not in use");
+    if (h->pos_host >= h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_trace_step: context full");
+    CU(cudaSetDevice(h->device));
+    const int np = h->step.nphases, grid = h->step_grid;
+    const size_t n = (size_t)grid * np * 8;
+    const int need = 2 + np + (int)n;
+    if (cap < need) return need;  // ask for a bigger buffer
+    long long* d = nullptr;
+    CU(cudaMalloc(&d, n * sizeof(long long)));
+    CU(cudaMemset(d, 0, n * sizeof(long long)));
+    StepParams sp = h->step;
+    sp.trace = d;
+    h->h_pin[6] = h->max_ctx;
+    int rc = QWC_OK;
+    if (cudaMemcpyAsync(h->n_prompt, &h->h_pin[6], sizeof(int), cudaMemcpyHostToDevice, h->stream) != cudaSuccess ||
+        launch_decode_step(sp, h->NQ / h->NKV, grid, h->stream) != cudaSuccess)
+        rc = fail(h, QWC_E_CUDA, "qwc_trace_step: launch failed");
+    if (rc == QWC_OK) rc = check_device_error(h);
+    if (rc == QWC_OK) {
+        out[0] = grid;
+        out[1] = np;
+        for (int i = 0; i < np; ++i) out[2 + i] = h->step_kinds[i];
+        if (cudaMemcpy(out + 2 + np, d, n * sizeof(long long), cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = fail(h, QWC_E_CUDA, "qwc_trace_step: copy failed");
+    }
+    cudaFree(d);
+    if (rc != QWC_OK) return rc;
+    h->pos_host++;
+    return need;
 }
 
 // ------------------------------------------------------------------ kernel-level API

@@ -1,158 +1,125 @@
-// Decode GEMV family: bf16 weight streaming by 1-D bulk TMA into a shared-memory ring,
-// fp32 dot products on CUDA cores, fused prologues/epilogues (see kernels.h).
+// Decode GEMV family: bf16 weights streamed from HBM straight into registers, fp32 dot
+// products on CUDA cores, fused prologues/epilogues (see kernels.h).
 //
-// Work split. The rows of W are cut into gridDim contiguous, balanced ranges (one CTA
-// per SM). Inside a CTA, consumer warp w owns rows r0+w, r0+w+8, ...; each row is
-// staged in segments of up to 1024 elements (2 KB). Every consumer warp has its own
-// `slots_per_warp` ring slots (a full/empty mbarrier pair each); one producer warp
-// issues the bulk copies round-robin over the warps. The first ring fill (up to 96 KB
-// per CTA) is issued BEFORE griddepcontrol.wait, so under programmatic dependent
-// launch the weights of this kernel stream in while the previous kernel finishes.
+// Work split. The rows of W are cut into gridDim balanced contiguous ranges (one CTA per
+// SM), and each CTA range into 8 balanced contiguous warp ranges. A warp walks its rows
+// as one flat stream of "groups": 32 lanes x 16 bytes = 256 consecutive elements of a
+// row. Loads are 128-bit, non-coherent, L1-bypassing, issued in batches of kU groups per
+// lane into two register buffers used in ping-pong, so every warp keeps up to 2*kU x 512 B
+// in flight; two CTAs per SM.
+//
+// Programmatic dependent launch: the weights do not depend on the previous kernel, so
+// before griddepcontrol.wait each warp (a) asks L2 to prefetch the start of its row
+// block and (b) issues its first register batch. Only x (the activation) waits.
 #include "common.cuh"
 #include "kernels.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace qwc {
 
-constexpr int kCW = 8;                    // consumer warps
-constexpr int kThreads = (kCW + 1) * 32;  // + 1 producer warp
-constexpr int kSeg = 1024;                // elements per staged segment
-constexpr int kMaxSlots = 6;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kU = 8;                       // groups per batch per lane
+constexpr uint32_t kPrefetchPiece = 8192;   // bytes per L2 prefetch request
+constexpr uint32_t kPrefetchCap = 32768;    // bytes prefetched per warp before the wait
 
-struct SmemPlan {
-    size_t ring, xs, bars, red, total;
-};
+size_t gemv_smem_bytes(const GemvParams& p) { return ((size_t)p.x_len * 4 + 15) / 16 * 16; }
 
-static __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
-static __host__ __device__ inline SmemPlan plan_smem(int x_len, int slots) {
-    SmemPlan s;
-    s.ring = 0;
-    size_t ring_bytes = (size_t)kCW * slots * kSeg * 2;
-    s.xs = ring_bytes;
-    s.bars = align_up(s.xs + (size_t)x_len * 4, 16);
-    s.red = s.bars + (size_t)2 * kCW * slots * 8;
-    s.total = align_up(s.red + 64 * 4, 128);
-    return s;
-}
-
-size_t gemv_smem_bytes(const GemvParams& p) { return plan_smem(p.x_len, p.slots_per_warp).total; }
-
-// Consumer-warp named barrier (the producer warp does not take part).
-__device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory");
+// 128-bit streaming load: read-only path, no L1 allocation, 256-byte L2 fetch granule.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
 }
 
 // dot of 8 bf16 weights (one uint4) with 8 fp32 x values
 __device__ __forceinline__ float dot8(uint4 w, const float* x, float acc) {
-    acc = fmaf(bf16lo(w.x), x[0], acc);
-    acc = fmaf(bf16hi(w.x), x[1], acc);
-    acc = fmaf(bf16lo(w.y), x[2], acc);
-    acc = fmaf(bf16hi(w.y), x[3], acc);
-    acc = fmaf(bf16lo(w.z), x[4], acc);
-    acc = fmaf(bf16hi(w.z), x[5], acc);
-    acc = fmaf(bf16lo(w.w), x[6], acc);
-    acc = fmaf(bf16hi(w.w), x[7], acc);
+    const float4 x0 = *reinterpret_cast<const float4*>(x);
+    const float4 x1 = *reinterpret_cast<const float4*>(x + 4);
+    acc = fmaf(bf16lo(w.x), x0.x, acc);
+    acc = fmaf(bf16hi(w.x), x0.y, acc);
+    acc = fmaf(bf16lo(w.y), x0.z, acc);
+    acc = fmaf(bf16hi(w.y), x0.w, acc);
+    acc = fmaf(bf16lo(w.z), x1.x, acc);
+    acc = fmaf(bf16hi(w.z), x1.y, acc);
+    acc = fmaf(bf16lo(w.w), x1.z, acc);
+    acc = fmaf(bf16hi(w.w), x1.w, acc);
     return acc;
 }
 
-// Block-wide (consumer warps) sum in double, identical result in every thread.
-__device__ __forceinline__ double consumers_sum_d(double v, double* red_d) {
+// Block-wide sum in double, identical result in every thread.
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) red_d[warp] = v;
-    consumers_sync();
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
     double s = 0.0;
 #pragma unroll
-    for (int w = 0; w < kCW; ++w) s += red_d[w];
-    consumers_sync();
+    for (int w = 0; w < kWarps; ++w) s += red[w];
     return s;
 }
 
-template <int PRO, int EPI, bool XREG>
+// Cursor over a warp's group stream: group -> (row, q), q = group index inside the row.
+struct Cursor {
+    int row, q;
+    __device__ __forceinline__ void next(int gpr) {
+        if (++q == gpr) { q = 0; ++row; }
+    }
+};
+
+template <int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) k_gemv(const GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int SL = p.slots_per_warp;
-    const SmemPlan plan = plan_smem(p.x_len, SL);
-    uint16_t* ring = reinterpret_cast<uint16_t*>(smem);
-    float* xs = reinterpret_cast<float*>(smem + plan.xs);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.bars);
-    uint64_t* empty = full + kCW * SL;
-    double* red_d = reinterpret_cast<double*>(smem + plan.red);
+    extern __shared__ __align__(16) float xs[];
+    __shared__ double red_d[kWarps];
+    __shared__ float rv[kWarps];
+    __shared__ int ri[kWarps];
+    __shared__ int s_last;
 
     const int in = p.in_dim, xlen = p.x_len;
-    const int seg_len = in < kSeg ? in : kSeg;
-    const int nseg = (in + seg_len - 1) / seg_len;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cpr = in >> 3;             // 16-byte chunks per row
+    const int gpr = (cpr + 31) >> 5;     // groups per row
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int r0 = (int)((long long)p.rows * blockIdx.x / gridDim.x);
     const int r1 = (int)((long long)p.rows * (blockIdx.x + 1) / gridDim.x);
+    const int nr = r1 - r0;
+    const int a = r0 + (int)((long long)nr * warp / kWarps);
+    const int b = r0 + (int)((long long)nr * (warp + 1) / kWarps);
+    const long long G = (long long)(b - a) * gpr;
+    const uint16_t* W = p.W;
 
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kCW * SL; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-        }
-        fence_mbar_init();
+    // ---- before the dependency wait: L2 prefetch + first register batch of weights
+    if (b > a) {
+        const uint8_t* base = reinterpret_cast<const uint8_t*>(W + (size_t)a * in);
+        const size_t bytes = (size_t)(b - a) * in * 2;
+        const uint32_t cap = kPrefetchCap, piece = kPrefetchPiece;
+        const uint32_t lim = bytes < (size_t)cap ? (uint32_t)bytes : cap;
+        for (uint32_t off = lane * piece; off < lim; off += 32 * piece)
+            bulk_prefetch_l2(base + off, min(piece, lim - off));
     }
-    __syncthreads();
-
-    // ------------------------------------------------------------ producer warp
-    if (warp == kCW) {
-        if (lane == 0) {
-            const int max_rows_w = (r1 - r0 + kCW - 1) / kCW;
-            const int max_items = max_rows_w * nseg;
-            int issued[kCW * kMaxSlots];
-            for (int i = 0; i < kCW * SL; ++i) issued[i] = 0;
-            bool ok = true, waited = false;
-            for (int k = 0; k < max_items && ok; ++k) {
-                if (k == SL && !waited) {
-                    pdl_wait();
-                    pdl_launch_dependents();
-                    waited = true;
-                }
-                const int j = k / nseg, s = k - j * nseg;
-                for (int w = 0; w < kCW; ++w) {
-                    const int row = r0 + w + kCW * j;
-                    if (row >= r1) break;
-                    const int slot = w * SL + (k % SL);
-                    if (k >= SL &&
-                        !mbar_wait_bounded(&empty[slot], ((k / SL) - 1) & 1, p.dev_err, DEV_GEMV_EMPTY_TIMEOUT)) {
-                        ok = false;
-                        break;
-                    }
-                    const int c0 = s * seg_len;
-                    const int len = min(seg_len, in - c0);
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)len * 2);
-                    bulk_g2s(ring + (size_t)slot * kSeg, p.W + (size_t)row * in + c0, (uint32_t)len * 2,
-                             &full[slot]);
-                    issued[slot]++;
-                }
-            }
-            if (!waited) {
-                pdl_wait();
-                pdl_launch_dependents();
-            }
-            // Drain: every issued copy must have landed before this CTA may exit. One
-            // overall time window; after it expires the remaining slots are not awaited.
-            bool drained = true;
-            for (int i = 0; i < kCW * SL && drained; ++i)
-                if (issued[i] > 0)
-                    drained = mbar_wait_bounded(&full[i], (issued[i] - 1) & 1, p.dev_err, DEV_GEMV_DRAIN_TIMEOUT);
+    uint4 cur[kU], nxt[kU];
+    Cursor lc{a, 0};  // load cursor
+    auto load_batch = [&](long long g0, uint4* dst) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int c = lc.q * 32 + lane;
+            if (g0 + u < G && c < cpr) dst[u] = ld_stream(W + (size_t)lc.row * in + (size_t)c * 8);
+            else dst[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (g0 + u < G) lc.next(gpr);
         }
-        return;
-    }
+    };
+    load_batch(0, cur);
 
-    // ------------------------------------------------------------ consumer warps
     pdl_wait();
-    const int tid = threadIdx.x;  // 0 .. kCW*32-1
-    constexpr int NT = kCW * 32;
+    // ---- prologue: build x in shared memory
     if constexpr (PRO == PRO_PLAIN) {
-        for (int i = tid; i < xlen; i += NT) xs[i] = p.x[i];
-        consumers_sync();
+        for (int i = tid; i < xlen; i += kThreads) xs[i] = p.x[i];
+        __syncthreads();
     } else if constexpr (PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM) {
-        const float* src = p.x;
         if constexpr (PRO == PRO_EMBED_RMSNORM) {
             int tok = p.tokens[*p.pos];
             if (tok < 0 || tok >= p.vocab) {
@@ -160,114 +127,92 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv(const GemvParams p) {
                 tok = 0;
             }
             const uint16_t* row = p.embed + (size_t)tok * xlen;
-            for (int i = tid; i < xlen; i += NT) {
-                float v = __uint_as_float((uint32_t)row[i] << 16);
+            for (int i = tid; i < xlen; i += kThreads) {
+                const float v = __uint_as_float((uint32_t)row[i] << 16);
                 xs[i] = v;
                 if (blockIdx.x == 0) p.hidden_out[i] = v;
             }
-            consumers_sync();
         } else {
-            for (int i = tid; i < xlen; i += NT) xs[i] = src[i];
-            consumers_sync();
+            for (int i = tid; i < xlen; i += kThreads) xs[i] = p.x[i];
         }
         double ss = 0.0;
-        for (int i = tid; i < xlen; i += NT) ss += (double)xs[i] * xs[i];
-        ss = consumers_sum_d(ss, red_d);
+        for (int i = tid; i < xlen; i += kThreads) ss += (double)xs[i] * xs[i];
+        ss = block_sum_d(ss, red_d);  // also orders the xs stores above
         const float inv = 1.0f / sqrtf((float)(ss / xlen) + p.eps);
-        for (int i = tid; i < xlen; i += NT) xs[i] = xs[i] * inv * p.norm_w[i];
-        consumers_sync();
+        for (int i = tid; i < xlen; i += kThreads) xs[i] = xs[i] * inv * p.norm_w[i];
+        __syncthreads();
     } else if constexpr (PRO == PRO_GATED_NORM) {
         // one warp per head of gn_dim values: w * (o * inv_head) * silu(z)
         const int D = p.gn_dim, nh = xlen / D;
-        for (int h = warp; h < nh; h += kCW) {
+        for (int h = warp; h < nh; h += kWarps) {
             const float* o = p.x + (size_t)h * D;
             double ss = 0.0;
             for (int i = lane; i < D; i += 32) ss += (double)o[i] * o[i];
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
             const float inv = 1.0f / sqrtf((float)(ss / D) + p.eps);
-            for (int i = lane; i < D; i += 32) {
-                const float zz = p.z[(size_t)h * D + i];
-                xs[(size_t)h * D + i] = p.norm_w[i] * (o[i] * inv) * silu_f(zz);
-            }
+            for (int i = lane; i < D; i += 32)
+                xs[(size_t)h * D + i] = p.norm_w[i] * (o[i] * inv) * silu_f(p.z[(size_t)h * D + i]);
         }
-        consumers_sync();
+        __syncthreads();
     }
     pdl_launch_dependents();
 
-    // x chunks of this lane in registers when one 1024-element segment spans all of x
-    float xr[XREG ? 4 : 1][8];
-    if constexpr (XREG) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xr[c][e] = xs[(lane + 32 * c) * 8 + e];
-    }
-
+    // ---- main stream: two register buffers in ping-pong, no copies between them, so
+    // one batch stays in flight while the other is consumed
+    float acc = 0.f, acc_u = 0.f;
     float best = -INFINITY;
     int best_idx = 0x7fffffff;
-    bool ok = true;
-    int k = 0;  // item counter of this warp
-    for (int row = r0 + warp; row < r1 && ok; row += kCW) {
-        float acc = 0.f, acc_u = 0.f;
-        for (int s = 0; s < nseg; ++s, ++k) {
-            const int slot = warp * SL + (k % SL);
-            if (!mbar_wait_bounded(&full[slot], (k / SL) & 1, p.dev_err, DEV_GEMV_FULL_TIMEOUT)) {
-                ok = false;
-                break;
-            }
-            const uint4* wv = reinterpret_cast<const uint4*>(ring + (size_t)slot * kSeg);
-            const int c0 = s * seg_len;
-            const int nch = min(seg_len, in - c0) / 8;
-            if constexpr (XREG) {
-                float a = 0.f;
+    Cursor cc{a, 0};  // compute cursor
+    auto consume = [&](long long g0, const uint4* buf) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int ch = lane + 32 * c;
-                    if (ch < nch) a = dot8(wv[ch], xr[c], a);
+        for (int u = 0; u < kU; ++u) {
+            if (g0 + u < G) {
+                const int c = cc.q * 32 + lane;
+                if (c < cpr) {
+                    const int col = c * 8;
+                    if (EPI == EPI_SWIGLU && col >= xlen) acc_u = dot8(buf[u], xs + (col - xlen), acc_u);
+                    else acc = dot8(buf[u], xs + col, acc);
                 }
-                if (EPI == EPI_SWIGLU && c0 >= xlen) acc_u += a; else acc += a;
-            } else {
-                for (int ch = lane; ch < nch; ch += 32) {
-                    const int col = c0 + ch * 8;
-                    if (EPI == EPI_SWIGLU && col >= xlen) {
-                        acc_u = dot8(wv[ch], xs + (col - xlen), acc_u);
-                    } else {
-                        acc = dot8(wv[ch], xs + col, acc);
+                if (cc.q == gpr - 1) {
+                    const float s = warp_sum(acc);
+                    float su = 0.f;
+                    if constexpr (EPI == EPI_SWIGLU) su = warp_sum(acc_u);
+                    if (lane == 0) {
+                        const int row = cc.row;
+                        if constexpr (EPI == EPI_STORE) {
+                            p.y[row] = s;
+                        } else if constexpr (EPI == EPI_RESIDUAL) {
+                            p.y[row] = p.y[row] + s;
+                        } else if constexpr (EPI == EPI_SWIGLU) {
+                            p.y[row] = silu_f(s) * su;
+                        } else {
+                            p.y[row] = s;
+                            if (s > best) { best = s; best_idx = row; }
+                        }
                     }
+                    acc = 0.f;
+                    acc_u = 0.f;
                 }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        if (!ok) break;
-        acc = warp_sum(acc);
-        if constexpr (EPI == EPI_SWIGLU) acc_u = warp_sum(acc_u);
-        if (lane == 0) {
-            if constexpr (EPI == EPI_STORE) {
-                p.y[row] = acc;
-            } else if constexpr (EPI == EPI_RESIDUAL) {
-                p.y[row] = p.y[row] + acc;
-            } else if constexpr (EPI == EPI_SWIGLU) {
-                p.y[row] = silu_f(acc) * acc_u;
-            } else {
-                p.y[row] = acc;
-                if (acc > best) { best = acc; best_idx = row; }
+                cc.next(gpr);
             }
         }
+    };
+    for (long long g0 = 0; g0 < G; g0 += 2 * kU) {
+        if (g0 + kU < G) load_batch(g0 + kU, nxt);
+        consume(g0, cur);
+        if (g0 + 2 * kU < G) load_batch(g0 + 2 * kU, cur);
+        if (g0 + kU < G) consume(g0 + kU, nxt);
     }
 
     if constexpr (EPI == EPI_ARGMAX) {
         // CTA argmax: larger value wins, equal values -> lower index (strict '>' scan).
-        float* rv = reinterpret_cast<float*>(red_d);
-        int* ri = reinterpret_cast<int*>(rv + kCW);
         if (lane == 0) { rv[warp] = best; ri[warp] = best_idx; }
-        consumers_sync();
-        __shared__ int s_last;
+        __syncthreads();
         if (tid == 0) {
             float bv = rv[0];
             int bi = ri[0];
-            for (int w = 1; w < kCW; ++w)
+            for (int w = 1; w < kWarps; ++w)
                 if (rv[w] > bv || (rv[w] == bv && ri[w] < bi)) { bv = rv[w]; bi = ri[w]; }
             p.am_val[blockIdx.x] = bv;
             p.am_idx[blockIdx.x] = bi;
@@ -275,12 +220,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv(const GemvParams p) {
             const unsigned t = atomicAdd(p.am_counter, 1u);
             s_last = (t == gridDim.x - 1) ? 1 : 0;
         }
-        consumers_sync();
+        __syncthreads();
         if (s_last) {
             __threadfence();
             float bv = -INFINITY;
             int bi = 0x7fffffff;
-            for (int c = tid; c < (int)gridDim.x; c += NT) {
+            for (int c = tid; c < (int)gridDim.x; c += kThreads) {
                 const float v = __ldcg(&p.am_val[c]);
                 const int i = __ldcg(&p.am_idx[c]);
                 if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
@@ -291,19 +236,19 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv(const GemvParams p) {
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
             }
+            __syncthreads();
             if (lane == 0) { rv[warp] = bv; ri[warp] = bi; }
-            consumers_sync();
+            __syncthreads();
             if (tid == 0) {
                 bv = rv[0];
                 bi = ri[0];
-                for (int w = 1; w < kCW; ++w)
+                for (int w = 1; w < kWarps; ++w)
                     if (rv[w] > bv || (rv[w] == bv && ri[w] < bi)) { bv = rv[w]; bi = ri[w]; }
                 if (bi == 0x7fffffff) bi = 0;  // all logits NaN: the reference scan keeps id 0
                 if (p.argmax_out) *p.argmax_out = bi;
                 if (p.pos_inout) {
                     const int pos = *p.pos_inout;
-                    if (p.tokens_out && pos + 1 < p.max_ctx && pos + 1 >= *p.n_prompt)
-                        p.tokens_out[pos + 1] = bi;
+                    if (p.tokens_out && pos + 1 < p.max_ctx && pos + 1 >= *p.n_prompt) p.tokens_out[pos + 1] = bi;
                     *p.pos_inout = pos + 1;
                 }
                 *p.am_counter = 0u;
@@ -323,15 +268,26 @@ int num_sms() {
     return n;
 }
 
-int gemv_grid(int rows) { return std::max(1, std::min(rows, num_sms())); }
+// One CTA per SM by default: a GEMV CTA holds half of an SM's registers, so the CTA of
+// the next kernel (programmatic dependent launch) fits beside it and prefetches its own
+// weights while this one streams. The lm_head, last of the step, uses two per SM.
+int gemv_grid(int rows, int per_sm) {
+    static int override_per_sm = -1;
+    if (override_per_sm < 0) {
+        const char* e = std::getenv("QWC_GEMV_CTAS_PER_SM");  // tuning knob, 0 = default
+        override_per_sm = e ? std::atoi(e) : 0;
+    }
+    if (override_per_sm > 0) per_sm = override_per_sm;
+    return std::max(1, std::min(rows, per_sm * num_sms()));
+}
 
-template <int PRO, int EPI, bool XREG>
+template <int PRO, int EPI>
 static cudaError_t launch_one(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
     const size_t smem = gemv_smem_bytes(p);
-    auto kern = k_gemv<PRO, EPI, XREG>;
+    auto kern = k_gemv<PRO, EPI>;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 120 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -348,23 +304,14 @@ static cudaError_t launch_one(const GemvParams& p, int grid, cudaStream_t s, boo
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int PRO, int EPI>
-static cudaError_t launch_x(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-    const int seg_len = p.in_dim < kSeg ? p.in_dim : kSeg;
-    const bool xreg = (p.x_len == kSeg) && (seg_len == kSeg);
-    return xreg ? launch_one<PRO, EPI, true>(p, grid, s, pdl) : launch_one<PRO, EPI, false>(p, grid, s, pdl);
-}
-
 cudaError_t launch_gemv(int pro, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl) {
-    if (p.in_dim <= 0 || p.in_dim % 8 != 0 || p.rows <= 0) return cudaErrorInvalidValue;
+    if (p.in_dim <= 0 || p.in_dim % 8 != 0 || p.rows <= 0 || p.x_len <= 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(p.W) & 15) != 0) return cudaErrorInvalidValue;
-    // ring depth: keep the CTA under ~112 KB so two GEMV CTAs fit one SM (PDL overlap)
-    const size_t xs_bytes = (size_t)p.x_len * 4;
-    int slots = (int)((112 * 1024 - 1024 - (long)xs_bytes) / (kCW * kSeg * 2));
-    p.slots_per_warp = std::max(2, std::min(kMaxSlots, slots));
-    if (gemv_smem_bytes(p) > 120 * 1024) return cudaErrorInvalidValue;
+    if (epi == EPI_SWIGLU ? (p.in_dim != 2 * p.x_len || p.x_len % 8) : (p.in_dim != p.x_len))
+        return cudaErrorInvalidValue;
+    if (gemv_smem_bytes(p) > 96 * 1024) return cudaErrorInvalidValue;
 #define QWC_GEMV_CASE(PR, EP) \
-    if (pro == PR && epi == EP) return launch_x<PR, EP>(p, grid, s, pdl);
+    if (pro == PR && epi == EP) return launch_one<PR, EP>(p, grid, s, pdl);
     QWC_GEMV_CASE(PRO_PLAIN, EPI_STORE)
     QWC_GEMV_CASE(PRO_PLAIN, EPI_RESIDUAL)
     QWC_GEMV_CASE(PRO_RMSNORM, EPI_STORE)

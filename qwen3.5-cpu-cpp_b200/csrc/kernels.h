@@ -57,7 +57,7 @@ struct GemvParams {
 
 size_t gemv_smem_bytes(const GemvParams& p);
 cudaError_t launch_gemv(int pro, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl);
-int gemv_grid(int rows);
+int gemv_grid(int rows, int per_sm = 1);
 
 // ------------------------------------------------------------------ GDN decode
 // One token of the Gated DeltaNet mixer core (qwen_model.cpp:173-207): causal conv over
@@ -88,7 +88,7 @@ struct AttnDecodeParams {
     const float* gate_in = nullptr; // op mode: gate [NQ][HD]
     const float* qn1 = nullptr;     // (1+w) q_norm [HD]
     const float* kn1 = nullptr;     // (1+w) k_norm [HD]
-    const double* inv_freq = nullptr;  // [rot/2] theta^(-2i/rot)
+    const float* rope_cs = nullptr;   // [max_ctx][rot/2][2] (cos, sin) of pos * theta^(-2i/rot)
     void* k_cache = nullptr;        // [NKV][max_ctx][HD]
     void* v_cache = nullptr;
     int kv_bf16 = 0;
@@ -104,6 +104,32 @@ struct AttnDecodeParams {
 };
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t s, bool pdl);
 int attn_nsplit_for(int max_ctx);
+
+// ------------------------------------------------------------------ persistent step
+// One launch = one decode step: a list of phases run by a cooperative grid of one CTA
+// per SM with grid-wide barriers between them (decode_step.cu).
+enum PhaseType : int { PH_GEMV = 0, PH_GDN = 1, PH_ATTN = 2 };
+struct alignas(16) StepPhase {
+    int type = PH_GEMV, pro = 0, epi = 0, pad = 0;
+    GemvParams g;
+    GdnDecodeParams d;
+    AttnDecodeParams a;
+};
+struct StepParams {
+    const StepPhase* phases = nullptr;  // device array
+    int nphases = 0;
+    unsigned long long* bar = nullptr;  // arrival counter, zero between steps
+    unsigned* done = nullptr;           // end-of-step ticket, zero between steps
+    int* dev_err = nullptr;
+    int nslot = 4;                      // ring slots per warp (4 KB each)
+    int xs_max = 0;                     // largest GEMV x length (floats)
+    long long* trace = nullptr;         // optional [grid][nphases][8] globaltimer stamps / counters
+};
+static_assert(sizeof(StepPhase) % 16 == 0, "staged as int4");
+int step_slots(int xs_max, int grp, int nphases);
+size_t step_smem_bytes(int nslot, int xs_max, int nphases);
+int decode_step_max_grid(int grp, int nslot, int xs_max, int nphases);  // 0: not co-resident
+cudaError_t launch_decode_step(const StepParams& sp, int grp, int grid, cudaStream_t s);
 
 int num_sms();
 

@@ -12,8 +12,10 @@ reference processes its prompt one token at a time).
              token) are far larger than the 126 MB L2, so no flush is needed.
   e2e        the same through the C ABI call qwc_generate_greedy with host buffers:
              prompt H2D, reset, 160 graph replays, token ids D2H, all in the timed region.
-  roofline   the dominant kernel class of the step, timed live per launch (eager step,
-             CUDA events) against MEASURED_PEAKS.json's HBM copy bandwidth.
+  roofline   the dominant kernel: the persistent decode-step kernel (one launch = one
+             token), timed live per launch with CUDA events against MEASURED_PEAKS.json's
+             HBM copy bandwidth; `traffic` is the DRAM bytes per launch from the ncu
+             capture summarised in profiles/ (null when no summary is present).
   cpu_baseline  the reference engine itself (oracle/_ref: its own sources, built here)
              on this host's cores, one full generation.
 
@@ -34,6 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_PROMPT, N_NEW = 32, 128
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "k_decode_step_qwen35_0.8b.md")
 SHAPE = "qwen3.5-0.8b-shaped"
 METRIC = "decode tok/s"
 UNIT = "tok/s"
@@ -147,6 +150,41 @@ class ClockSampler:
                 "power_w_max": max(power) if power else None}
 
 
+_JSON_FD = None
+
+
+def emit(line):
+    """The one JSON line goes to the original stdout; everything else (the engine's
+    load-time messages, library output) was redirected to stderr."""
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(line) + "\n").encode())
+
+
+def ncu_traffic():
+    """DRAM bytes per launch of k_decode_step from the committed ncu summary."""
+    try:
+        with open(TRAFFIC_FILE) as f:
+            for ln in f:
+                if ln.startswith("traffic_bytes_per_launch:"):
+                    return int(ln.split(":", 1)[1].strip())
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def phase_shares(m):
+    """Share of the persistent step spent in each phase kind (device timestamps)."""
+    import numpy as np
+    kinds, st = m.trace_step()
+    t0 = st[:, 0, 0].min()
+    end = (st[:, :, 3] - t0).max(0)
+    dur = np.diff(np.concatenate([[0], end]))
+    tot = float(dur.sum())
+    out = {}
+    for k, d in zip(kinds, dur):
+        out[k] = out.get(k, 0.0) + float(d) / tot
+    return {k: round(v, 4) for k, v in out.items()}, round(tot / 1e3, 2)
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -211,7 +249,7 @@ def run_reference(args):
                              "sample": f"{args.steps} x generate_greedy({N_PROMPT} prompt + {n_new} new)"},
             "e2e": {"value": round(val, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -297,12 +335,14 @@ def run_ours(args):
            "h2d_bytes_per_step": N_PROMPT * 4, "d2h_bytes_per_step": N_NEW * 4 + 4,
            "wall_clock_value": round(WORLD * args.steps * n_tok / wall, 2)}
 
-    # ---- live per-kernel timing of eager steps -> roofline of the dominant kernel class
+    # ---- live per-launch timing of eager steps -> roofline of the dominant kernel
     m.generate_greedy(prompt, 8)  # position 40, mid-workload context
     prof = []
     for _ in range(4):
         prof += m.profile_step()
     launches_per_step = len(prof) // 4
+    persistent = any(k == "decode_step" for k, _, _ in prof)
+    shares, traced_us = phase_shares(m) if persistent else (None, None)
     by_kind = {}
     for k, ms, b in prof:
         e = by_kind.setdefault(k, [0.0, 0, 0])
@@ -327,9 +367,12 @@ def run_ours(args):
             "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args),
-            "roofline": {"bound": "hbm", "kernel": f"k_gemv ({dom})", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm",
+                         "kernel": "k_decode_step (whole step)" if dom == "decode_step" else f"k_gemv ({dom})",
+                         "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_source": peak_src, "traffic": None,
+                         "peak_source": peak_src,
+                         "traffic": ncu_traffic() if dom == "decode_step" else None,
                          "bytes_per_launch": int(dbytes / dn), "avg_launch_ms": round(dms / dn, 5),
                          "timing": "eager launches, CUDA events per launch"},
             "step_roofline": {"bytes_per_token": int(step_bytes / n_tok),
@@ -337,6 +380,7 @@ def run_ours(args):
                               "frac": round(step_gbs / peak, 4), "peak_source": peak_src},
             "kernel_share": share, "kernel_gbs": kernel_gbs,
             "eager_step_ms": round(tot_ms / 4, 4),
+            "phase_share": shares, "traced_step_us": traced_us,
             "e2e": e2e, "gpu_launches": int(args.steps * n_tok * launches_per_step),
             "clocks": clk}
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
@@ -345,7 +389,7 @@ def run_ours(args):
         line["cpu_baseline"] = cb
     m.close()
     if RANK == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -353,6 +397,10 @@ def run_ours(args):
 
 
 def main():
+    global _JSON_FD
+    _JSON_FD = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

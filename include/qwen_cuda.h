@@ -184,9 +184,12 @@ int qwc_enqueue_greedy(qwc_handle* h, int n_prompt, int n_new);
 int qwc_read_tokens(qwc_handle* h, int start, int n, int* out);
 
 /* Runs ONE decode step eagerly (no graph, no programmatic launch) at the current
- * position with the token id already at that position, timing every kernel with CUDA
- * events. For each launch i < cap: kind[i] (QWC_K_*), ms[i], bytes[i] (algorithmic HBM
- * bytes of that launch). Returns the number of launches (>= 0) or an error code. */
+ * position with the token id already at that position, on the path qwc_step uses,
+ * timing every kernel with CUDA events. For each launch i < cap: kind[i] (QWC_K_*),
+ * ms[i], bytes[i] (algorithmic HBM bytes of that launch). With the persistent decode
+ * kernel in use that is a single launch of kind QWC_K_DECODE_STEP; with
+ * QWC_DECODE=kernels it is one launch per GEMV / mixer kernel. Returns the number of
+ * launches (>= 0) or an error code. */
 #define QWC_K_MIX_IN 0      /* norm + mixer input projection GEMV */
 #define QWC_K_GDN 1         /* GDN conv + delta-rule recurrence */
 #define QWC_K_ATTN 2        /* attention (norm/rope/append + split-K) */
@@ -194,6 +197,7 @@ int qwc_read_tokens(qwc_handle* h, int start, int n, int* out);
 #define QWC_K_GATE_UP 4     /* norm + gate/up GEMV + SwiGLU */
 #define QWC_K_DOWN 5        /* down GEMV + residual */
 #define QWC_K_LM_HEAD 6     /* final norm + lm_head GEMV + argmax */
+#define QWC_K_DECODE_STEP 7 /* the persistent kernel: the whole step in one launch */
 int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* bytes);
 
 /* Runs ONE step of the persistent decode kernel (the one the CUDA graph replays) eagerly

@@ -30,7 +30,7 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_gemv_bf16",
            "qwc_gdn_decode_step", "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
-                6: "lm_head"}
+                6: "lm_head", 7: "decode_step"}
 
 
 class qwc_config(C.Structure):

@@ -97,6 +97,7 @@ struct qwc_handle {
     StepPhase* step_phases = nullptr;  // device array
     int step_grid = 0;
     std::vector<int> step_kinds;  // QWC_K_* of each phase
+    std::vector<StepPhase> step_host;  // host copy of the phases (algorithmic bytes)
     unsigned long long* step_bar = nullptr;
     unsigned* step_done = nullptr;
 
@@ -680,6 +681,7 @@ static int setup_persistent(qwc_handle* h) {
     if (grid <= 0) return QWC_OK;
     CU(cudaMalloc(&h->step_phases, phases.size() * sizeof(StepPhase)));
     CU(cudaMemcpy(h->step_phases, phases.data(), phases.size() * sizeof(StepPhase), cudaMemcpyHostToDevice));
+    h->step_host = phases;
     h->step.phases = h->step_phases;
     h->step.nphases = (int)phases.size();
     h->step.bar = h->step_bar;
@@ -1079,7 +1081,22 @@ extern "C" int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, in
     int rc = QWC_OK;
     if (cudaMemcpyAsync(h->n_prompt, &h->h_pin[6], sizeof(int), cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
         rc = fail(h, QWC_E_CUDA, "qwc_profile_step: copy failed");
-    if (rc == QWC_OK) rc = enqueue_step(h, h->st, false, &prof, h->pos_host);
+    if (rc == QWC_OK && h->step_grid > 0) {
+        // the persistent kernel: one launch, the whole step
+        int64_t b = 0;
+        for (const StepPhase& ph : h->step_host) b += phase_bytes(h, ph, h->pos_host);
+        if (cudaEventRecord(prof.ev[0], h->stream) != cudaSuccess ||
+            launch_decode_step(h->step, h->NQ / h->NKV, h->step_grid, h->stream) != cudaSuccess ||
+            (cap > 0 && cudaEventRecord(prof.ev[1], h->stream) != cudaSuccess))
+            rc = fail(h, QWC_E_CUDA, "qwc_profile_step: launch failed");
+        if (cap > 0) {
+            prof.kind[0] = QWC_K_DECODE_STEP;
+            prof.bytes[0] = b;
+        }
+        prof.n = 1;
+    } else if (rc == QWC_OK) {
+        rc = enqueue_step(h, h->st, false, &prof, h->pos_host);
+    }
     if (rc == QWC_OK) rc = check_device_error(h);
     int n = std::min(prof.n, cap);
     for (int i = 0; i < n && rc == QWC_OK; ++i) {

@@ -82,3 +82,27 @@ def test_errors_are_reported(pkg):
         m.generate_greedy([1, 2, 3], 2)
     assert e.value.code == -5
     m.close()
+
+
+def test_measurement_entry_points(pkg, oracle):
+    """qwc_profile_step / qwc_trace_step run a real step on the production path: the
+    position advances and the following step still matches the oracle."""
+    d = model_dir(pkg, "small-0.8b-widths")
+    s = pkg.synth.SHAPES["small-0.8b-widths"]
+    prompt = pkg.synth.random_prompt(s.vocab_size, 6, seed=3)
+    m = pkg.abi.Model(d, max_context=64)
+    m.generate_greedy(prompt, 2)
+    pos = m.position()
+    prof = m.profile_step()
+    assert len(prof) >= 1 and all(ms > 0 and b > 0 for _, ms, b in prof)
+    kinds = {k for k, _, _ in prof}
+    assert kinds == {"decode_step"} or "lm_head" in kinds
+    assert m.position() == pos + 1
+    if kinds == {"decode_step"}:
+        tk, st = m.trace_step()
+        assert st.shape[1] == len(tk) and st.shape[2] == 8
+        assert tk[-1] == "lm_head"
+        # stamps are ordered within every CTA and phase: start <= barrier <= end
+        assert (st[:, :, 1] >= st[:, :, 0]).all() and (st[:, :, 3] >= st[:, :, 1]).all()
+        assert m.position() == pos + 2
+    m.close()

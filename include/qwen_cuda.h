@@ -220,6 +220,15 @@ int qwc_trace_step(qwc_handle* h, int cap, int64_t* out);
 int qwc_gemv_bf16(const uint16_t* W, const float* x, float* y, int out_dim, int in_dim,
                   void* stream);
 
+/* The projections of QwenForward::prefill (src/qwen_forward.cpp:154-206, each row a
+ * matmul of src/forward_pass.cpp:65-75) for N tokens at once on the tensor cores:
+ * Y[N][M] (=, or += when accumulate) sum_k X[n][k] W[m][k], W bf16 [M][K] row-major,
+ * X given as bf16 pairs Xs[N][2K] with Xs[n][k] = bf16(x), Xs[n][K+k] = bf16(x - that)
+ * so that hi + lo carries x to ~2^-17 relative; fp32 accumulation. K must be a multiple
+ * of 64; W and Xs 16-byte aligned. Device pointers; asynchronous on `stream`. */
+int qwc_gemm_bf16(const uint16_t* W, const uint16_t* Xs, float* Y, int M, int N, int K, int accumulate,
+                  void* stream);
+
 /* The decode GDN mixer core of gdn_step (src/qwen_model.cpp:173-207) for one token on
  * device memory, as used by step(): conv over the rolling state, SiLU, l2norm(q,k),
  * gates, delta-rule update of S and o = S^T q (before the gated norm).

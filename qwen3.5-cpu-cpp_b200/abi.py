@@ -27,7 +27,7 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_get_config", "qwc_reset", "qwc_position", "qwc_step", "qwc_generate_greedy",
            "qwc_forward_logits", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
-           "qwc_gemv_bf16",
+           "qwc_gemv_bf16", "qwc_gemm_bf16",
            "qwc_gdn_decode_step", "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
                 6: "lm_head", 7: "decode_step"}
@@ -249,6 +249,13 @@ class Model:
 
 def gemv_bf16(W_ptr, x_ptr, y_ptr, out_dim, in_dim, stream=0):
     check(lib().qwc_gemv_bf16(W_ptr, x_ptr, y_ptr, out_dim, in_dim, stream))
+
+
+def gemm_bf16(W_ptr, Xs_ptr, Y_ptr, M, N, K, accumulate=False, stream=0):
+    """qwc_gemm_bf16: Y[N][M] (+)= X W^T on the tensor cores, X as hi/lo bf16 [N][2K]."""
+    fn = lib().qwc_gemm_bf16
+    fn.argtypes = [C.c_void_p] * 3 + [C.c_int] * 4 + [C.c_void_p]
+    check(fn(W_ptr, Xs_ptr, Y_ptr, M, N, K, int(bool(accumulate)), stream))
 
 
 def gdn_decode_step(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state, out, KH, VH,

@@ -18,6 +18,10 @@ enum DevError : int {
     DEV_BAD_POS = 5,              // position beyond the KV cache
     DEV_PREFILL_TIMEOUT = 6,
     DEV_STEP_BARRIER_TIMEOUT = 7, // a persistent-step CTA waited too long for the grid
+    DEV_TC_PRODUCER_TIMEOUT = 8,  // tensor-core GEMM: TMA producer waited for a free stage
+    DEV_TC_MMA_TIMEOUT = 9,       // tensor-core GEMM: MMA issuer waited for operands
+    DEV_TC_EPI_TIMEOUT = 10,      // tensor-core GEMM: epilogue waited for an accumulator
+    DEV_TC_DRAIN_TIMEOUT = 11,    // tensor-core GEMM: in-flight copies / MMAs at exit
 };
 
 __device__ __forceinline__ void post_error(int* flag, int code) {

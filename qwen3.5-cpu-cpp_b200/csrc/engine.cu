@@ -101,6 +101,19 @@ struct qwc_handle {
     unsigned long long* step_bar = nullptr;
     unsigned* step_done = nullptr;
 
+    // batched forward pass (prefill): weight tensor maps (built on first use) and a
+    // workspace for chunks of up to pf_cap tokens
+    bool pf_maps_ready = false;
+    std::vector<CUtensorMap> pf_map_in, pf_map_out, pf_map_gu, pf_map_down;
+    CUtensorMap pf_map_head{};
+    uint8_t* pf_ws = nullptr;
+    int pf_cap = 0;
+    long pf_ldp = 0, pf_lda = 0, pf_ldb = 0;
+    int* pf_ids = nullptr;
+    float *pf_hid = nullptr, *pf_proj = nullptr, *pf_o = nullptr, *pf_qn = nullptr, *pf_kn = nullptr,
+          *pf_vc = nullptr, *pf_decay = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
+    uint16_t *pf_xa = nullptr, *pf_xb = nullptr;
+
     cudaGraphExec_t graph = nullptr;
     bool use_graph = true, use_pdl = true;
     int pos_host = 0;
@@ -725,6 +738,7 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     cudaFree(h->st.kv);
     cudaFree(h->scratch);
     cudaFree(h->step_phases);
+    cudaFree(h->pf_ws);
     if (h->h_pin) cudaFreeHost(h->h_pin);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
@@ -952,6 +966,205 @@ extern "C" int qwc_get_config(const qwc_handle* h, qwc_config* out) {
 // ------------------------------------------------------------------ prefill (stepping)
 // First implementation: the prompt goes through the decode step one token at a time,
 // exactly as the reference's generate_greedy feeds it (src/qwen_model.cpp:245).
+// ------------------------------------------------------------------ batched forward pass
+// QwenForward::prefill (src/qwen_forward.cpp:154-206) as whole-chunk GEMMs on the tensor
+// cores plus token-parallel kernels (prefill.cu, tc_gemm.cu), continuing from and updating
+// a decode state, so the same code serves the stateless forward pass (fresh state) and
+// the prefill that seeds decoding.
+constexpr int kPfChunk = 4096;     // tokens per chunk (bounds the workspace)
+constexpr int kPfLogitRows = 128;  // lm_head rows per GEMM when every position's logits are wanted
+
+static int pf_build_maps(qwc_handle* h) {
+    if (h->pf_maps_ready) return QWC_OK;
+    const int L = h->L;
+    h->pf_map_in.resize(L);
+    h->pf_map_out.resize(L);
+    h->pf_map_gu.resize(L);
+    h->pf_map_down.resize(L);
+    for (int l = 0; l < L; ++l) {
+        const Layer& lw = h->layers[l];
+        if (tc_make_map(&h->pf_map_in[l], lw.w_in, lw.in_rows, h->H, h->H) ||
+            tc_make_map(&h->pf_map_out[l], lw.w_out, h->H, lw.out_in, lw.out_in) ||
+            // [I][2H] rows [gate_i | up_i] read as [2I][H]: rows alternate gate_i, up_i
+            tc_make_map(&h->pf_map_gu[l], lw.w_gu, 2L * h->I, h->H, h->H) ||
+            tc_make_map(&h->pf_map_down[l], lw.w_down, h->H, h->I, h->I))
+            return fail(h, QWC_E_CUDA, "prefill: tensor map creation failed");
+    }
+    if (tc_make_map(&h->pf_map_head, h->head, h->V, h->H, h->H))
+        return fail(h, QWC_E_CUDA, "prefill: tensor map creation failed");
+    h->pf_maps_ready = true;
+    return QWC_OK;
+}
+
+static int pf_workspace(qwc_handle* h, int cap) {
+    if (h->pf_cap >= cap) return QWC_OK;
+    cudaFree(h->pf_ws);
+    h->pf_ws = nullptr;
+    h->pf_cap = 0;
+    int ldp = 0;
+    for (const Layer& lw : h->layers) ldp = std::max(ldp, lw.in_rows);
+    h->pf_ldp = (ldp + 63) / 64 * 64;
+    const long ka = std::max({h->H, h->VD, h->NQ * h->HD});
+    h->pf_lda = 2 * ka;
+    h->pf_ldb = 2L * h->I;
+    size_t off = 0;
+    auto carve = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 255) / 256 * 256;
+        return o;
+    };
+    const size_t c = (size_t)cap;
+    const size_t o_ids = carve(c * 4), o_hid = carve(c * h->H * 4), o_proj = carve(c * h->pf_ldp * 4),
+                 o_o = carve(c * h->VD * 4), o_qn = carve(c * h->KD * 4), o_kn = carve(c * h->KD * 4),
+                 o_vc = carve(c * h->VD * 4), o_dec = carve(c * h->VH * 4), o_beta = carve(c * h->VH * 4),
+                 o_qbuf = carve(c * h->NQ * h->HD * 4), o_log = carve((size_t)kPfLogitRows * h->V * 4),
+                 o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2);
+    if (cudaMalloc(&h->pf_ws, off) != cudaSuccess) {
+        h->pf_ws = nullptr;
+        return fail(h, QWC_E_OOM, "prefill workspace allocation failed");
+    }
+    uint8_t* b = h->pf_ws;
+    h->pf_ids = reinterpret_cast<int*>(b + o_ids);
+    h->pf_hid = reinterpret_cast<float*>(b + o_hid);
+    h->pf_proj = reinterpret_cast<float*>(b + o_proj);
+    h->pf_o = reinterpret_cast<float*>(b + o_o);
+    h->pf_qn = reinterpret_cast<float*>(b + o_qn);
+    h->pf_kn = reinterpret_cast<float*>(b + o_kn);
+    h->pf_vc = reinterpret_cast<float*>(b + o_vc);
+    h->pf_decay = reinterpret_cast<float*>(b + o_dec);
+    h->pf_beta = reinterpret_cast<float*>(b + o_beta);
+    h->pf_qbuf = reinterpret_cast<float*>(b + o_qbuf);
+    h->pf_logits = reinterpret_cast<float*>(b + o_log);
+    h->pf_xa = reinterpret_cast<uint16_t*>(b + o_xa);
+    h->pf_xb = reinterpret_cast<uint16_t*>(b + o_xb);
+    h->pf_cap = cap;
+    return QWC_OK;
+}
+
+static int pf_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t* xs, long ldxs, int M, int N, int K,
+                   TcGemmParams p) {
+    CUtensorMap mx;
+    if (tc_make_map(&mx, xs, N, 2L * K, ldxs)) return fail(h, QWC_E_CUDA, "prefill: activation tensor map failed");
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.err = h->dev_err;
+    CU(launch_tc_gemm(mw, mx, p, h->stream));
+    return QWC_OK;
+}
+
+// Forward pass of ids[0..T) at positions p0.. on state sv. Logits: every position's
+// rows into logits_host[T][V] (all), only the last position's into logits_host[V]
+// (!all), or none (logits_host == nullptr).
+static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int p0, float* logits_host, bool all) {
+    if (h->H % 64 || h->I % 64 || h->VD % 64 || (h->NQ * h->HD) % 64)
+        return fail(h, QWC_E_SHAPE, "batched prefill needs hidden, intermediate, GDN value and attention widths that are multiples of 64");
+    int rc = pf_build_maps(h);
+    if (rc) return rc;
+    rc = pf_workspace(h, std::min(T, kPfChunk));
+    if (rc) return rc;
+    const int H = h->H;
+    const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
+    for (int c0 = 0; c0 < T; c0 += kPfChunk) {
+        const int Tc = std::min(kPfChunk, T - c0), pc = p0 + c0;
+        CU(cudaMemcpyAsync(h->pf_ids, ids + c0, (size_t)Tc * 4, cudaMemcpyHostToDevice, h->stream));
+        CU(pf_embed(h->pf_ids, Tc, h->embed, H, h->V, h->pf_hid, h->dev_err, h->stream));
+        for (int l = 0; l < h->L; ++l) {
+            const Layer& lw = h->layers[l];
+            CU(pf_rmsnorm_split(h->pf_hid, H, Tc, lw.in_ln1, H, h->eps, h->pf_xa, h->pf_lda, h->stream));
+            TcGemmParams gi;
+            gi.epi = TC_STORE;
+            gi.y = h->pf_proj;
+            gi.ldy = h->pf_ldp;
+            if ((rc = pf_gemm(h, h->pf_map_in[l], h->pf_xa, h->pf_lda, lw.in_rows, Tc, H, gi))) return rc;
+            if (lw.is_attn) {
+                uint8_t* kvl = static_cast<uint8_t*>(sv.kv) + kv_layer * lw.idx;
+                PfAttnArgs a;
+                a.proj = h->pf_proj;
+                a.ldp = h->pf_ldp;
+                a.qn1 = lw.qn1;
+                a.kn1 = lw.kn1;
+                a.rope_cs = h->rope_cs;
+                a.qbuf = h->pf_qbuf;
+                a.k_cache = kvl;
+                a.v_cache = kvl + kv_layer / 2;
+                a.kv_bf16 = h->kv_dtype == QWC_DTYPE_BF16;
+                a.max_ctx = sv.max_ctx;
+                a.p0 = pc;
+                a.T = Tc;
+                a.NQ = h->NQ;
+                a.NKV = h->NKV;
+                a.rot = h->ROT;
+                a.eps = h->eps;
+                a.xs = h->pf_xa;
+                a.ldxs = h->pf_lda;
+                CU(pf_attention(a, h->stream));
+            } else {
+                PfGdnArgs g;
+                g.proj = h->pf_proj;
+                g.ldp = h->pf_ldp;
+                g.conv_w = lw.conv_w;
+                g.ring = sv.conv_ring + (size_t)lw.idx * h->C * 4;
+                g.neg_exp_A = lw.neg_exp_A;
+                g.dt_bias = lw.dt_bias;
+                g.qn = h->pf_qn;
+                g.kn = h->pf_kn;
+                g.vc = h->pf_vc;
+                g.decay = h->pf_decay;
+                g.beta = h->pf_beta;
+                g.state = sv.gdn_state + (size_t)lw.idx * h->VH * h->DK * h->DV;
+                g.out = h->pf_o;
+                g.T = Tc;
+                g.p0 = pc;
+                g.KH = h->KH;
+                g.VH = h->VH;
+                g.C = h->C;
+                g.VD = h->VD;
+                CU(pf_gdn(g, h->stream));
+                CU(pf_gated_norm_split(h->pf_o, h->VD, h->pf_proj + h->C, h->pf_ldp, lw.gn_w, Tc, h->VH, h->eps,
+                                       h->pf_xa, h->pf_lda, h->stream));
+            }
+            TcGemmParams go;
+            go.epi = TC_RESIDUAL;
+            go.y = h->pf_hid;
+            go.ldy = H;
+            if ((rc = pf_gemm(h, h->pf_map_out[l], h->pf_xa, h->pf_lda, H, Tc, lw.out_in, go))) return rc;
+            // FFN: post-attention norm, gate/up + SwiGLU (written as hi/lo for down), down + residual
+            CU(pf_rmsnorm_split(h->pf_hid, H, Tc, lw.post_ln1, H, h->eps, h->pf_xa, h->pf_lda, h->stream));
+            TcGemmParams gu;
+            gu.epi = TC_SWIGLU_SPLIT;
+            gu.ys = h->pf_xb;
+            gu.ldys = h->pf_ldb;
+            gu.split_k = h->I;
+            if ((rc = pf_gemm(h, h->pf_map_gu[l], h->pf_xa, h->pf_lda, 2 * h->I, Tc, H, gu))) return rc;
+            TcGemmParams gd;
+            gd.epi = TC_RESIDUAL;
+            gd.y = h->pf_hid;
+            gd.ldy = H;
+            if ((rc = pf_gemm(h, h->pf_map_down[l], h->pf_xb, h->pf_ldb, H, Tc, h->I, gd))) return rc;
+        }
+        // final norm + lm_head for the rows whose logits are wanted
+        if (!logits_host) continue;
+        const bool last_chunk = c0 + Tc == T;
+        if (!all && !last_chunk) continue;
+        const int r0 = all ? 0 : Tc - 1, nrows = all ? Tc : 1;
+        for (int g0 = 0; g0 < nrows; g0 += kPfLogitRows) {
+            const int gn = std::min(kPfLogitRows, nrows - g0);
+            CU(pf_rmsnorm_split(h->pf_hid + (size_t)(r0 + g0) * H, H, gn, h->final_ln1, H, h->eps, h->pf_xa,
+                                h->pf_lda, h->stream));
+            TcGemmParams gl;
+            gl.epi = TC_STORE;
+            gl.y = h->pf_logits;
+            gl.ldy = h->V;
+            if ((rc = pf_gemm(h, h->pf_map_head, h->pf_xa, h->pf_lda, h->V, gn, H, gl))) return rc;
+            float* dst = logits_host + (all ? (size_t)(c0 + g0) * h->V : 0);
+            CU(cudaMemcpyAsync(dst, h->pf_logits, (size_t)gn * h->V * 4, cudaMemcpyDeviceToHost, h->stream));
+        }
+    }
+    CU(cudaStreamSynchronize(h->stream));
+    return check_device_error(h);
+}
+
 extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out) {
     if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_prefill: null handle");
     if (T <= 0 || !ids) return fail(h, QWC_E_INVALID, "qwc_prefill: empty prompt");
@@ -960,16 +1173,14 @@ extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_o
         if (ids[i] < 0 || ids[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_prefill: token id out of range");
     int rc = qwc_reset(h);
     if (rc) return rc;
+    // the batched pass fills the KV cache, GDN state and conv ring for positions 0..T-1;
+    // decoding continues at position T
     CU(cudaMemcpyAsync(h->tokens, ids, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
-    h->h_pin[4] = h->max_ctx;
-    CU(cudaMemcpyAsync(h->n_prompt, &h->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, h->stream));
-    for (int i = 0; i < T; ++i) {
-        rc = run_step(h);
-        if (rc) return rc;
-    }
-    if (logits_out) CU(cudaMemcpyAsync(logits_out, h->logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost, h->stream));
-    rc = check_device_error(h);
+    rc = pf_run(h, h->st, ids, T, 0, logits_out, false);
     if (rc) return rc;
+    h->h_pin[4] = T;
+    CU(cudaMemcpyAsync(h->pos, &h->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    CU(cudaStreamSynchronize(h->stream));
     h->pos_host = T;
     return QWC_OK;
 }
@@ -981,48 +1192,20 @@ extern "C" int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* l
     if (T <= 0 || !ids || !logits_out) return fail(h, QWC_E_INVALID, "qwc_forward_logits: invalid argument");
     for (int i = 0; i < T; ++i)
         if (ids[i] < 0 || ids[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_forward_logits: token id out of range");
+    if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_forward_logits: T exceeds max_context");
     CU(cudaSetDevice(h->device));
     StateView tv;
     tv.max_ctx = T;
     const size_t gb = h->gdn_bytes, cb = h->conv_bytes;
     const size_t kb = (size_t)h->n_attn * 2 * h->NKV * (size_t)T * h->HD * h->kv_bytes;
-    if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_forward_logits: T exceeds max_context");
     if (gb && cudaMalloc(&tv.gdn_state, gb) != cudaSuccess) return fail(h, QWC_E_OOM, "forward state allocation failed");
     if (cb && cudaMalloc(&tv.conv_ring, cb) != cudaSuccess) { cudaFree(tv.gdn_state); return fail(h, QWC_E_OOM, "forward state allocation failed"); }
     if (kb && cudaMalloc(&tv.kv, kb) != cudaSuccess) { cudaFree(tv.gdn_state); cudaFree(tv.conv_ring); return fail(h, QWC_E_OOM, "forward state allocation failed"); }
     int rc = QWC_OK;
-    // the handle's token buffer and position are borrowed and restored afterwards
-    do {
-        if (gb && cudaMemsetAsync(tv.gdn_state, 0, gb, h->stream) != cudaSuccess) { rc = fail(h, QWC_E_CUDA, "memset"); break; }
-        if (cb && cudaMemsetAsync(tv.conv_ring, 0, cb, h->stream) != cudaSuccess) { rc = fail(h, QWC_E_CUDA, "memset"); break; }
-        std::vector<int> saved_tokens((size_t)h->max_ctx + 1);
-        cudaMemcpyAsync(saved_tokens.data(), h->tokens, saved_tokens.size() * 4, cudaMemcpyDeviceToHost, h->stream);
-        cudaMemcpyAsync(&h->h_pin[10], h->pos, sizeof(int), cudaMemcpyDeviceToHost, h->stream);
-        cudaMemcpyAsync(&h->h_pin[11], h->n_prompt, sizeof(int), cudaMemcpyDeviceToHost, h->stream);
-        cudaStreamSynchronize(h->stream);
-        const int saved_pos = h->h_pin[10], saved_np = h->h_pin[11];
-        cudaMemcpyAsync(h->tokens, ids, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream);
-        h->h_pin[12] = 0;
-        h->h_pin[13] = h->max_ctx;
-        cudaMemcpyAsync(h->pos, &h->h_pin[12], sizeof(int), cudaMemcpyHostToDevice, h->stream);
-        cudaMemcpyAsync(h->n_prompt, &h->h_pin[13], sizeof(int), cudaMemcpyHostToDevice, h->stream);
-        for (int t = 0; t < T && rc == QWC_OK; ++t) {
-            rc = enqueue_step(h, tv, h->use_pdl);
-            if (rc) break;
-            if (!last_only || t == T - 1) {
-                float* dst = logits_out + (last_only ? 0 : (size_t)t * h->V);
-                if (cudaMemcpyAsync(dst, h->logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess)
-                    rc = fail(h, QWC_E_CUDA, "logits copy failed");
-            }
-        }
-        cudaMemcpyAsync(h->tokens, saved_tokens.data(), saved_tokens.size() * 4, cudaMemcpyHostToDevice, h->stream);
-        h->h_pin[10] = saved_pos;
-        h->h_pin[11] = saved_np;
-        cudaMemcpyAsync(h->pos, &h->h_pin[10], sizeof(int), cudaMemcpyHostToDevice, h->stream);
-        cudaMemcpyAsync(h->n_prompt, &h->h_pin[11], sizeof(int), cudaMemcpyHostToDevice, h->stream);
-        int rc2 = check_device_error(h);
-        if (rc == QWC_OK) rc = rc2;
-    } while (0);
+    if ((gb && cudaMemsetAsync(tv.gdn_state, 0, gb, h->stream) != cudaSuccess) ||
+        (cb && cudaMemsetAsync(tv.conv_ring, 0, cb, h->stream) != cudaSuccess))
+        rc = fail(h, QWC_E_CUDA, "forward state clear failed");
+    if (rc == QWC_OK) rc = pf_run(h, tv, ids, T, 0, logits_out, !last_only);
     cudaStreamSynchronize(h->stream);
     cudaFree(tv.gdn_state);
     cudaFree(tv.conv_ring);
@@ -1165,6 +1348,26 @@ extern "C" int qwc_gemv_bf16(const uint16_t* W, const float* x, float* y, int ou
     p.dev_err = kernel_api_err();
     cudaError_t e = launch_gemv(PRO_PLAIN, EPI_STORE, p, gemv_grid(out_dim), (cudaStream_t)stream, false);
     if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gemv_bf16: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+extern "C" int qwc_gemm_bf16(const uint16_t* W, const uint16_t* Xs, float* Y, int M, int N, int K, int accumulate,
+                             void* stream) {
+    if (!W || !Xs || !Y || M <= 0 || N <= 0 || K <= 0 || K % 64)
+        return fail(nullptr, QWC_E_INVALID, "qwc_gemm_bf16: invalid argument");
+    CUtensorMap mw, mx;
+    if (tc_make_map(&mw, W, M, K, K) || tc_make_map(&mx, Xs, N, 2L * K, 2L * K))
+        return fail(nullptr, QWC_E_INVALID, "qwc_gemm_bf16: tensor map creation failed (alignment)");
+    TcGemmParams p;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.epi = accumulate ? TC_RESIDUAL : TC_STORE;
+    p.y = Y;
+    p.ldy = M;
+    p.err = kernel_api_err();
+    cudaError_t e = launch_tc_gemm(mw, mx, p, (cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gemm_bf16: ") + cudaGetErrorString(e));
     return QWC_OK;
 }
 

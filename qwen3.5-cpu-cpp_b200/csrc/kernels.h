@@ -1,6 +1,7 @@
 // Internal launch interface of the sm_100a kernels (not part of the C ABI).
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace qwc {
@@ -132,6 +133,70 @@ int decode_step_max_grid(int grp, int nslot, int xs_max, int nphases);  // 0: no
 cudaError_t launch_decode_step(const StepParams& sp, int grp, int grid, cudaStream_t s);
 
 int num_sms();
+
+// ------------------------------------------------------------------ tensor-core GEMM
+// Batched forward pass (tc_gemm.cu): Y[n][m] (op)= sum_k X[n][k] W[m][k] over N tokens,
+// W bf16 [M][K], X carried as bf16 hi/lo pairs [N][ld] (hi at [0,K), lo at [K,2K)).
+enum TcEpi : int {
+    TC_STORE = 0,        // y[n][m] = acc
+    TC_RESIDUAL = 1,     // y[n][m] += acc
+    TC_SWIGLU_SPLIT = 2, // rows alternate gate_i/up_i: ys[n][i], ys[n][split_k+i] = hi/lo of silu(g)*u
+};
+struct TcGemmParams {
+    int M = 0, N = 0, K = 0;
+    int epi = TC_STORE;
+    float* y = nullptr;
+    long ldy = 0;
+    uint16_t* ys = nullptr;
+    long ldys = 0;
+    int split_k = 0;
+    int* err = nullptr;
+};
+// Tensor map of a row-major bf16 matrix [rows][cols] with row stride ld (elements), in
+// 128 x 64 boxes with the 128-byte swizzle. Returns 0 on success.
+int tc_make_map(CUtensorMap* map, const void* base, long rows, long cols, long ld);
+cudaError_t launch_tc_gemm(const CUtensorMap& mapW, const CUtensorMap& mapX, const TcGemmParams& p, cudaStream_t s);
+
+// ------------------------------------------------------------------ prefill kernels
+// Token-parallel pieces of the batched forward pass over a chunk of T tokens at
+// positions p0.. (prefill.cu). Activation inputs of the GEMMs are written as hi/lo pairs.
+cudaError_t pf_embed(const int* ids, int T, const uint16_t* embed, int H, int V, float* hid, int* err, cudaStream_t s);
+cudaError_t pf_rmsnorm_split(const float* x, long ldx, int rows, const float* w1, int H, float eps, uint16_t* xs,
+                             long ldxs, cudaStream_t s);
+struct PfGdnArgs {
+    const float* proj = nullptr;  // [T][ldp]: qkv C | z VD | b VH | a VH
+    long ldp = 0;
+    const float* conv_w = nullptr;
+    float* ring = nullptr;        // [C][4], read then updated
+    const float* neg_exp_A = nullptr;
+    const float* dt_bias = nullptr;
+    float* qn = nullptr;          // scratch [T][KD]
+    float* kn = nullptr;          // scratch [T][KD]
+    float* vc = nullptr;          // scratch [T][VD]
+    float* decay = nullptr;       // scratch [T][VH]
+    float* beta = nullptr;        // scratch [T][VH]
+    float* state = nullptr;       // [VH][DK][DV], read then updated
+    float* out = nullptr;         // [T][VD]
+    int T = 0, p0 = 0, KH = 0, VH = 0, C = 0, VD = 0;
+};
+cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s);
+cudaError_t pf_gated_norm_split(const float* o, long ldo, const float* z, long ldz, const float* w, int T, int nh,
+                                float eps, uint16_t* xs, long ldxs, cudaStream_t s);
+struct PfAttnArgs {
+    const float* proj = nullptr;  // [T][ldp]: NQ x [q | gate], NKV x k, NKV x v
+    long ldp = 0;
+    const float* qn1 = nullptr;
+    const float* kn1 = nullptr;
+    const float* rope_cs = nullptr;
+    float* qbuf = nullptr;        // scratch [T][NQ][HD]
+    void* k_cache = nullptr;
+    void* v_cache = nullptr;
+    int kv_bf16 = 0, max_ctx = 0, p0 = 0, T = 0, NQ = 0, NKV = 0, rot = 64;
+    float eps = 1e-6f;
+    uint16_t* xs = nullptr;       // output [T][ldxs], K = NQ*HD
+    long ldxs = 0;
+};
+cudaError_t pf_attention(const PfAttnArgs& a, cudaStream_t s);
 
 // Records a handle-less failure message (what qwc_last_error(NULL) returns).
 void set_api_error(const char* msg);

@@ -1,0 +1,305 @@
+// Tensor-core GEMM of the batched forward pass (prefill): for T tokens,
+//   Y[n][m] (op)= sum_k X[n][k] * W[m][k]      n < T tokens, m < M output features
+// with W the bf16 weight matrix [M][K] (row-major, as stored) and X the fp32 activations.
+//
+// Precision: the reference multiplies bf16 weights by fp32 activations in fp32
+// (forward_pass.cpp:44-75). The tensor cores take bf16 x bf16 products, so every
+// activation is carried as an exact-ish pair x = hi + lo of bf16 values (hi = bf16(x),
+// lo = bf16(x - hi); |x - hi - lo| <= 2^-17 |x|). Both halves are multiplied by the same
+// weight tile and accumulated in fp32 in tensor memory, so Y carries ~16 significant
+// bits of every product instead of bf16's 8 -- the error stays well inside the parity
+// tolerance while the FLOPs run on tcgen05. Activations live in HBM as [T][2K] bf16
+// (hi in columns [0, K), lo in [K, 2K)) and are written in that form by the kernels
+// that produce them.
+//
+// Kernel: one CTA per SM, persistent over 128 x 128 output tiles (feature tile outer,
+// token tile inner, so concurrent CTAs share a weight tile through L2).
+//   warp 0 (one lane)  TMA producer: 2-D tiled loads (128-byte swizzle) of the weight
+//                      tile (128 x 64) and the hi / lo activation tiles (128 x 64 each)
+//                      into a 4-stage ring; no multicast.
+//   warp 1             allocates 256 TMEM columns (two fp32 accumulators of 128 x 128);
+//                      one lane issues tcgen05.mma (M=128, N=128, K=16, kind::f16, bf16
+//                      in, fp32 accumulate) from shared-memory descriptors and commits
+//                      each stage back to the producer and each finished tile to the
+//                      epilogue.
+//   warps 2-5          epilogue: tcgen05.ld of their 32 TMEM lanes (= output features),
+//                      store / residual add / SwiGLU + hi-lo split, coalesced across the
+//                      warp (consecutive features of one token).
+// Every wait is bounded: on a timeout the kernel posts an error code and all roles stop.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace qwc {
+
+constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 4, kTThreads = 192;
+constexpr uint32_t kTileABytes = kTM * kTK * 2;  // 16 KB
+constexpr uint32_t kTileBBytes = kTN * kTK * 2;  // 16 KB
+constexpr uint32_t kStageBytes = kTileABytes + 2 * kTileBBytes;
+constexpr int kTmemCols = 2 * kTN;
+constexpr size_t kTcSmem = (size_t)kTStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+// Shared-memory matrix descriptor of a K-major tile with 128-byte rows in the 128-byte
+// swizzle layout that TMA writes: 8-row groups 1024 bytes apart (SBO), leading offset
+// unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B). Tiles are 1024-aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+// Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, M=128, N=128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
+                            ((uint32_t)(kTM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(kIdesc), "r"(accum)
+        : "memory");
+}
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// fp32 -> bf16 bits, round to nearest even (finite inputs)
+__device__ __forceinline__ uint16_t bf16_rne(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// ---------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(kTThreads, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
+              const TcGemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kTStages * kStageBytes);
+    uint64_t* empty = full + kTStages;
+    uint64_t* acc_full = empty + kTStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntm = (p.M + kTM - 1) / kTM, ntn = (p.N + kTN - 1) / kTN, ntiles = ntm * ntn;
+    const int nkb = p.K / kTK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(mma_done, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto aborted = [&]() { return *reinterpret_cast<volatile int*>(s_abort) != 0; };
+    auto abort_with = [&](int code) {
+        post_error(p.err, code);
+        *reinterpret_cast<volatile int*>(s_abort) = 1;
+    };
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer
+        long kc = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !aborted(); tile += gridDim.x) {
+            const int m0 = (tile / ntn) * kTM, n0 = (tile % ntn) * kTN;
+            for (int kb = 0; kb < nkb; ++kb, ++kc) {
+                const int s = (int)(kc % kTStages);
+                const uint32_t ph = (uint32_t)((kc / kTStages) & 1);
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, DEV_TC_PRODUCER_TIMEOUT)) { abort_with(DEV_TC_PRODUCER_TIMEOUT); break; }
+                uint8_t* st = smem + (size_t)s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                tma_load_2d(st, &mapW, kb * kTK, m0, &full[s]);
+                tma_load_2d(st + kTileABytes, &mapX, kb * kTK, n0, &full[s]);
+                tma_load_2d(st + kTileABytes + kTileBBytes, &mapX, p.K + kb * kTK, n0, &full[s]);
+            }
+        }
+        // every stage issued has been consumed (its MMAs completed) before the CTA exits
+        for (long k = (kc > kTStages ? kc - kTStages : 0); k < kc; ++k) {
+            const int s = (int)(k % kTStages);
+            if (!mbar_wait_bounded(&empty[s], (uint32_t)((k / kTStages) & 1), p.err, DEV_TC_DRAIN_TIMEOUT)) break;
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------ MMA issuer
+        long kc = 0;
+        int it = 0;
+        const uint32_t sbase = smem_u32(smem);
+        for (int tile = blockIdx.x; tile < ntiles && !aborted(); tile += gridDim.x, ++it) {
+            const int buf = it & 1;
+            const uint32_t use = (uint32_t)(it >> 1);
+            if (!mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, p.err, DEV_TC_MMA_TIMEOUT)) { abort_with(DEV_TC_MMA_TIMEOUT); break; }
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(buf * kTN);
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb, ++kc) {
+                const int s = (int)(kc % kTStages);
+                const uint32_t ph = (uint32_t)((kc / kTStages) & 1);
+                if (!mbar_wait_bounded(&full[s], ph, p.err, DEV_TC_MMA_TIMEOUT)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a0 = sbase + (uint32_t)s * kStageBytes;
+                const uint64_t da = sw128_desc(a0), dh = sw128_desc(a0 + kTileABytes),
+                               dl = sw128_desc(a0 + kTileABytes + kTileBBytes);
+#pragma unroll
+                for (int ks = 0; ks < kTK / 16; ++ks) {
+                    const uint64_t adv = (uint64_t)((ks * 32) >> 4);  // +32 bytes along K
+                    umma_bf16(d, da + adv, dh + adv, (kb | ks) != 0 ? 1u : 0u);
+                    umma_bf16(d, da + adv, dl + adv, 1u);
+                }
+                umma_commit(&empty[s]);  // stage free once these MMAs have read it
+            }
+            if (!ok) { abort_with(DEV_TC_MMA_TIMEOUT); break; }
+            umma_commit(&acc_full[buf]);  // accumulator complete
+        }
+        umma_commit(mma_done);
+        mbar_wait_bounded(mma_done, 0u, p.err, DEV_TC_DRAIN_TIMEOUT);
+    } else if (warp >= 2) {
+        // ------------------------------------------------ epilogue
+        const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+            const int buf = it & 1;
+            const uint32_t use = (uint32_t)(it >> 1);
+            bool ok = mbar_wait_bounded(&acc_full[buf], use & 1u, p.err, DEV_TC_EPI_TIMEOUT);
+            ok = __all_sync(0xffffffffu, ok && !aborted());
+            if (!ok) break;
+            tc_fence_after();
+            const int m0 = (tile / ntn) * kTM, n0 = (tile % ntn) * kTN;
+            const int m = m0 + 32 * q + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTN);
+            for (int c = 0; c < kTN; c += 16) {
+                float v[16];
+                tmem_ld16(taddr + (uint32_t)c, v);
+                if (p.epi == TC_SWIGLU_SPLIT) {
+                    // rows alternate gate_i (even) / up_i (odd): pair lanes l, l^1
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float u = __shfl_xor_sync(0xffffffffu, v[j], 1);
+                        const int n = n0 + c + j;
+                        if ((lane & 1) == 0 && m + 1 < p.M && n < p.N) {
+                            const float a = silu_f(v[j]) * u;
+                            const uint16_t hi = bf16_rne(a);
+                            const uint16_t lo = bf16_rne(a - __uint_as_float((uint32_t)hi << 16));
+                            uint16_t* row = p.ys + (size_t)n * p.ldys;
+                            row[m >> 1] = hi;
+                            row[p.split_k + (m >> 1)] = lo;
+                        }
+                    }
+                } else if (m < p.M) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = n0 + c + j;
+                        if (n < p.N) {
+                            float* dst = p.y + (size_t)n * p.ldy + m;
+                            if (p.epi == TC_RESIDUAL) *dst += v[j];
+                            else *dst = v[j];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows][cols] matrix (row stride ld elements),
+// boxes of 128 rows x 64 columns in the 128-byte swizzle; out-of-range rows read as zero.
+int tc_make_map(CUtensorMap* map, const void* base, long rows, long cols, long ld) {
+    auto fn = encode_fn();
+    if (!fn) return -1;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || rows <= 0 || cols <= 0 || ld < cols) return -2;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)kTM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+cudaError_t launch_tc_gemm(const CUtensorMap& mapW, const CUtensorMap& mapX, const TcGemmParams& p,
+                           cudaStream_t s) {
+    if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.K % kTK) return cudaErrorInvalidValue;
+    if (p.epi == TC_SWIGLU_SPLIT ? (!p.ys || p.M % 2) : !p.y) return cudaErrorInvalidValue;
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+        if (e != cudaSuccess) return e;
+        attr_done[dev] = true;
+    }
+    const long ntiles = (long)((p.M + kTM - 1) / kTM) * ((p.N + kTN - 1) / kTN);
+    const int grid = (int)std::min<long>(ntiles, num_sms());
+    k_tc_gemm<<<grid, kTThreads, kTcSmem, s>>>(mapW, mapX, p);
+    return cudaGetLastError();
+}
+
+}  // namespace qwc

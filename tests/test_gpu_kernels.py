@@ -97,3 +97,29 @@ def test_attention_decode_matches_oracle(pkg, oracle, kv_dtype, n_ctx):
                                  NQ, NKV, max_ctx, n_ctx, dout.data_ptr())
         torch.cuda.synchronize()
         assert rel_l2(dout.cpu().numpy(), want) < TOL
+
+
+@pytest.mark.parametrize("M,N,K,acc", [(128, 128, 64, False), (1028, 12, 256, False), (300, 257, 1024, True),
+                                       (8224, 130, 1024, False), (1024, 200, 3584, True),
+                                       (7168, 64, 1024, False), (2000, 1, 2048, False)])
+def test_tc_gemm_matches_fp64(pkg, M, N, K, acc):
+    """qwc_gemm_bf16 (tcgen05, hi/lo activations) against fp64 on the same bf16 operands;
+    with x = hi + lo exact to ~2^-17 the fp32 result agrees to ~1e-5."""
+    g = torch.Generator().manual_seed(M * 31 + N * 7 + K)
+    W = (torch.randn(M, K, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(N, K, generator=g)
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    Xs = torch.cat([hi, lo], dim=1).contiguous()
+    Y0 = torch.randn(N, M, generator=g) if acc else torch.full((N, M), float("nan"))
+    Wd, Xd, Yd = W.cuda(), Xs.cuda(), Y0.clone().cuda()
+    pkg.abi.gemm_bf16(Wd.data_ptr(), Xd.data_ptr(), Yd.data_ptr(), M, N, K, acc)
+    torch.cuda.synchronize()
+    got = Yd.cpu().double()
+    want = (hi.double() + lo.double()) @ W.double().T + (Y0.double() if acc else 0.0)
+    assert torch.isfinite(got).all()
+    err = float((got - want).norm() / want.norm())
+    assert err < 1e-5, err
+    # the split carries x itself to ~2^-17: compare with the exact fp32 activations too
+    exact = x.double() @ W.double().T + (Y0.double() if acc else 0.0)
+    assert float((got - exact).norm() / exact.norm()) < 1e-4

@@ -104,21 +104,39 @@ bool QwenForward::prefill(const std::vector<int>& ids, std::vector<float>& logit
 }
 
 // ---------------------------------------------------------------- C entry points
+namespace qwc {
+void set_api_error(const char* msg);  // engine.cu: the message qwc_last_error(nullptr) returns
+}
+
 extern "C" int qwc_load_config(const char* path, qwc_config* out) {
-    if (!path || !out) return QWC_E_INVALID;
+    if (!path || !out) {
+        qwc::set_api_error("qwc_load_config: null argument");
+        return QWC_E_INVALID;
+    }
     ModelConfig m;
     bool ok = load_model_config(path, m);
-    qwh::to_c(m, *out);
+    qwh::to_c(m, *out);  // the defaults when the file cannot be read, as the reference does
+    if (!ok) qwc::set_api_error((std::string("qwc_load_config: cannot read ") + path).c_str());
     return ok ? QWC_OK : QWC_E_IO;
 }
 
 extern "C" int qwc_create_from_dir(const char* model_dir, int max_context, int kv_dtype, int device, qwc_handle** out) {
-    if (!model_dir || !out) return QWC_E_INVALID;
+    if (!model_dir || !out) {
+        qwc::set_api_error("qwc_create_from_dir: null argument");
+        return QWC_E_INVALID;
+    }
+    *out = nullptr;
     const std::string dir(model_dir);
     ModelConfig m;
-    if (!load_model_config(dir + "/config.json", m)) return QWC_E_IO;
+    if (!load_model_config(dir + "/config.json", m)) {
+        qwc::set_api_error(("qwc_create_from_dir: cannot read " + dir + "/config.json").c_str());
+        return QWC_E_IO;
+    }
     SafeTensors st;
-    if (!st.load_model(dir)) return QWC_E_IO;
+    if (!st.load_model(dir)) {
+        qwc::set_api_error(("qwc_create_from_dir: cannot load the safetensors shards of " + dir).c_str());
+        return QWC_E_IO;
+    }
     qwc_config c;
     qwh::to_c(m, c);
     std::vector<std::string> names;

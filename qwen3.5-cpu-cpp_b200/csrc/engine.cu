@@ -971,7 +971,12 @@ extern "C" int qwc_get_config(const qwc_handle* h, qwc_config* out) {
 // cores plus token-parallel kernels (prefill.cu, tc_gemm.cu), continuing from and updating
 // a decode state, so the same code serves the stateless forward pass (fresh state) and
 // the prefill that seeds decoding.
-constexpr int kPfChunk = 4096;     // tokens per chunk (bounds the workspace)
+constexpr int kPfChunk = 4096;     // tokens per chunk (bounds the workspace); QWC_PREFILL_CHUNK overrides
+static int pf_chunk() {
+    const char* e = std::getenv("QWC_PREFILL_CHUNK");
+    const int v = e ? std::atoi(e) : 0;
+    return v > 0 ? v : kPfChunk;
+}
 constexpr int kPfLogitRows = 128;  // lm_head rows per GEMM when every position's logits are wanted
 
 static int pf_build_maps(qwc_handle* h) {
@@ -1061,12 +1066,13 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
         return fail(h, QWC_E_SHAPE, "batched prefill needs hidden, intermediate, GDN value and attention widths that are multiples of 64");
     int rc = pf_build_maps(h);
     if (rc) return rc;
-    rc = pf_workspace(h, std::min(T, kPfChunk));
+    const int chunk = pf_chunk();
+    rc = pf_workspace(h, std::min(T, chunk));
     if (rc) return rc;
     const int H = h->H;
     const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
-    for (int c0 = 0; c0 < T; c0 += kPfChunk) {
-        const int Tc = std::min(kPfChunk, T - c0), pc = p0 + c0;
+    for (int c0 = 0; c0 < T; c0 += chunk) {
+        const int Tc = std::min(chunk, T - c0), pc = p0 + c0;
         CU(cudaMemcpyAsync(h->pf_ids, ids + c0, (size_t)Tc * 4, cudaMemcpyHostToDevice, h->stream));
         CU(pf_embed(h->pf_ids, Tc, h->embed, H, h->V, h->pf_hid, h->dev_err, h->stream));
         for (int l = 0; l < h->L; ++l) {

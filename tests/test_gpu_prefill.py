@@ -1,0 +1,84 @@
+"""The batched forward pass (tensor-core GEMMs, GDN scan, causal attention) against the
+CPU oracle's QwenForward::prefill and QwenModel::step restatements, at lengths that
+cross chunk boundaries (QWC_PREFILL_CHUNK shrinks the chunk so that small models cover
+the multi-chunk path: KV from earlier chunks, GDN state and conv ring carried over).
+
+Bar (north star): logits rel_l2 <= 2e-3, greedy continuation identical."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import model_dir, rel_l2
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-3
+
+
+@pytest.fixture
+def chunk(request):
+    old = os.environ.get("QWC_PREFILL_CHUNK")
+    os.environ["QWC_PREFILL_CHUNK"] = str(request.param)
+    yield request.param
+    if old is None:
+        del os.environ["QWC_PREFILL_CHUNK"]
+    else:
+        os.environ["QWC_PREFILL_CHUNK"] = old
+
+
+@pytest.mark.parametrize("chunk", [128, 4096], indirect=True)
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_forward_logits_long_all_rows(pkg, oracle, chunk, kv_dtype):
+    d = model_dir(pkg, "tiny")
+    s = pkg.synth.SHAPES["tiny"]
+    T = 300
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=21)
+    m = pkg.abi.Model(d, max_context=T + 8, kv_dtype=kv_dtype)
+    got = m.forward_logits(ids)
+    want = oracle.OracleModel(d, T + 8).prefill(ids)
+    assert got.shape == want.shape == (T, s.vocab_size)
+    per_row = np.array([rel_l2(got[i], want[i]) for i in range(T)])
+    assert per_row.max() < LOGIT_TOL, (per_row.argmax(), per_row.max())
+    assert (got.argmax(1) == want.argmax(1)).mean() > 0.99
+    m.close()
+
+
+@pytest.mark.parametrize("chunk", [96], indirect=True)
+@pytest.mark.parametrize("shape", ["tiny-rep", "small-0.8b-widths"])
+def test_prefill_then_decode_matches_stepping(pkg, oracle, chunk, shape):
+    """qwc_prefill seeds KV / GDN state / conv ring; the decode that follows matches the
+    oracle stepping the same prompt (the reference's generate_greedy path)."""
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    T, n_new = 250, 16
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=5)
+    m = pkg.abi.Model(d, max_context=T + n_new + 4)
+    lg = m.prefill(ids)
+    assert m.position() == T
+    orc = oracle.OracleModel(d, T + n_new + 4)
+    ref = None
+    for t in ids:
+        ref = orc.step(int(t))
+    assert rel_l2(lg, ref) < LOGIT_TOL
+    tok, want_tok = int(np.argmax(lg)), int(np.argmax(ref))
+    assert tok == want_tok
+    for i in range(n_new):
+        lg, am = m.step(tok)
+        ref = orc.step(tok)
+        assert rel_l2(lg, ref) < LOGIT_TOL, f"decode step {i}"
+        assert am == int(np.argmax(ref))
+        tok = am
+    m.close()
+
+
+def test_prefill_is_repeatable_and_resets_state(pkg):
+    d = model_dir(pkg, "tiny")
+    s = pkg.synth.SHAPES["tiny"]
+    ids = pkg.synth.random_prompt(s.vocab_size, 40, seed=2)
+    m = pkg.abi.Model(d, max_context=64)
+    a = m.prefill(ids)
+    m.step(3)
+    b = m.prefill(ids)  # starts again from a reset state
+    assert np.array_equal(a, b)
+    assert m.position() == len(ids)
+    m.close()

@@ -242,6 +242,19 @@ int qwc_gdn_decode_step(const float* mixed, const float* a, const float* b,
                         float* conv_ring, float* state, float* out, int KH, int VH, int pos,
                         void* stream);
 
+/* The GDN mixer core of QwenForward::prefill's mix_gdn (src/qwen_forward.cpp:83-152; per
+ * token the arithmetic of gdn_step, src/qwen_model.cpp:173-207) for T tokens at positions
+ * pos0..pos0+T-1, continuing from conv_ring / state and leaving them as T calls of
+ * qwc_gdn_decode_step would: mixed [T][C] raw conv inputs, a/b [T][VH] raw gate inputs,
+ * out [T][VH][DV] (before the gated norm). The recurrence runs in the chunked WY form
+ * (64-token chunks). workspace: device scratch of at least
+ * qwc_gdn_prefill_workspace(KH, VH, T) bytes. DK = DV = 128, K = 4. */
+size_t qwc_gdn_prefill_workspace(int KH, int VH, int T);
+int qwc_gdn_prefill(const float* mixed, const float* a, const float* b, const float* conv_w,
+                    const float* neg_exp_A, const float* dt_bias, float* conv_ring, float* state,
+                    float* out, int KH, int VH, int T, int pos0, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* Attention of one query over a KV cache on device memory (the loop of attn_step,
  * src/qwen_model.cpp:134-150): q [NQ][HD] (normed and roped), gate [NQ][HD],
  * K/V cache [NKV][max_ctx][HD] of kv_dtype, positions 0..n_ctx-1; out [NQ][HD] =

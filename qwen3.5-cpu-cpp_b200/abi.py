@@ -28,7 +28,8 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_forward_logits", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
            "qwc_gemv_bf16", "qwc_gemm_bf16",
-           "qwc_gdn_decode_step", "qwc_attention_decode")
+           "qwc_gdn_decode_step", "qwc_gdn_prefill", "qwc_gdn_prefill_workspace",
+           "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
                 6: "lm_head", 7: "decode_step"}
 
@@ -156,7 +157,10 @@ class Model:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):
+            pass  # interpreter shutdown: module globals already cleared
 
     def reset(self):
         check(lib().qwc_reset(self._h), self._h)
@@ -262,6 +266,22 @@ def gdn_decode_step(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state, o
                     pos, stream=0):
     check(lib().qwc_gdn_decode_step(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state,
                                     out, KH, VH, pos, stream))
+
+
+def gdn_prefill(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state, out, KH, VH, T, pos0,
+                workspace, workspace_bytes, stream=0):
+    """qwc_gdn_prefill: T tokens of the GDN mixer core (chunked WY recurrence)."""
+    fn = lib().qwc_gdn_prefill
+    fn.argtypes = [C.c_void_p] * 9 + [C.c_int] * 4 + [C.c_void_p, C.c_size_t, C.c_void_p]
+    check(fn(mixed, a, b, conv_w, neg_exp_A, dt_bias, conv_ring, state, out, KH, VH, T, pos0,
+             workspace, workspace_bytes, stream))
+
+
+def gdn_prefill_workspace(KH, VH, T) -> int:
+    fn = lib().qwc_gdn_prefill_workspace
+    fn.argtypes = [C.c_int] * 3
+    fn.restype = C.c_size_t
+    return int(fn(KH, VH, T))
 
 
 def attention_decode_noalloc(q, gate, k_cache, v_cache, kv_dtype, NQ, NKV, max_ctx, n_ctx,

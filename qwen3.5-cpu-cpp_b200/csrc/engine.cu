@@ -111,7 +111,8 @@ struct qwc_handle {
     long pf_ldp = 0, pf_lda = 0, pf_ldb = 0;
     int* pf_ids = nullptr;
     float *pf_hid = nullptr, *pf_proj = nullptr, *pf_o = nullptr, *pf_qn = nullptr, *pf_kn = nullptr,
-          *pf_vc = nullptr, *pf_decay = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
+          *pf_vc = nullptr, *pf_glog = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
+    float *pf_u = nullptr, *pf_w = nullptr, *pf_qg = nullptr, *pf_kd = nullptr, *pf_p = nullptr, *pf_gc = nullptr;
     uint16_t *pf_xa = nullptr, *pf_xb = nullptr;
 
     cudaGraphExec_t graph = nullptr;
@@ -1023,6 +1024,9 @@ static int pf_workspace(qwc_handle* h, int cap) {
                  o_o = carve(c * h->VD * 4), o_qn = carve(c * h->KD * 4), o_kn = carve(c * h->KD * 4),
                  o_vc = carve(c * h->VD * 4), o_dec = carve(c * h->VH * 4), o_beta = carve(c * h->VH * 4),
                  o_qbuf = carve(c * h->NQ * h->HD * 4), o_log = carve((size_t)kPfLogitRows * h->V * 4),
+                 o_u = carve(c * h->VD * 4), o_w = carve(c * h->VD * 4), o_qg = carve(c * h->VD * 4),
+                 o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 64 * 64 * 4),
+                 o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4),
                  o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2);
     if (cudaMalloc(&h->pf_ws, off) != cudaSuccess) {
         h->pf_ws = nullptr;
@@ -1036,7 +1040,13 @@ static int pf_workspace(qwc_handle* h, int cap) {
     h->pf_qn = reinterpret_cast<float*>(b + o_qn);
     h->pf_kn = reinterpret_cast<float*>(b + o_kn);
     h->pf_vc = reinterpret_cast<float*>(b + o_vc);
-    h->pf_decay = reinterpret_cast<float*>(b + o_dec);
+    h->pf_glog = reinterpret_cast<float*>(b + o_dec);
+    h->pf_u = reinterpret_cast<float*>(b + o_u);
+    h->pf_w = reinterpret_cast<float*>(b + o_w);
+    h->pf_qg = reinterpret_cast<float*>(b + o_qg);
+    h->pf_kd = reinterpret_cast<float*>(b + o_kd);
+    h->pf_p = reinterpret_cast<float*>(b + o_p);
+    h->pf_gc = reinterpret_cast<float*>(b + o_gc);
     h->pf_beta = reinterpret_cast<float*>(b + o_beta);
     h->pf_qbuf = reinterpret_cast<float*>(b + o_qbuf);
     h->pf_logits = reinterpret_cast<float*>(b + o_log);
@@ -1109,6 +1119,9 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 PfGdnArgs g;
                 g.proj = h->pf_proj;
                 g.ldp = h->pf_ldp;
+                g.b_in = h->pf_proj + h->C + h->VD;
+                g.a_in = h->pf_proj + h->C + h->VD + h->VH;
+                g.ldab = h->pf_ldp;
                 g.conv_w = lw.conv_w;
                 g.ring = sv.conv_ring + (size_t)lw.idx * h->C * 4;
                 g.neg_exp_A = lw.neg_exp_A;
@@ -1116,7 +1129,13 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 g.qn = h->pf_qn;
                 g.kn = h->pf_kn;
                 g.vc = h->pf_vc;
-                g.decay = h->pf_decay;
+                g.glog = h->pf_glog;
+                g.U = h->pf_u;
+                g.W = h->pf_w;
+                g.QG = h->pf_qg;
+                g.KD = h->pf_kd;
+                g.P = h->pf_p;
+                g.gC = h->pf_gc;
                 g.beta = h->pf_beta;
                 g.state = sv.gdn_state + (size_t)lw.idx * h->VH * h->DK * h->DV;
                 g.out = h->pf_o;
@@ -1374,6 +1393,42 @@ extern "C" int qwc_gemm_bf16(const uint16_t* W, const uint16_t* Xs, float* Y, in
     p.err = kernel_api_err();
     cudaError_t e = launch_tc_gemm(mw, mx, p, (cudaStream_t)stream);
     if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gemm_bf16: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+extern "C" size_t qwc_gdn_prefill_workspace(int KH, int VH, int T) {
+    if (KH <= 0 || VH <= 0 || VH % KH || T <= 0) return 0;
+    return pf_gdn_workspace_bytes(KH, VH, T);
+}
+
+extern "C" int qwc_gdn_prefill(const float* mixed, const float* a, const float* b, const float* conv_w,
+                               const float* neg_exp_A, const float* dt_bias, float* conv_ring, float* state, float* out,
+                               int KH, int VH, int T, int pos0, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!mixed || !a || !b || !conv_w || !neg_exp_A || !dt_bias || !conv_ring || !state || !out || KH <= 0 ||
+        VH <= 0 || VH % KH || T <= 0 || pos0 < 0)
+        return fail(nullptr, QWC_E_INVALID, "qwc_gdn_prefill: invalid argument");
+    PfGdnArgs g;
+    g.T = T;
+    g.KH = KH;
+    g.VH = VH;
+    g.VD = VH * 128;
+    g.C = 2 * KH * 128 + VH * 128;
+    if (pf_gdn_carve(g, workspace, workspace_bytes))
+        return fail(nullptr, QWC_E_INVALID, "qwc_gdn_prefill: workspace missing or smaller than qwc_gdn_prefill_workspace()");
+    g.proj = mixed;
+    g.ldp = g.C;
+    g.a_in = a;
+    g.b_in = b;
+    g.ldab = VH;
+    g.conv_w = conv_w;
+    g.ring = conv_ring;
+    g.neg_exp_A = neg_exp_A;
+    g.dt_bias = dt_bias;
+    g.state = state;
+    g.out = out;
+    g.p0 = pos0;
+    cudaError_t e = pf_gdn(g, (cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gdn_prefill: ") + cudaGetErrorString(e));
     return QWC_OK;
 }
 

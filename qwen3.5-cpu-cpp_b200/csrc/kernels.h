@@ -164,8 +164,11 @@ cudaError_t pf_embed(const int* ids, int T, const uint16_t* embed, int H, int V,
 cudaError_t pf_rmsnorm_split(const float* x, long ldx, int rows, const float* w1, int H, float eps, uint16_t* xs,
                              long ldxs, cudaStream_t s);
 struct PfGdnArgs {
-    const float* proj = nullptr;  // [T][ldp]: qkv C | z VD | b VH | a VH
+    const float* proj = nullptr;  // [T][ldp]: the C conv inputs (q | k | v) first
     long ldp = 0;
+    const float* a_in = nullptr;  // [T][ldab] raw a gate inputs
+    const float* b_in = nullptr;  // [T][ldab] raw b gate inputs
+    long ldab = 0;
     const float* conv_w = nullptr;
     float* ring = nullptr;        // [C][4], read then updated
     const float* neg_exp_A = nullptr;
@@ -173,13 +176,22 @@ struct PfGdnArgs {
     float* qn = nullptr;          // scratch [T][KD]
     float* kn = nullptr;          // scratch [T][KD]
     float* vc = nullptr;          // scratch [T][VD]
-    float* decay = nullptr;       // scratch [T][VH]
+    float* glog = nullptr;        // scratch [T][VH] log decay
     float* beta = nullptr;        // scratch [T][VH]
+    float* U = nullptr;           // scratch [VH][T][128]  (chunked WY form)
+    float* W = nullptr;           // scratch [VH][T][128]
+    float* QG = nullptr;          // scratch [VH][T][128]
+    float* KD = nullptr;          // scratch [VH][T][128]
+    float* P = nullptr;           // scratch [VH][ceil(T/64)][64][64]
+    float* gC = nullptr;          // scratch [VH][ceil(T/64)]
     float* state = nullptr;       // [VH][DK][DV], read then updated
     float* out = nullptr;         // [T][VD]
     int T = 0, p0 = 0, KH = 0, VH = 0, C = 0, VD = 0;
 };
 cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s);
+// Scratch of pf_gdn for T tokens, and its carving into the args' scratch pointers.
+size_t pf_gdn_workspace_bytes(int KH, int VH, int T);
+int pf_gdn_carve(PfGdnArgs& a, void* ws, size_t bytes);
 cudaError_t pf_gated_norm_split(const float* o, long ldo, const float* z, long ldz, const float* w, int T, int nh,
                                 float eps, uint16_t* xs, long ldxs, cudaStream_t s);
 struct PfAttnArgs {

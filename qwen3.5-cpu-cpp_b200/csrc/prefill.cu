@@ -69,11 +69,14 @@ __global__ void __launch_bounds__(kPT) k_pf_rmsnorm_split(const float* x, long l
 // ---------------------------------------------------------------- GDN input preparation
 // Per token: causal depthwise conv (K=4) over the qkv channels, continuing from the conv
 // ring for positions before the chunk, SiLU; l2norm of q and k per head (q also scaled by
-// 1/sqrt(DK)); the gates decay = exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b).
+// 1/sqrt(DK)); the gates g = -exp(A_log) softplus(a + dt_bias) (decay exp(g)), beta = sigmoid(b).
 // One warp per 128-channel head vector (q heads, k heads, v heads), 4 channels per lane.
 struct PfGdnPrep {
-    const float* proj;    // [T][ldp]: qkv C | z VD | b VH | a VH
+    const float* proj;    // [T][ldp]: the C conv inputs (q | k | v) first
     long ldp;
+    const float* a_in;    // [T][ldab] raw a gate inputs (VH)
+    const float* b_in;    // [T][ldab] raw b gate inputs (VH)
+    long ldab;
     const float* conv_w;  // [C][4]
     const float* ring;    // [C][4] (read only here)
     const float* neg_exp_A;
@@ -81,7 +84,7 @@ struct PfGdnPrep {
     float* qn;            // [T][KD]
     float* kn;            // [T][KD]
     float* vc;            // [T][VD]
-    float* decay;         // [T][VH]
+    float* glog;          // [T][VH] g (the decay is exp(g))
     float* beta;          // [T][VH]
     int p0, KH, VH, C, VD;
 };
@@ -89,7 +92,6 @@ __global__ void __launch_bounds__(kPT) k_pf_gdn_prep(const PfGdnPrep p) {
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KD = p.KH * 128;
     const int nvec = 2 * p.KH + p.VH;
-    const float* row = p.proj + (size_t)t * p.ldp;
     for (int v = warp; v < nvec; v += kPT / 32) {
         const int kind = v < p.KH ? 0 : (v < 2 * p.KH ? 1 : 2);
         const int head = kind == 0 ? v : (kind == 1 ? v - p.KH : v - 2 * p.KH);
@@ -138,9 +140,9 @@ __global__ void __launch_bounds__(kPT) k_pf_gdn_prep(const PfGdnPrep p) {
         }
     }
     for (int h = threadIdx.x; h < p.VH; h += kPT) {
-        const float bv = row[p.C + p.VD + h], av = row[p.C + p.VD + p.VH + h];
+        const float bv = p.b_in[(size_t)t * p.ldab + h], av = p.a_in[(size_t)t * p.ldab + h];
         const float g = p.neg_exp_A[h] * softplus_f(av + p.dt_bias[h]);
-        p.decay[(size_t)t * p.VH + h] = expf(g);
+        p.glog[(size_t)t * p.VH + h] = g;  // log of the decay exp(g)
         p.beta[(size_t)t * p.VH + h] = sigmoid_f(bv);
     }
 }
@@ -153,97 +155,289 @@ __global__ void k_pf_conv_ring(const float* proj, long ldp, int T, int p0, int C
     for (int t = (T > 4 ? T - 4 : 0); t < T; ++t) ring[(size_t)c * 4 + ((p0 + t) & 3)] = proj[(size_t)t * ldp + c];
 }
 
-// ---------------------------------------------------------------- GDN recurrence
-// One (value head, 16-column slice) per CTA of 128 threads; thread r owns row r of the
-// slice of S (16 fp32 in registers). The chunk's tokens are processed in order with the
-// delta rule of gdn_step (qwen_model.cpp:199-205), exactly as the decode item does;
-// the inputs of the next 8 tokens are loaded while the current 8 are processed.
-struct PfGdnScan {
-    const float* qn;
-    const float* kn;
-    const float* vc;
-    const float* decay;
-    const float* beta;
-    float* state;  // [VH][DK][DV]
-    float* out;    // [T][VD]
+// ---------------------------------------------------------------- GDN recurrence, chunked
+// The delta rule of gdn_step (qwen_model.cpp:199-205), per value head, in the order
+//   S_t = a_t S_{t-1};  e_t = v_t - S_t^T k_t;  S_t += b_t k_t e_t^T;  o_t = S_t^T q_t
+// (a_t = exp(g_t) the decay, b_t = beta_t), is evaluated for chunks of C = 64 tokens in
+// the WY form. With G_i = g_1 + .. + g_i inside the chunk, gamma_i = exp(G_i) and S0 the
+// state entering the chunk:
+//   e_i = v_i - gamma_i S0^T k_i - sum_{j<i} exp(G_i - G_j) b_j (k_i . k_j) e_j
+//   => (I + L) E = V - Gamma K S0,  L[i][j] = exp(G_i - G_j) b_j (k_i . k_j), j < i
+//   => E = U - W S0 with U = (I + L)^-1 V, W = (I + L)^-1 Gamma K  (forward substitution)
+//   o_i = gamma_i S0^T q_i + sum_{j<=i} P[i][j] e_j,  P[i][j] = exp(G_i - G_j) b_j (q_i . k_j)
+//   S_C = gamma_C S0 + sum_i Kd_i e_i^T,  Kd_i = b_i exp(G_C - G_i) k_i
+// Every exponent is a difference G_i - G_j <= 0 (or a G_i <= 0), so nothing overflows.
+// Kernel A (parallel over chunks and heads) builds U, W, Gamma Q, Kd, P and gamma_C;
+// kernel B (sequential over chunks, parallel over heads and 32-column slices of S) applies
+// E = U - W S, O = (Gamma Q) S + P E, S = gamma_C S + Kd^T E in fp32 on CUDA cores.
+constexpr int kGC = 64;            // tokens per chunk
+constexpr int kGP = 128 + 4;       // padded row stride of 128-wide shared tiles
+constexpr int kGLP = kGC + 1;      // padded row stride of 64 x 64 shared tiles
+constexpr size_t kGdnASmem = (size_t)(3 * kGC * kGP + 2 * kGC * kGLP + 2 * kGC) * 4;
+
+struct PfGdnChunk {
+    const float* qn;     // [T][KD]
+    const float* kn;     // [T][KD]
+    const float* vc;     // [T][VD]
+    const float* glog;   // [T][VH] g = log of the decay
+    const float* beta;   // [T][VH]
+    float* U;            // [VH][T][128]
+    float* W;            // [VH][T][128]
+    float* QG;           // [VH][T][128]  gamma_i q_i
+    float* KD;           // [VH][T][128]  b_i exp(G_C - G_i) k_i
+    float* P;            // [VH][nch][64][64]
+    float* gC;           // [VH][nch]
+    float* state;        // [VH][DK][DV]
+    float* out;          // [T][VD]
     int T, KH, VH, VD;
 };
-constexpr int kScanAhead = 8;
-__global__ void __launch_bounds__(128) k_pf_gdn_scan(const PfGdnScan p) {
-    __shared__ float red16[2][4][16];  // [0]: S^T k partials, [1]: S^T q partials
-    __shared__ float s_d[16];
-    const int vh = blockIdx.x >> 3, vs = blockIdx.x & 7;
-    const int r = threadIdx.x, warp = r >> 5, lane = r & 31;
+
+__global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
+    extern __shared__ __align__(16) float sa[];
+    float* Ks = sa;                 // [64][132] k, later Gamma K -> W
+    float* Qs = Ks + kGC * kGP;     // [64][132]
+    float* Vs = Qs + kGC * kGP;     // [64][132] v -> U
+    float* Ls = Vs + kGC * kGP;     // [64][65]
+    float* Ps = Ls + kGC * kGLP;    // [64][65]
+    float* Gc = Ps + kGC * kGLP;    // [64]
+    float* Bs = Gc + kGC;           // [64]
+    const int c = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x;
+    const int nch = gridDim.x;
     const int rep = p.VH / p.KH, kh = vh / rep, KD = p.KH * 128;
-    float S[16];
-    float* Srow = p.state + ((size_t)vh * 128 + r) * 128 + vs * 16;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float4 v = reinterpret_cast<const float4*>(Srow)[i];
-        S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
+    const int t0 = c * kGC, n = min(kGC, p.T - t0);
+    for (int e = tid; e < kGC * 32; e += 256) {
+        const int i = e >> 5, c4 = (e & 31) * 4;
+        float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = k4, v4 = k4;
+        if (i < n) {
+            const size_t t = (size_t)(t0 + i);
+            k4 = *reinterpret_cast<const float4*>(p.kn + t * KD + kh * 128 + c4);
+            q4 = *reinterpret_cast<const float4*>(p.qn + t * KD + kh * 128 + c4);
+            v4 = *reinterpret_cast<const float4*>(p.vc + t * p.VD + vh * 128 + c4);
+        }
+        *reinterpret_cast<float4*>(Ks + i * kGP + c4) = k4;
+        *reinterpret_cast<float4*>(Qs + i * kGP + c4) = q4;
+        *reinterpret_cast<float4*>(Vs + i * kGP + c4) = v4;
     }
-    const int sidx = scatter_index(lane);
-    // per-token inputs of this thread: q[r], k[r], (v[col] for r < 16), decay, beta
-    float cq[kScanAhead], ck[kScanAhead], cv[kScanAhead], cdec[kScanAhead], cbeta[kScanAhead];
-    auto load = [&](int t0, float* q, float* k, float* v, float* dec, float* be) {
+    if (tid < 32) {
+        // inclusive prefix sum of g over the chunk (two values per lane)
+        const int i0 = 2 * tid;
+        const float ga = i0 < n ? p.glog[(size_t)(t0 + i0) * p.VH + vh] : 0.f;
+        const float gb = i0 + 1 < n ? p.glog[(size_t)(t0 + i0 + 1) * p.VH + vh] : 0.f;
+        float sum = ga + gb;
 #pragma unroll
-        for (int i = 0; i < kScanAhead; ++i) {
-            const int t = t0 + i;
-            const bool in = t < p.T;
-            q[i] = in ? p.qn[(size_t)t * KD + kh * 128 + r] : 0.f;
-            k[i] = in ? p.kn[(size_t)t * KD + kh * 128 + r] : 0.f;
-            v[i] = (in && r < 16) ? p.vc[(size_t)t * p.VD + vh * 128 + vs * 16 + r] : 0.f;
-            dec[i] = in ? p.decay[(size_t)t * p.VH + vh] : 0.f;
-            be[i] = in ? p.beta[(size_t)t * p.VH + vh] : 0.f;
+        for (int o = 1; o < 32; o <<= 1) {
+            const float up = __shfl_up_sync(0xffffffffu, sum, o);
+            if (tid >= o) sum += up;
         }
-    };
-    load(0, cq, ck, cv, cdec, cbeta);
-    for (int t0 = 0; t0 < p.T; t0 += kScanAhead) {
-        float nq[kScanAhead], nk[kScanAhead], nv[kScanAhead], ndec[kScanAhead], nbeta[kScanAhead];
-        load(t0 + kScanAhead, nq, nk, nv, ndec, nbeta);
+        const float excl = sum - (ga + gb);
+        Gc[i0] = excl + ga;
+        Gc[i0 + 1] = excl + ga + gb;
+        Bs[i0] = i0 < n ? p.beta[(size_t)(t0 + i0) * p.VH + vh] : 0.f;
+        Bs[i0 + 1] = i0 + 1 < n ? p.beta[(size_t)(t0 + i0 + 1) * p.VH + vh] : 0.f;
+    }
+    __syncthreads();
+    // KK and QK, 4 x 4 register tiles: rows 4*(tid>>4).., columns (tid&15) + 16*b
+    {
+        const int i0 = (tid >> 4) * 4, jq = tid & 15;
+        float kk[4][4], qk[4][4];
 #pragma unroll
-        for (int i = 0; i < kScanAhead; ++i) {
-            const int t = t0 + i;
-            if (t >= p.T) break;  // uniform
-            const float decay = cdec[i], k = ck[i], q = cq[i];
-            float part[16];
+        for (int a = 0; a < 4; ++a)
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                S[j] *= decay;
-                part[j] = S[j] * k;
-            }
-            // Barriers: (1) km partials written; (2) d written (km partials read);
-            // (3) o partials written. The next token writes km partials only after (3),
-            // when d and the previous km partials are no longer read, and its o partials
-            // only after its own (2), when this token's o partials have been read.
-            float rr = reduce_scatter16(part, lane);
-            if ((lane & 1) == 0) red16[0][warp][sidx] = rr;
-            __syncthreads();
-            if (r < 16) {
-                const float km = (red16[0][0][r] + red16[0][1][r]) + (red16[0][2][r] + red16[0][3][r]);
-                s_d[r] = (cv[i] - km) * cbeta[i];
-            }
-            __syncthreads();
+            for (int b = 0; b < 4; ++b) { kk[a][b] = 0.f; qk[a][b] = 0.f; }
+        for (int d = 0; d < 128; d += 4) {
+            float4 ki[4], qi[4], kj[4];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                S[j] += k * s_d[j];
-                part[j] = S[j] * q;
+            for (int a = 0; a < 4; ++a) {
+                ki[a] = *reinterpret_cast<const float4*>(Ks + (i0 + a) * kGP + d);
+                qi[a] = *reinterpret_cast<const float4*>(Qs + (i0 + a) * kGP + d);
             }
-            rr = reduce_scatter16(part, lane);
-            if ((lane & 1) == 0) red16[1][warp][sidx] = rr;
-            __syncthreads();
-            if (r < 16)
-                p.out[(size_t)t * p.VD + vh * 128 + vs * 16 + r] =
-                    (red16[1][0][r] + red16[1][1][r]) + (red16[1][2][r] + red16[1][3][r]);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) kj[b] = *reinterpret_cast<const float4*>(Ks + (jq + 16 * b) * kGP + d);
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    kk[a][b] += ki[a].x * kj[b].x + ki[a].y * kj[b].y + ki[a].z * kj[b].z + ki[a].w * kj[b].w;
+                    qk[a][b] += qi[a].x * kj[b].x + qi[a].y * kj[b].y + qi[a].z * kj[b].z + qi[a].w * kj[b].w;
+                }
         }
 #pragma unroll
-        for (int i = 0; i < kScanAhead; ++i) {
-            cq[i] = nq[i]; ck[i] = nk[i]; cv[i] = nv[i]; cdec[i] = ndec[i]; cbeta[i] = nbeta[i];
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int i = i0 + a, j = jq + 16 * b;
+                const float f = (j <= i && i < n) ? expf(Gc[i] - Gc[j]) * Bs[j] : 0.f;
+                Ls[i * kGLP + j] = j < i ? f * kk[a][b] : 0.f;
+                Ps[i * kGLP + j] = f * qk[a][b];
+            }
+    }
+    __syncthreads();
+    // outputs that need the raw k and q: Kd, Gamma Q, P, gamma_C; then Ks <- Gamma K
+    const float GC = Gc[n - 1];
+    const size_t hrow = ((size_t)vh * p.T + t0) * 128;
+    for (int e = tid; e < kGC * 32; e += 256) {
+        const int i = e >> 5, c4 = (e & 31) * 4;
+        if (i >= n) continue;
+        const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * kGP + c4);
+        const float4 q4 = *reinterpret_cast<const float4*>(Qs + i * kGP + c4);
+        const float fd = Bs[i] * expf(GC - Gc[i]), fg = expf(Gc[i]);
+        *reinterpret_cast<float4*>(p.KD + hrow + (size_t)i * 128 + c4) =
+            make_float4(fd * k4.x, fd * k4.y, fd * k4.z, fd * k4.w);
+        *reinterpret_cast<float4*>(p.QG + hrow + (size_t)i * 128 + c4) =
+            make_float4(fg * q4.x, fg * q4.y, fg * q4.z, fg * q4.w);
+    }
+    float* Pg = p.P + ((size_t)vh * nch + c) * kGC * kGC;
+    for (int e = tid; e < kGC * kGC; e += 256) Pg[e] = Ps[(e >> 6) * kGLP + (e & 63)];
+    if (tid == 0) p.gC[(size_t)vh * nch + c] = expf(GC);
+    __syncthreads();
+    for (int e = tid; e < kGC * 128; e += 256) {
+        const int i = e >> 7, col = e & 127;
+        Ks[i * kGP + col] *= expf(Gc[i]);
+    }
+    __syncthreads();
+    // forward substitution: U (columns of V) on threads 0-127, W (columns of Gamma K) on 128-255
+    {
+        float* M = tid < 128 ? Vs : Ks;
+        const int col = tid & 127;
+        for (int i = 1; i < n; ++i) {
+            float acc = M[i * kGP + col];
+            for (int m = 0; m < i; ++m) acc -= Ls[i * kGLP + m] * M[m * kGP + col];
+            M[i * kGP + col] = acc;
+            __syncthreads();
         }
     }
+    for (int e = tid; e < kGC * 32; e += 256) {
+        const int i = e >> 5, c4 = (e & 31) * 4;
+        if (i >= n) continue;
+        *reinterpret_cast<float4*>(p.U + hrow + (size_t)i * 128 + c4) = *reinterpret_cast<const float4*>(Vs + i * kGP + c4);
+        *reinterpret_cast<float4*>(p.W + hrow + (size_t)i * 128 + c4) = *reinterpret_cast<const float4*>(Ks + i * kGP + c4);
+    }
+}
+
+// Kernel B: (value head, 32-column slice of S) per CTA of 256 threads, chunks in order.
+constexpr int kGS = 32;              // columns of S per CTA
+constexpr int kGSP = kGS + 4;        // padded stride of [.][32] tiles
+constexpr size_t kGdnBSmem = (size_t)(3 * kGC * kGP + kGC * kGLP + 128 * kGSP + 2 * kGC * kGSP) * 4;
+__global__ void __launch_bounds__(256) k_pf_gdn_chunk_b(const PfGdnChunk p) {
+    extern __shared__ __align__(16) float sb[];
+    float* Wsm = sb;                    // [64][132]
+    float* Qsm = Wsm + kGC * kGP;       // [64][132]
+    float* Ksm = Qsm + kGC * kGP;       // [64][132]
+    float* Psm = Ksm + kGC * kGP;       // [64][65]
+    float* Ssm = Psm + kGC * kGLP;      // [128][36]
+    float* Usm = Ssm + 128 * kGSP;      // [64][36] U slice, then E
+    float* Osm = Usm + kGC * kGSP;      // [64][36]
+    const int vh = blockIdx.x / (128 / kGS), sl = blockIdx.x % (128 / kGS), tid = threadIdx.x;
+    const int nch = (p.T + kGC - 1) / kGC;
+    float* Sg = p.state + (size_t)vh * 128 * 128 + sl * kGS;
+    for (int e = tid; e < 128 * (kGS / 4); e += 256) {
+        const int r = e / (kGS / 4), c4 = (e % (kGS / 4)) * 4;
+        *reinterpret_cast<float4*>(Ssm + r * kGSP + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
+    }
+    // output tiles: rows 2*(tid>>3) .. +1, columns 4*(tid&7) .. +3 (64 x 32)
+    const int oi = (tid >> 3) * 2, oc = (tid & 7) * 4;
+    // state tiles: rows 4*(tid>>3) .. +3, columns 4*(tid&7) .. +3 (128 x 32)
+    const int sr = (tid >> 3) * 4;
+    for (int c = 0; c < nch; ++c) {
+        const int t0 = c * kGC, n = min(kGC, p.T - t0);
+        const size_t hrow = ((size_t)vh * p.T + t0) * 128;
+        __syncthreads();  // previous chunk fully consumed
+        for (int e = tid; e < kGC * 32; e += 256) {
+            const int i = e >> 5, c4 = (e & 31) * 4;
+            float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = w4, k4 = w4;
+            if (i < n) {
+                w4 = *reinterpret_cast<const float4*>(p.W + hrow + (size_t)i * 128 + c4);
+                q4 = *reinterpret_cast<const float4*>(p.QG + hrow + (size_t)i * 128 + c4);
+                k4 = *reinterpret_cast<const float4*>(p.KD + hrow + (size_t)i * 128 + c4);
+            }
+            *reinterpret_cast<float4*>(Wsm + i * kGP + c4) = w4;
+            *reinterpret_cast<float4*>(Qsm + i * kGP + c4) = q4;
+            *reinterpret_cast<float4*>(Ksm + i * kGP + c4) = k4;
+        }
+        const float* Pg = p.P + ((size_t)vh * nch + c) * kGC * kGC;
+        for (int e = tid; e < kGC * kGC; e += 256) Psm[(e >> 6) * kGLP + (e & 63)] = Pg[e];
+        for (int e = tid; e < kGC * (kGS / 4); e += 256) {
+            const int i = e / (kGS / 4), c4 = (e % (kGS / 4)) * 4;
+            float4 u4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n) u4 = *reinterpret_cast<const float4*>(p.U + hrow + (size_t)i * 128 + sl * kGS + c4);
+            *reinterpret_cast<float4*>(Usm + i * kGSP + c4) = u4;
+        }
+        const float gC = p.gC[(size_t)vh * nch + c];
+        __syncthreads();
+        // E = U - W S and the (Gamma Q) S part of O
+        {
+            float e2[2][4], o2[2][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-        reinterpret_cast<float4*>(Srow)[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+            for (int a = 0; a < 2; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) { e2[a][b] = 0.f; o2[a][b] = 0.f; }
+            for (int r = 0; r < 128; ++r) {
+                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGSP + oc);
+#pragma unroll
+                for (int a = 0; a < 2; ++a) {
+                    const float w = Wsm[(oi + a) * kGP + r], q = Qsm[(oi + a) * kGP + r];
+                    e2[a][0] += w * s4.x; e2[a][1] += w * s4.y; e2[a][2] += w * s4.z; e2[a][3] += w * s4.w;
+                    o2[a][0] += q * s4.x; o2[a][1] += q * s4.y; o2[a][2] += q * s4.z; o2[a][3] += q * s4.w;
+                }
+            }
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+                float4* u = reinterpret_cast<float4*>(Usm + (oi + a) * kGSP + oc);
+                const float4 uv = *u;
+                *u = make_float4(uv.x - e2[a][0], uv.y - e2[a][1], uv.z - e2[a][2], uv.w - e2[a][3]);
+                *reinterpret_cast<float4*>(Osm + (oi + a) * kGSP + oc) = make_float4(o2[a][0], o2[a][1], o2[a][2], o2[a][3]);
+            }
+        }
+        __syncthreads();  // E complete (in Usm); S still the chunk's input state
+        // O += P E, written out; S = gamma_C S + Kd^T E
+        {
+            float o2[2][4];
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+                const float4 ov = *reinterpret_cast<const float4*>(Osm + (oi + a) * kGSP + oc);
+                o2[a][0] = ov.x; o2[a][1] = ov.y; o2[a][2] = ov.z; o2[a][3] = ov.w;
+            }
+            for (int j = 0; j <= oi + 1 && j < kGC; ++j) {
+                const float4 e4 = *reinterpret_cast<const float4*>(Usm + j * kGSP + oc);
+#pragma unroll
+                for (int a = 0; a < 2; ++a) {
+                    const float pv = Psm[(oi + a) * kGLP + j];
+                    o2[a][0] += pv * e4.x; o2[a][1] += pv * e4.y; o2[a][2] += pv * e4.z; o2[a][3] += pv * e4.w;
+                }
+            }
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+                const int i = oi + a;
+                if (i < n)
+                    *reinterpret_cast<float4*>(p.out + (size_t)(t0 + i) * p.VD + vh * 128 + sl * kGS + oc) =
+                        make_float4(o2[a][0], o2[a][1], o2[a][2], o2[a][3]);
+            }
+            float s4[4][4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float4 sv = *reinterpret_cast<const float4*>(Ssm + (sr + a) * kGSP + oc);
+                s4[a][0] = gC * sv.x; s4[a][1] = gC * sv.y; s4[a][2] = gC * sv.z; s4[a][3] = gC * sv.w;
+            }
+            for (int i = 0; i < n; ++i) {
+                const float4 e4 = *reinterpret_cast<const float4*>(Usm + i * kGSP + oc);
+                const float4 k4 = *reinterpret_cast<const float4*>(Ksm + i * kGP + sr);
+                const float kr[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    s4[a][0] += kr[a] * e4.x; s4[a][1] += kr[a] * e4.y; s4[a][2] += kr[a] * e4.z; s4[a][3] += kr[a] * e4.w;
+                }
+            }
+            __syncthreads();  // every read of the old S (above, other threads) is done
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+                *reinterpret_cast<float4*>(Ssm + (sr + a) * kGSP + oc) = make_float4(s4[a][0], s4[a][1], s4[a][2], s4[a][3]);
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < 128 * (kGS / 4); e += 256) {
+        const int r = e / (kGS / 4), c4 = (e % (kGS / 4)) * 4;
+        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * kGSP + c4);
+    }
 }
 
 // ---------------------------------------------------------------- gated RMSNorm -> split
@@ -518,14 +712,53 @@ cudaError_t pf_rmsnorm_split(const float* x, long ldx, int rows, const float* w1
     return cudaGetLastError();
 }
 cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
-    PfGdnPrep pp{a.proj, a.ldp, a.conv_w, a.ring, a.neg_exp_A, a.dt_bias, a.qn, a.kn, a.vc, a.decay, a.beta,
-                 a.p0, a.KH, a.VH, a.C, a.VD};
+    if (a.VH % a.KH) return cudaErrorInvalidValue;
+    PfGdnPrep pp{a.proj, a.ldp, a.a_in, a.b_in, a.ldab, a.conv_w, a.ring, a.neg_exp_A, a.dt_bias, a.qn, a.kn, a.vc,
+                 a.glog, a.beta, a.p0, a.KH, a.VH, a.C, a.VD};
     k_pf_gdn_prep<<<a.T, kPT, 0, s>>>(pp);
     k_pf_conv_ring<<<(a.C + 255) / 256, 256, 0, s>>>(a.proj, a.ldp, a.T, a.p0, a.C, a.ring);
-    PfGdnScan sc{a.qn, a.kn, a.vc, a.decay, a.beta, a.state, a.out, a.T, a.KH, a.VH, a.VD};
-    k_pf_gdn_scan<<<a.VH * 8, 128, 0, s>>>(sc);
+    PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.state, a.out,
+                  a.T, a.KH, a.VH, a.VD};
+    {
+        cudaError_t e = cudaFuncSetAttribute(k_pf_gdn_chunk_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnASmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_pf_gdn_chunk_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnBSmem);
+        if (e != cudaSuccess) return e;
+    }
+    const int nch = (a.T + kGC - 1) / kGC;
+    k_pf_gdn_chunk_a<<<dim3(nch, a.VH), 256, kGdnASmem, s>>>(ck);
+    k_pf_gdn_chunk_b<<<a.VH * (128 / kGS), 256, kGdnBSmem, s>>>(ck);
     return cudaGetLastError();
 }
+size_t pf_gdn_workspace_bytes(int KH, int VH, int T) {
+    const size_t t = (size_t)T, nch = (t + kGC - 1) / kGC, KD = (size_t)KH * 128, VD = (size_t)VH * 128;
+    auto r = [](size_t b) { return (b + 255) / 256 * 256; };
+    return 2 * r(t * KD * 4) + 5 * r(t * VD * 4) + 2 * r(t * VH * 4) + r(VH * nch * kGC * kGC * 4) + r(VH * nch * 4);
+}
+int pf_gdn_carve(PfGdnArgs& a, void* ws, size_t bytes) {
+    const size_t t = (size_t)a.T, nch = (t + kGC - 1) / kGC, KD = (size_t)a.KH * 128, VD = (size_t)a.VH * 128;
+    if (!ws || bytes < pf_gdn_workspace_bytes(a.KH, a.VH, a.T)) return -1;
+    uint8_t* b = static_cast<uint8_t*>(ws);
+    size_t off = 0;
+    auto take = [&](size_t n) {
+        float* f = reinterpret_cast<float*>(b + off);
+        off += (n * 4 + 255) / 256 * 256;
+        return f;
+    };
+    a.qn = take(t * KD);
+    a.kn = take(t * KD);
+    a.vc = take(t * VD);
+    a.U = take(t * VD);
+    a.W = take(t * VD);
+    a.QG = take(t * VD);
+    a.KD = take(t * VD);
+    a.glog = take(t * a.VH);
+    a.beta = take(t * a.VH);
+    a.P = take(a.VH * nch * kGC * kGC);
+    a.gC = take(a.VH * nch);
+    return 0;
+}
+
 cudaError_t pf_gated_norm_split(const float* o, long ldo, const float* z, long ldz, const float* w, int T, int nh,
                                 float eps, uint16_t* xs, long ldxs, cudaStream_t s) {
     k_pf_gated_norm_split<<<T, kPT, 0, s>>>(o, ldo, z, ldz, w, nh, eps, xs, ldxs);

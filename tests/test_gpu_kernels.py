@@ -123,3 +123,49 @@ def test_tc_gemm_matches_fp64(pkg, M, N, K, acc):
     # the split carries x itself to ~2^-17: compare with the exact fp32 activations too
     exact = x.double() @ W.double().T + (Y0.double() if acc else 0.0)
     assert float((got - exact).norm() / exact.norm()) < 1e-4
+
+
+@pytest.mark.parametrize("KH,VH", [(16, 16), (2, 4)])
+@pytest.mark.parametrize("split", [None, 130])
+def test_gdn_prefill_matches_oracle(pkg, oracle, KH, VH, split):
+    """qwc_gdn_prefill (chunked WY recurrence) against the oracle's token-by-token
+    restatement, from a non-zero state, in one call or two calls that continue."""
+    DK = DV = 128
+    C = 2 * KH * DK + VH * DV
+    T = 300
+    rng = np.random.default_rng(KH * 100 + VH)
+    mixed = rng.standard_normal((T, C), dtype=np.float32)
+    a = rng.standard_normal((T, VH), dtype=np.float32)
+    b = rng.standard_normal((T, VH), dtype=np.float32)
+    conv_w = (rng.standard_normal((C, 4), dtype=np.float32) * 0.1).astype(np.float32)
+    A_log = rng.uniform(0, np.log(16), VH).astype(np.float32)
+    dt = np.ones(VH, np.float32)
+    state = (rng.standard_normal((VH, DK, DV), dtype=np.float32) * 0.1).astype(np.float32)
+    want = np.empty((T, VH, DV), np.float32)
+    cs = np.zeros((C, 3), np.float32)
+    st_want = state.copy()
+    oracle.orc_lib().orc_gdn_core(T, KH, VH, DK, DV, 4, mixed, conv_w, a, b, A_log, dt, st_want, cs, want)
+
+    neg = (-np.exp(A_log)).astype(np.float32)
+    d_conv_w, d_neg, d_dt = dev(conv_w), dev(neg), dev(dt)
+    d_ring = torch.zeros((C, 4), device="cuda")
+    d_state = dev(state)
+    d_mixed, d_a, d_b = dev(mixed), dev(a), dev(b)
+    d_out = torch.full((T, VH * DV), float("nan"), device="cuda")
+    ws_bytes = pkg.abi.gdn_prefill_workspace(KH, VH, T)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    parts = [(0, T)] if split is None else [(0, split), (split, T - split)]
+    for p0, n in parts:
+        pkg.abi.gdn_prefill(d_mixed[p0].data_ptr(), d_a[p0].data_ptr(), d_b[p0].data_ptr(), d_conv_w.data_ptr(),
+                            d_neg.data_ptr(), d_dt.data_ptr(), d_ring.data_ptr(), d_state.data_ptr(),
+                            d_out[p0].data_ptr(), KH, VH, n, p0, ws.data_ptr(), ws_bytes)
+    torch.cuda.synchronize()
+    got = d_out.cpu().numpy().reshape(T, VH, DV)
+    assert np.isfinite(got).all()
+    assert rel_l2(got, want) < 2e-5
+    assert rel_l2(d_state.cpu().numpy(), st_want) < 2e-5
+    # the conv ring holds the last inputs in slot pos % 4 (the oracle keeps the last K-1)
+    ring = d_ring.cpu().numpy()
+    for j in range(3):
+        pos = T - 3 + j
+        assert np.array_equal(ring[:, pos % 4], mixed[pos])

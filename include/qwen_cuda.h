@@ -89,6 +89,17 @@ typedef struct {
 
 typedef struct qwc_handle qwc_handle;
 
+/* Head-wise tensor-parallel shard of one rank (no reference counterpart: the reference is
+ * single-process). GDN k heads [kh0, kh0+n_kh) and v heads [vh0, vh0+n_vh) with their q/k/v
+ * channels, z rows, b/a rows, conv channels, A_log/dt_bias and out_proj input columns;
+ * attention q heads [q0, q0+n_q) with the kv heads [kv0, kv0+n_kv) they read (replicated
+ * when world > attn_kv_heads) and the o_proj input columns; FFN intermediate rows
+ * [i0, i0+n_i) of gate/up and the down_proj input columns. Embedding, norms and lm_head
+ * are replicated. */
+typedef struct {
+    int kh0, n_kh, vh0, n_vh, q0, n_q, kv0, n_kv, i0, n_i;
+} qwc_tp_shard;
+
 /* ---------------------------------------------------------------- config / budget */
 
 /* load_model_config (src/config_loader.cpp:59-108): fills *cfg from config.json
@@ -211,6 +222,29 @@ int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* byte
  * error code (QWC_E_INVALID when the persistent kernel is not in use). Allocates a
  * temporary device buffer. */
 int qwc_trace_step(qwc_handle* h, int cap, int64_t* out);
+
+/* ---------------------------------------------------------------- tensor parallel */
+
+/* The shard of `rank` among `world` ranks; QWC_E_SHAPE when the model does not divide
+ * (GDN heads, q heads and the FFN width must divide by world, the per-rank FFN width by 64,
+ * and world must divide the kv heads or be a multiple of them). */
+int qwc_tp_shard_of(const qwc_config* cfg, int rank, int world, qwc_tp_shard* out);
+
+/* NCCL unique id (128 bytes) that rank 0 creates and sends to the other ranks (the caller's
+ * own transport, e.g. torch.distributed), before every rank calls qwc_create_tp. */
+int qwc_tp_unique_id(void* out, int bytes);
+
+/* As qwc_create, for rank `rank` of a `world`-rank tensor-parallel group on one node: the
+ * handle holds only its shard (qwc_tp_shard_of) and an NCCL communicator over the ranks
+ * (every rank calls this concurrently). Such a handle serves the batched forward pass
+ * (qwc_forward_logits, qwc_prefill) with an all-reduce of the [T][hidden] partial sums
+ * after each mixer output projection and each down_proj; decode (qwc_step and the
+ * generation calls) needs a single-GPU handle and returns QWC_E_INVALID. */
+int qwc_create_tp(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
+                  int kv_dtype, int device, int rank, int world, const void* unique_id,
+                  qwc_handle** out);
+int qwc_create_from_dir_tp(const char* model_dir, int max_context, int kv_dtype, int device, int rank,
+                           int world, const void* unique_id, qwc_handle** out);
 
 /* ---------------------------------------------------------------- kernel level */
 

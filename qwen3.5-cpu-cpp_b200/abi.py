@@ -28,6 +28,7 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_forward_logits", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
            "qwc_gemv_bf16", "qwc_gemm_bf16",
+           "qwc_tp_shard_of", "qwc_tp_unique_id", "qwc_create_tp", "qwc_create_from_dir_tp",
            "qwc_gdn_decode_step", "qwc_gdn_prefill", "qwc_gdn_prefill_workspace",
            "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
@@ -48,6 +49,14 @@ class qwc_budget(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "weight_bytes", "gdn_state_bytes", "gdn_conv_bytes", "kv_cache_bytes",
         "activation_bytes", "vision_scratch_bytes")]
+
+    def as_dict(self):
+        return {n: int(getattr(self, n)) for n, _ in self._fields_}
+
+
+class qwc_tp_shard(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("kh0", "n_kh", "vh0", "n_vh", "q0", "n_q", "kv0", "n_kv",
+                                       "i0", "n_i")]
 
     def as_dict(self):
         return {n: int(getattr(self, n)) for n, _ in self._fields_}
@@ -86,6 +95,10 @@ def lib():
     L.qwc_create.argtypes = [C.POINTER(qwc_config), C.POINTER(qwc_tensor), C.c_int, C.c_int,
                              C.c_int, C.c_int, C.POINTER(vp)]
     L.qwc_create_from_dir.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]
+    L.qwc_create_from_dir_tp.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.c_char_p, C.POINTER(vp)]
+    L.qwc_tp_unique_id.argtypes = [C.c_char_p, C.c_int]
+    L.qwc_tp_shard_of.argtypes = [C.POINTER(qwc_config), C.c_int, C.c_int, C.POINTER(qwc_tp_shard)]
     L.qwc_destroy.argtypes = [vp]
     L.qwc_destroy.restype = None
     L.qwc_last_error.argtypes = [vp]
@@ -136,14 +149,35 @@ def compute_budget(cfg: qwc_config, bpw=2, max_context=1024, kv_bytes=4, tiles=4
     return b.as_dict()
 
 
+def tp_unique_id() -> bytes:
+    """qwc_tp_unique_id: the NCCL id rank 0 sends to the other ranks."""
+    buf = C.create_string_buffer(128)
+    check(lib().qwc_tp_unique_id(buf, 128))
+    return buf.raw
+
+
+def tp_shard(cfg: qwc_config, rank: int, world: int) -> dict:
+    """qwc_tp_shard_of: the heads / rows / columns that `rank` holds."""
+    sh = qwc_tp_shard()
+    check(lib().qwc_tp_shard_of(C.byref(cfg), rank, world, C.byref(sh)))
+    return sh.as_dict()
+
+
 class Model:
-    """One device-resident model + decode state (QwenModel over the C ABI)."""
+    """One device-resident model + decode state (QwenModel over the C ABI). With
+    world > 1 the handle is rank `rank`'s tensor-parallel shard (prefill only); every
+    rank must construct it concurrently with the same `unique_id`."""
 
     def __init__(self, model_dir: str, max_context: int = 4096, kv_dtype: int = DTYPE_F32,
-                 device: int = 0):
+                 device: int = 0, rank: int = 0, world: int = 1, unique_id: bytes | None = None):
         h = C.c_void_p()
-        check(lib().qwc_create_from_dir(model_dir.encode(), max_context, kv_dtype, device,
-                                        C.byref(h)))
+        if world == 1:
+            check(lib().qwc_create_from_dir(model_dir.encode(), max_context, kv_dtype, device,
+                                            C.byref(h)))
+        else:
+            check(lib().qwc_create_from_dir_tp(model_dir.encode(), max_context, kv_dtype, device,
+                                               rank, world, unique_id, C.byref(h)))
+        self.rank, self.world = rank, world
         self._h = h
         cfg = qwc_config()
         check(lib().qwc_get_config(self._h, C.byref(cfg)), self._h)

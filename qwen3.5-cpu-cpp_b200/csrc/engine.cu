@@ -10,6 +10,8 @@
 #include "qwen_cuda.h"
 #include "kernels.h"
 
+#include <nccl.h>
+
 #include <algorithm>
 
 #include <cmath>
@@ -114,6 +116,14 @@ struct qwc_handle {
           *pf_vc = nullptr, *pf_glog = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
     float *pf_u = nullptr, *pf_w = nullptr, *pf_qg = nullptr, *pf_kd = nullptr, *pf_p = nullptr, *pf_gc = nullptr;
     uint16_t *pf_xa = nullptr, *pf_xb = nullptr;
+
+    // tensor parallelism: this handle holds `shard` of a tp_world-rank group; the working
+    // sizes above (KH, VH, KD, VD, C, NQ, NKV, I) are the shard's, g_* the whole model's
+    int tp_rank = 0, tp_world = 1;
+    qwc_tp_shard shard{};
+    int gKH = 0, gVH = 0, gKD = 0, gVD = 0, gC = 0, gNQ = 0, gNKV = 0, gI = 0;
+    ncclComm_t nccl = nullptr;
+    float* pf_part = nullptr;  // prefill: [chunk][H] partial sums to all-reduce
 
     cudaGraphExec_t graph = nullptr;
     bool use_graph = true, use_pdl = true;
@@ -291,6 +301,30 @@ static int upload_mat(qwc_handle* h, uint16_t* dst, size_t dpitch, const qwc_ten
     return QWC_OK;
 }
 
+// Rows [row0, row0+nrows) of a BF16 matrix [total_rows][cols] into dst (row pitch dpitch).
+static int upload_rows(qwc_handle* h, uint16_t* dst, size_t dpitch, const qwc_tensor* t, int64_t total_rows,
+                       int64_t cols, int64_t row0, int64_t nrows) {
+    if (t->dtype != QWC_DTYPE_BF16)
+        return fail(h, QWC_E_SHAPE, std::string("matrix ") + t->name + " must be BF16");
+    if (numel_of(t) != total_rows * cols)
+        return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected shape");
+    const uint16_t* src = static_cast<const uint16_t*>(t->data) + row0 * cols;
+    CU(cudaMemcpy2D(dst, dpitch * 2, src, cols * 2, cols * 2, nrows, cudaMemcpyHostToDevice));
+    return QWC_OK;
+}
+
+// Columns [col0, col0+ncols) of a BF16 matrix [rows][total_cols] into a dense [rows][ncols].
+static int upload_cols(qwc_handle* h, uint16_t* dst, const qwc_tensor* t, int64_t rows, int64_t total_cols,
+                       int64_t col0, int64_t ncols) {
+    if (t->dtype != QWC_DTYPE_BF16)
+        return fail(h, QWC_E_SHAPE, std::string("matrix ") + t->name + " must be BF16");
+    if (numel_of(t) != rows * total_cols)
+        return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected shape");
+    const uint16_t* src = static_cast<const uint16_t*>(t->data) + col0;
+    CU(cudaMemcpy2D(dst, ncols * 2, src, total_cols * 2, ncols * 2, rows, cudaMemcpyHostToDevice));
+    return QWC_OK;
+}
+
 static int vec_f32(qwc_handle* h, const qwc_tensor* t, int64_t n, std::vector<float>& out, float add = 0.f) {
     if (numel_of(t) != n) return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected size");
     out.resize(n);
@@ -329,7 +363,9 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
             const qwc_tensor* o = b.need(A + "o_proj.weight");
             const qwc_tensor* qn = b.need(A + "q_norm.weight");
             const qwc_tensor* kn = b.need(A + "k_norm.weight");
+            // this shard's q heads [q0, q0+NQ) and the kv heads [kv0, kv0+NKV) they read
             const int qr = 2 * h->NQ * h->HD, kr = h->NKV * h->HD;
+            const int64_t q0 = h->shard.q0, kv0 = h->shard.kv0;
             lw.in_rows = qr + 2 * kr;
             lw.w_in = (const uint16_t*)a.take((size_t)lw.in_rows * H * 2);
             lw.out_in = h->NQ * h->HD;
@@ -339,10 +375,11 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
             if (doit && b.missing.empty()) {
                 uint16_t* wi = const_cast<uint16_t*>(lw.w_in);
                 int rc;
-                if ((rc = upload_mat(h, wi, H, q, qr, H))) return rc;
-                if ((rc = upload_mat(h, wi + (size_t)qr * H, H, k, kr, H))) return rc;
-                if ((rc = upload_mat(h, wi + (size_t)(qr + kr) * H, H, v, kr, H))) return rc;
-                if ((rc = upload_mat(h, const_cast<uint16_t*>(lw.w_out), lw.out_in, o, H, lw.out_in))) return rc;
+                const int64_t HD = h->HD;
+                if ((rc = upload_rows(h, wi, H, q, 2L * h->gNQ * HD, H, q0 * 2 * HD, qr))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)qr * H, H, k, (int64_t)h->gNKV * HD, H, kv0 * HD, kr))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)(qr + kr) * H, H, v, (int64_t)h->gNKV * HD, H, kv0 * HD, kr))) return rc;
+                if ((rc = upload_cols(h, const_cast<uint16_t*>(lw.w_out), o, H, (int64_t)h->gNQ * HD, q0 * HD, lw.out_in))) return rc;
                 if ((rc = vec_f32(h, qn, h->HD, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.qn1), tmp))) return rc;
                 if ((rc = vec_f32(h, kn, h->HD, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.kn1), tmp))) return rc;
             }
@@ -367,20 +404,38 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
             lw.dt_bias = (const float*)a.take((size_t)h->VH * 4);
             lw.gn_w = (const float*)a.take((size_t)h->DV * 4);
             if (doit && b.missing.empty()) {
+                // this shard's k heads [kh0, +KH) and v heads [vh0, +VH): their q, k, v channels,
+                // z rows, b / a rows, conv channels and gates, out_proj input columns
                 uint16_t* wi = const_cast<uint16_t*>(lw.w_in);
+                const int64_t kh0 = h->shard.kh0, vh0 = h->shard.vh0, DK = h->DK, DV = h->DV;
+                const int64_t KD = h->KD, VD = h->VD, C = h->C, VHl = h->VH;
                 int rc;
-                if ((rc = upload_mat(h, wi, H, qkv, h->C, H))) return rc;
-                if ((rc = upload_mat(h, wi + (size_t)h->C * H, H, z, h->VD, H))) return rc;
-                if ((rc = upload_mat(h, wi + (size_t)(h->C + h->VD) * H, H, bb, h->VH, H))) return rc;
-                if ((rc = upload_mat(h, wi + (size_t)(h->C + h->VD + h->VH) * H, H, aa, h->VH, H))) return rc;
-                if ((rc = upload_mat(h, const_cast<uint16_t*>(lw.w_out), h->VD, op, H, h->VD))) return rc;
-                if ((rc = vec_f32(h, cw, (int64_t)h->C * h->KER, tmp))) return rc;
-                if ((rc = upload_f32(h, const_cast<float*>(lw.conv_w), tmp))) return rc;
+                if ((rc = upload_rows(h, wi, H, qkv, h->gC, H, kh0 * DK, KD))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)KD * H, H, qkv, h->gC, H, h->gKD + kh0 * DK, KD))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)2 * KD * H, H, qkv, h->gC, H, 2L * h->gKD + vh0 * DV, VD))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)C * H, H, z, h->gVD, H, vh0 * DV, VD))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)(C + VD) * H, H, bb, h->gVH, H, vh0, VHl))) return rc;
+                if ((rc = upload_rows(h, wi + (size_t)(C + VD + VHl) * H, H, aa, h->gVH, H, vh0, VHl))) return rc;
+                if ((rc = upload_cols(h, const_cast<uint16_t*>(lw.w_out), op, H, h->gVD, vh0 * DV, VD))) return rc;
+                if ((rc = vec_f32(h, cw, (int64_t)h->gC * h->KER, tmp))) return rc;
+                {
+                    std::vector<float> cl((size_t)C * h->KER);
+                    auto take = [&](int64_t dst_ch, int64_t src_ch, int64_t n) {
+                        std::memcpy(&cl[(size_t)dst_ch * h->KER], &tmp[(size_t)src_ch * h->KER], (size_t)n * h->KER * 4);
+                    };
+                    take(0, kh0 * DK, KD);
+                    take(KD, h->gKD + kh0 * DK, KD);
+                    take(2 * KD, 2L * h->gKD + vh0 * DV, VD);
+                    if ((rc = upload_f32(h, const_cast<float*>(lw.conv_w), cl))) return rc;
+                }
                 // -exp(A_log) with the host expf, as the reference evaluates it
-                if ((rc = vec_f32(h, al, h->VH, tmp))) return rc;
+                if ((rc = vec_f32(h, al, h->gVH, tmp))) return rc;
+                tmp = std::vector<float>(tmp.begin() + vh0, tmp.begin() + vh0 + VHl);
                 for (auto& x : tmp) x = -std::exp(x);
                 if ((rc = upload_f32(h, const_cast<float*>(lw.neg_exp_A), tmp))) return rc;
-                if ((rc = vec_f32(h, dt, h->VH, tmp)) || (rc = upload_f32(h, const_cast<float*>(lw.dt_bias), tmp))) return rc;
+                if ((rc = vec_f32(h, dt, h->gVH, tmp))) return rc;
+                tmp = std::vector<float>(tmp.begin() + vh0, tmp.begin() + vh0 + VHl);
+                if ((rc = upload_f32(h, const_cast<float*>(lw.dt_bias), tmp))) return rc;
                 if ((rc = vec_f32(h, gn, h->DV, tmp)) || (rc = upload_f32(h, const_cast<float*>(lw.gn_w), tmp))) return rc;
             }
         }
@@ -388,10 +443,12 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
             int rc;
             if ((rc = vec_f32(h, iln, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.in_ln1), tmp))) return rc;
             if ((rc = vec_f32(h, pln, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(lw.post_ln1), tmp))) return rc;
+            // this shard's intermediate rows [i0, i0+I) of gate / up and down_proj columns
             uint16_t* gu = const_cast<uint16_t*>(lw.w_gu);
-            if ((rc = upload_mat(h, gu, 2 * (size_t)H, gp, I, H))) return rc;
-            if ((rc = upload_mat(h, gu + H, 2 * (size_t)H, up, I, H))) return rc;
-            if ((rc = upload_mat(h, const_cast<uint16_t*>(lw.w_down), I, dp, H, I))) return rc;
+            const int64_t i0 = h->shard.i0;
+            if ((rc = upload_rows(h, gu, 2 * (size_t)H, gp, h->gI, H, i0, I))) return rc;
+            if ((rc = upload_rows(h, gu + H, 2 * (size_t)H, up, h->gI, H, i0, I))) return rc;
+            if ((rc = upload_cols(h, const_cast<uint16_t*>(lw.w_down), dp, H, h->gI, i0, I))) return rc;
         }
     }
     const qwc_tensor* emb = b.need(LM + "embed_tokens.weight");
@@ -740,14 +797,65 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     cudaFree(h->scratch);
     cudaFree(h->step_phases);
     cudaFree(h->pf_ws);
+    if (h->nccl) ncclCommDestroy(h->nccl);
     if (h->h_pin) cudaFreeHost(h->h_pin);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
 }
 
+extern "C" int qwc_tp_shard_of(const qwc_config* c, int rank, int world, qwc_tp_shard* o) {
+    if (!c || !o || world < 1 || rank < 0 || rank >= world) return fail(nullptr, QWC_E_INVALID, "qwc_tp_shard_of: invalid argument");
+    const int KH = c->gdn_k_heads, VH = c->gdn_v_heads, NQ = c->attn_q_heads, NKV = c->attn_kv_heads;
+    const int I = c->ffn_intermediate;
+    if (KH <= 0 || VH <= 0 || NKV <= 0 || NQ % NKV || VH % KH)
+        return fail(nullptr, QWC_E_SHAPE, "qwc_tp_shard_of: inconsistent head counts");
+    if (KH % world || VH % world || NQ % world || I % world || (world > 1 && (I / world) % 64) ||
+        !(NKV % world == 0 || world % NKV == 0))
+        return fail(nullptr, QWC_E_SHAPE, "the model does not split over " + std::to_string(world) + " ranks");
+    o->n_kh = KH / world;
+    o->kh0 = rank * o->n_kh;
+    o->n_vh = VH / world;
+    o->vh0 = rank * o->n_vh;
+    o->n_q = NQ / world;
+    o->q0 = rank * o->n_q;
+    if (world <= NKV) {
+        o->n_kv = NKV / world;
+        o->kv0 = rank * o->n_kv;
+    } else {  // several ranks share (a replica of) one kv head
+        o->n_kv = 1;
+        o->kv0 = o->q0 / (NQ / NKV);
+    }
+    o->n_i = I / world;
+    o->i0 = rank * o->n_i;
+    return QWC_OK;
+}
+
+extern "C" int qwc_tp_unique_id(void* out, int bytes) {
+    if (!out || bytes < (int)sizeof(ncclUniqueId)) return fail(nullptr, QWC_E_INVALID, "qwc_tp_unique_id: buffer too small");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return fail(nullptr, QWC_E_CUDA, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
+    return QWC_OK;
+}
+
+static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
+                       int kv_dtype, int device, int rank, int world, const void* unique_id, qwc_handle** out);
+
 extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
                           int kv_dtype, int device, qwc_handle** out) {
-    if (!cfg || !out || (!tensors && n_tensors > 0) || max_context <= 0)
+    return create_impl(cfg, tensors, n_tensors, max_context, kv_dtype, device, 0, 1, nullptr, out);
+}
+
+extern "C" int qwc_create_tp(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
+                             int kv_dtype, int device, int rank, int world, const void* unique_id, qwc_handle** out) {
+    if (world > 1 && !unique_id) return fail(nullptr, QWC_E_INVALID, "qwc_create_tp: unique_id is required");
+    return create_impl(cfg, tensors, n_tensors, max_context, kv_dtype, device, rank, world, unique_id, out);
+}
+
+static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
+                       int kv_dtype, int device, int rank, int world, const void* unique_id, qwc_handle** out) {
+    if (!cfg || !out || (!tensors && n_tensors > 0) || max_context <= 0 || world < 1 || rank < 0 || rank >= world)
         return fail(nullptr, QWC_E_INVALID, "qwc_create: invalid argument");
     if (kv_dtype != QWC_DTYPE_F32 && kv_dtype != QWC_DTYPE_BF16)
         return fail(nullptr, QWC_E_INVALID, "qwc_create: kv_dtype must be F32 or BF16");
@@ -789,6 +897,21 @@ extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int 
     h->n_gdn = h->L - h->n_attn;
     h->cfg.n_layers_attn = h->n_attn;
     h->cfg.n_layers_gdn = h->n_gdn;
+    // tensor-parallel shard: the working sizes become the shard's
+    h->tp_rank = rank;
+    h->tp_world = world;
+    h->gKH = h->KH; h->gVH = h->VH; h->gKD = h->KD; h->gVD = h->VD; h->gC = h->C;
+    h->gNQ = h->NQ; h->gNKV = h->NKV; h->gI = h->I;
+    rc = qwc_tp_shard_of(&h->cfg, rank, world, &h->shard);
+    if (rc) { delete h; return rc; }
+    h->KH = h->shard.n_kh;
+    h->VH = h->shard.n_vh;
+    h->KD = h->KH * h->DK;
+    h->VD = h->VH * h->DV;
+    h->C = 2 * h->KD + h->VD;
+    h->NQ = h->shard.n_q;
+    h->NKV = h->shard.n_kv;
+    h->I = h->shard.n_i;
 
     Builder b;
     b.h = h;
@@ -812,8 +935,14 @@ extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int 
     rc = place_weights(h, b, real);
     if (rc) return bail(rc);
 
-    // state arenas, sized by the memory equation (compute_budget with bpw 2)
-    qwc_compute_budget(&h->cfg, 2, max_context, h->kv_bytes, 4, 1024, &h->budget);
+    // state arenas, sized by the memory equation (compute_budget with bpw 2) for this shard
+    qwc_config local = h->cfg;
+    local.gdn_k_heads = h->KH;
+    local.gdn_v_heads = h->VH;
+    local.attn_q_heads = h->NQ;
+    local.attn_kv_heads = h->NKV;
+    local.ffn_intermediate = h->I;
+    qwc_compute_budget(&local, 2, max_context, h->kv_bytes, 4, 1024, &h->budget);
     h->gdn_bytes = h->budget.gdn_state_bytes;
     h->kvc_bytes = h->budget.kv_cache_bytes;
     // conv state: a ring of K slots per channel (the equation counts K-1)
@@ -871,6 +1000,17 @@ extern "C" int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int 
 
     rc = qwc_reset(h);
     if (rc) return bail(rc);
+    if (world > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, unique_id, sizeof(id));
+        const ncclResult_t r = ncclCommInitRank(&h->nccl, world, id, rank);
+        if (r != ncclSuccess) {
+            h->nccl = nullptr;
+            return bail(fail(h, QWC_E_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(r)));
+        }
+        *out = h;  // decode state machinery is single-GPU only
+        return QWC_OK;
+    }
     rc = setup_persistent(h);
     if (rc) return bail(rc);
     rc = build_graph(h);
@@ -906,6 +1046,7 @@ extern "C" int qwc_position(const qwc_handle* h) { return h ? h->pos_host : -1; 
 
 extern "C" int qwc_step(qwc_handle* h, int token, float* logits_host, int* argmax_out) {
     if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_step: null handle");
+    if (h->tp_world > 1) return fail(h, QWC_E_INVALID, "qwc_step: decode needs a single-GPU handle");
     if (token < 0 || token >= h->V) return fail(h, QWC_E_INVALID, "qwc_step: token id out of range");
     if (h->pos_host >= h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_step: position would exceed max_context");
     CU(cudaSetDevice(h->device));
@@ -928,6 +1069,7 @@ extern "C" int qwc_step(qwc_handle* h, int token, float* logits_host, int* argma
 
 extern "C" int qwc_generate_greedy(qwc_handle* h, const int* prompt, int n_prompt, int n_new, int* out_tokens) {
     if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_generate_greedy: null handle");
+    if (h->tp_world > 1) return fail(h, QWC_E_INVALID, "qwc_generate_greedy: decode needs a single-GPU handle");
     if (n_prompt < 0 || n_new < 0 || (n_prompt > 0 && !prompt) || (n_new > 0 && !out_tokens))
         return fail(h, QWC_E_INVALID, "qwc_generate_greedy: invalid argument");
     for (int i = 0; i < n_prompt; ++i)
@@ -1026,7 +1168,7 @@ static int pf_workspace(qwc_handle* h, int cap) {
                  o_qbuf = carve(c * h->NQ * h->HD * 4), o_log = carve((size_t)kPfLogitRows * h->V * 4),
                  o_u = carve(c * h->VD * 4), o_w = carve(c * h->VD * 4), o_qg = carve(c * h->VD * 4),
                  o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 64 * 64 * 4),
-                 o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4),
+                 o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4), o_part = carve(c * h->H * 4),
                  o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2);
     if (cudaMalloc(&h->pf_ws, off) != cudaSuccess) {
         h->pf_ws = nullptr;
@@ -1047,6 +1189,7 @@ static int pf_workspace(qwc_handle* h, int cap) {
     h->pf_kd = reinterpret_cast<float*>(b + o_kd);
     h->pf_p = reinterpret_cast<float*>(b + o_p);
     h->pf_gc = reinterpret_cast<float*>(b + o_gc);
+    h->pf_part = reinterpret_cast<float*>(b + o_part);
     h->pf_beta = reinterpret_cast<float*>(b + o_beta);
     h->pf_qbuf = reinterpret_cast<float*>(b + o_qbuf);
     h->pf_logits = reinterpret_cast<float*>(b + o_log);
@@ -1065,6 +1208,27 @@ static int pf_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t* xs, lon
     p.K = K;
     p.err = h->dev_err;
     CU(launch_tc_gemm(mw, mx, p, h->stream));
+    return QWC_OK;
+}
+
+// hidden += W x for a row-parallel projection. One rank: the GEMM's residual epilogue.
+// Tensor parallel: each rank's partial sum over its input columns, summed over the ranks
+// by an NCCL all-reduce, then added to the (replicated) hidden state.
+static int pf_residual_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t* xs, long ldxs, int Tc, int K) {
+    TcGemmParams g;
+    g.ldy = h->H;
+    if (h->tp_world == 1) {
+        g.epi = TC_RESIDUAL;
+        g.y = h->pf_hid;
+        return pf_gemm(h, mw, xs, ldxs, h->H, Tc, K, g);
+    }
+    g.epi = TC_STORE;
+    g.y = h->pf_part;
+    int rc = pf_gemm(h, mw, xs, ldxs, h->H, Tc, K, g);
+    if (rc) return rc;
+    const ncclResult_t r = ncclAllReduce(h->pf_part, h->pf_part, (size_t)Tc * h->H, ncclFloat32, ncclSum, h->nccl, h->stream);
+    if (r != ncclSuccess) return fail(h, QWC_E_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+    CU(pf_add(h->pf_hid, h->pf_part, (size_t)Tc * h->H, h->stream));
     return QWC_OK;
 }
 
@@ -1149,11 +1313,7 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 CU(pf_gated_norm_split(h->pf_o, h->VD, h->pf_proj + h->C, h->pf_ldp, lw.gn_w, Tc, h->VH, h->eps,
                                        h->pf_xa, h->pf_lda, h->stream));
             }
-            TcGemmParams go;
-            go.epi = TC_RESIDUAL;
-            go.y = h->pf_hid;
-            go.ldy = H;
-            if ((rc = pf_gemm(h, h->pf_map_out[l], h->pf_xa, h->pf_lda, H, Tc, lw.out_in, go))) return rc;
+            if ((rc = pf_residual_gemm(h, h->pf_map_out[l], h->pf_xa, h->pf_lda, Tc, lw.out_in))) return rc;
             // FFN: post-attention norm, gate/up + SwiGLU (written as hi/lo for down), down + residual
             CU(pf_rmsnorm_split(h->pf_hid, H, Tc, lw.post_ln1, H, h->eps, h->pf_xa, h->pf_lda, h->stream));
             TcGemmParams gu;
@@ -1162,11 +1322,7 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
             gu.ldys = h->pf_ldb;
             gu.split_k = h->I;
             if ((rc = pf_gemm(h, h->pf_map_gu[l], h->pf_xa, h->pf_lda, 2 * h->I, Tc, H, gu))) return rc;
-            TcGemmParams gd;
-            gd.epi = TC_RESIDUAL;
-            gd.y = h->pf_hid;
-            gd.ldy = H;
-            if ((rc = pf_gemm(h, h->pf_map_down[l], h->pf_xb, h->pf_ldb, H, Tc, h->I, gd))) return rc;
+            if ((rc = pf_residual_gemm(h, h->pf_map_down[l], h->pf_xb, h->pf_ldb, Tc, h->I))) return rc;
         }
         // final norm + lm_head for the rows whose logits are wanted
         if (!logits_host) continue;
@@ -1252,7 +1408,7 @@ extern "C" int qwc_set_prompt(qwc_handle* h, const int* prompt, int n_prompt) {
 }
 
 extern "C" int qwc_enqueue_greedy(qwc_handle* h, int n_prompt, int n_new) {
-    if (!h || n_prompt <= 0 || n_new < 0) return fail(h, QWC_E_INVALID, "qwc_enqueue_greedy: invalid argument");
+    if (!h || n_prompt <= 0 || n_new < 0 || h->tp_world > 1) return fail(h, QWC_E_INVALID, "qwc_enqueue_greedy: invalid argument");
     if ((long)n_prompt + n_new > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_enqueue_greedy: exceeds max_context");
     if (h->gdn_bytes) CU(cudaMemsetAsync(h->st.gdn_state, 0, h->gdn_bytes, h->stream));
     if (h->conv_bytes) CU(cudaMemsetAsync(h->st.conv_ring, 0, h->conv_bytes, h->stream));
@@ -1276,7 +1432,7 @@ extern "C" int qwc_read_tokens(qwc_handle* h, int start, int n, int* out) {
 }
 
 extern "C" int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* bytes) {
-    if (!h || cap < 0 || (cap > 0 && (!kind || !ms || !bytes))) return fail(h, QWC_E_INVALID, "qwc_profile_step: invalid argument");
+    if (!h || cap < 0 || (cap > 0 && (!kind || !ms || !bytes)) || h->tp_world > 1) return fail(h, QWC_E_INVALID, "qwc_profile_step: invalid argument");
     if (h->pos_host >= h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_profile_step: context full");
     CU(cudaSetDevice(h->device));
     StepProfile prof;

@@ -209,6 +209,7 @@ struct PfAttnArgs {
     long ldxs = 0;
 };
 cudaError_t pf_attention(const PfAttnArgs& a, cudaStream_t s);
+cudaError_t pf_add(float* y, const float* x, size_t n, cudaStream_t s);  // y += x (16-byte aligned)
 
 // Records a handle-less failure message (what qwc_last_error(NULL) returns).
 void set_api_error(const char* msg);

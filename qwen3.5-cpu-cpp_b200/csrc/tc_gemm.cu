@@ -16,7 +16,7 @@
 // token tile inner, so concurrent CTAs share a weight tile through L2).
 //   warp 0 (one lane)  TMA producer: 2-D tiled loads (128-byte swizzle) of the weight
 //                      tile (128 x 64) and the hi / lo activation tiles (128 x 64 each)
-//                      into a 4-stage ring; no multicast.
+//                      into a 4-stage ring; every CTA loads its own tiles.
 //   warp 1             allocates 256 TMEM columns (two fp32 accumulators of 128 x 128);
 //                      one lane issues tcgen05.mma (M=128, N=128, K=16, kind::f16, bf16
 //                      in, fp32 accumulate) from shared-memory descriptors and commits

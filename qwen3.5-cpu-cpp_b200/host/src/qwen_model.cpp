@@ -120,21 +120,22 @@ extern "C" int qwc_load_config(const char* path, qwc_config* out) {
     return ok ? QWC_OK : QWC_E_IO;
 }
 
-extern "C" int qwc_create_from_dir(const char* model_dir, int max_context, int kv_dtype, int device, qwc_handle** out) {
+static int create_from_dir(const char* model_dir, int max_context, int kv_dtype, int device, int rank, int world,
+                           const void* unique_id, qwc_handle** out, const char* who) {
     if (!model_dir || !out) {
-        qwc::set_api_error("qwc_create_from_dir: null argument");
+        qwc::set_api_error((std::string(who) + ": null argument").c_str());
         return QWC_E_INVALID;
     }
     *out = nullptr;
     const std::string dir(model_dir);
     ModelConfig m;
     if (!load_model_config(dir + "/config.json", m)) {
-        qwc::set_api_error(("qwc_create_from_dir: cannot read " + dir + "/config.json").c_str());
+        qwc::set_api_error((std::string(who) + ": cannot read " + dir + "/config.json").c_str());
         return QWC_E_IO;
     }
     SafeTensors st;
     if (!st.load_model(dir)) {
-        qwc::set_api_error(("qwc_create_from_dir: cannot load the safetensors shards of " + dir).c_str());
+        qwc::set_api_error((std::string(who) + ": cannot load the safetensors shards of " + dir).c_str());
         return QWC_E_IO;
     }
     qwc_config c;
@@ -142,5 +143,17 @@ extern "C" int qwc_create_from_dir(const char* model_dir, int max_context, int k
     std::vector<std::string> names;
     std::vector<qwc_tensor> tensors;
     qwh::tensor_table(st, names, tensors);
-    return qwc_create(&c, tensors.data(), (int)tensors.size(), max_context, kv_dtype, device, out);
+    if (world == 1) return qwc_create(&c, tensors.data(), (int)tensors.size(), max_context, kv_dtype, device, out);
+    return qwc_create_tp(&c, tensors.data(), (int)tensors.size(), max_context, kv_dtype, device, rank, world,
+                         unique_id, out);
+}
+
+extern "C" int qwc_create_from_dir(const char* model_dir, int max_context, int kv_dtype, int device, qwc_handle** out) {
+    return create_from_dir(model_dir, max_context, kv_dtype, device, 0, 1, nullptr, out, "qwc_create_from_dir");
+}
+
+extern "C" int qwc_create_from_dir_tp(const char* model_dir, int max_context, int kv_dtype, int device, int rank,
+                                      int world, const void* unique_id, qwc_handle** out) {
+    return create_from_dir(model_dir, max_context, kv_dtype, device, rank, world, unique_id, out,
+                           "qwc_create_from_dir_tp");
 }

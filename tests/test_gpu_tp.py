@@ -1,0 +1,72 @@
+"""Tensor-parallel prefill (head-sharded GDN / attention, column/row-sharded FFN, NCCL
+all-reduce after out_proj / o_proj / down_proj) on 2, 4 or 8 GPUs of one box, against
+the single-GPU forward pass and the CPU oracle. Each rank is a separate process on its
+own GPU; the NCCL id travels over a gloo process group. Skipped with fewer GPUs."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import model_dir, rel_l2
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _rank_main(rank, world, port, d, ids, max_ctx, out_dir):
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    abi = __graft_entry__.load_package().abi
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        box = [abi.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        m = abi.Model(d, max_context=max_ctx, device=rank, rank=rank, world=world, unique_id=box[0])
+        all_rows = m.forward_logits(ids)
+        last = m.prefill(ids)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "all.npy"), all_rows)
+            np.save(os.path.join(out_dir, "last.npy"), last)
+        dist.barrier()
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("shape,world", [("tiny", 2), ("small-0.8b-widths", 2), ("small-0.8b-widths", 4),
+                                         ("small-0.8b-widths", 8)])
+def test_tp_prefill_matches_single_gpu_and_oracle(pkg, oracle, tmp_path, shape, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    T = 200
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=17)
+    mp.start_processes(_rank_main, args=(world, _free_port(), d, ids, T + 8, str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    got = np.load(tmp_path / "all.npy")
+    last = np.load(tmp_path / "last.npy")
+    one = pkg.abi.Model(d, max_context=T + 8)
+    want1 = one.forward_logits(ids)
+    one.close()
+    per_row = np.array([rel_l2(got[i], want1[i]) for i in range(T)])
+    assert per_row.max() < 1e-4, per_row.max()  # same arithmetic, partial sums reordered
+    assert rel_l2(last, got[-1]) < 1e-5
+    want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=True)
+    assert rel_l2(got[-1], want.reshape(-1)[-s.vocab_size:]) < 2e-3

@@ -22,6 +22,15 @@ reference processes its prompt one token at a time).
 --impl reference times the reference's CPU generate_greedy on the same workload.
 Multi-GPU: single-sequence decode does not shard; N ranks run N independent replicas
 (weak scaling), value = total tokens/s over all ranks.
+
+--workload prefill measures the batched forward pass instead (configs[3] / [4]: the
+2B-shaped model, --seq-len tokens, default 8192): one step = one qwc_prefill of the whole
+prompt (state seeded for decoding, last logits returned). Under torchrun the N ranks run it
+tensor parallel (heads sharded, NCCL all-reduce inside the library; strong scaling), value =
+prompt tokens / device time (max over ranks). Roofline: tensor, the algorithmic FLOPs of
+the forward pass (2 x projection parameters per token, causal attention
+4 NQ HD (t+1) per token per attention layer, GDN 7 DK DV per head per token per GDN layer,
+the lm_head for the last token) against the measured bf16 peak.
 """
 import argparse
 import json
@@ -183,6 +192,143 @@ def phase_shares(m):
     for k, d in zip(kinds, dur):
         out[k] = out.get(k, 0.0) + float(d) / tot
     return {k: round(v, 4) for k, v in out.items()}, round(tot / 1e3, 2)
+
+
+def prefill_flops(c, T):
+    """Algorithmic FLOPs of a T-token forward pass (see the module docstring)."""
+    H, I, V, L = c.hidden_size, c.ffn_intermediate, c.vocab_size, c.n_layers_total
+    DK, DV, KH, VH = c.gdn_k_head_dim, c.gdn_v_head_dim, c.gdn_k_heads, c.gdn_v_heads
+    KD, VD = KH * DK, VH * DV
+    NQ, NKV, HD = c.attn_q_heads, c.attn_kv_heads, c.attn_head_dim
+    n_attn = L // c.attn_interval
+    n_gdn = L - n_attn
+    gdn_proj = (2 * KD + VD + VD + 2 * VH) * H + H * VD
+    attn_proj = (2 * NQ * HD + 2 * NKV * HD) * H + H * NQ * HD
+    params = n_gdn * gdn_proj + n_attn * attn_proj + L * 3 * I * H
+    f = 2.0 * params * T
+    f += n_attn * 4.0 * NQ * HD * T * (T + 1) / 2
+    f += n_gdn * 7.0 * DK * DV * VH * T
+    f += 2.0 * V * H
+    return f, params
+
+
+def prefill_launches(c, T, world, chunk=4096):
+    """Kernels the library launches for one qwc_prefill: per chunk the embedding, per
+    layer two norms and four GEMMs, the mixer (attention: prep + attention; GDN: prep,
+    conv ring, the two chunked-recurrence kernels, gated norm), with tensor parallelism
+    one residual add per all-reduce; then final norm + lm_head."""
+    L = c.n_layers_total
+    n_attn = L // c.attn_interval
+    per_chunk = 1 + n_attn * (6 + 2) + (L - n_attn) * (6 + 5) + (2 * L if world > 1 else 0)
+    return ((T + chunk - 1) // chunk) * per_chunk + 2
+
+
+def measured_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops", 1590.0), "measured"
+    return 1590.0, "fallback"
+
+
+def run_prefill(args):
+    import numpy as np
+    import torch
+    import __graft_entry__
+    torch.cuda.set_device(LOCAL_RANK)
+    dist = None
+    if WORLD > 1:
+        import datetime
+        import torch.distributed as dist
+        # plumbing only (NCCL id, barriers, max over ranks); the all-reduces of the
+        # forward pass run on the library's own NCCL communicator
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    pkg = __graft_entry__.load_package()
+    name = args.model or "qwen3.5-2b-shaped"
+    shape = pkg.synth.SHAPES[name]
+    base = os.environ.get("QWC_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "qwc_models"))
+    mdir = os.path.join(base, f"{name}-s0")
+    if RANK == 0:
+        pkg.synth.write_model(shape, mdir, seed=0)
+    if dist:
+        dist.barrier()
+    d = pkg.synth.write_model(shape, mdir, seed=0)
+    T = args.seq_len
+    box = [pkg.abi.tp_unique_id() if RANK == 0 and WORLD > 1 else None]
+    if dist:
+        dist.broadcast_object_list(box, src=0)
+    m = pkg.abi.Model(d, max_context=T + 16, device=LOCAL_RANK, rank=RANK, world=WORLD, unique_id=box[0])
+    ids = pkg.synth.random_prompt(shape.vocab_size, T, seed=1234)
+    stream = torch.cuda.ExternalStream(m.stream())
+    for _ in range(args.warmup):
+        m.prefill(ids)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = LOCAL_RANK
+    if vis:
+        ids_v = [v for v in vis.split(",") if v.strip()]
+        if LOCAL_RANK < len(ids_v) and ids_v[LOCAL_RANK].strip().isdigit():
+            gpu_index = int(ids_v[LOCAL_RANK])
+    with ClockSampler(gpu_index) as clocks:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            lg = m.prefill(ids)
+        e1.record(stream)
+        stream.synchronize()
+        wall = time.perf_counter() - w0
+        if dist:
+            dist.barrier()
+    dev_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, wall = float(t[0]), float(t[1])
+    cfg = m.cfg
+    flops, params = prefill_flops(cfg, T)
+    tf, tf_src = measured_tflops()
+    achieved = flops * args.steps / (dev_ms / 1000.0) / 1e12
+    value = T * args.steps / (dev_ms / 1000.0)
+    line = {"metric": "prefill tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": WORLD,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"prefill of {T} random ids, {name} (configs[3]/[4] shape)", "model": name,
+                       "global_batch": 1, "seq_len": T, "parallelism": f"tp{WORLD}",
+                       "kv_cache": "fp32", "projection_params": params,
+                       "l2": "inputs larger than L2 (weights and activations of every layer streamed)"},
+            "roofline": {"bound": "tensor", "kernel": "whole forward pass (tcgen05 GEMMs + GDN + attention)",
+                         "achieved": round(achieved, 1), "peak": tf, "unit": "TFLOP/s",
+                         "frac": round(achieved / tf, 4), "peak_source": tf_src, "traffic": None,
+                         "flops_per_step": flops},
+            "e2e": {"value": round(T * args.steps / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * T,
+                    "d2h_bytes_per_step": 4 * shape.vocab_size},
+            "gpu_launches": args.steps * prefill_launches(cfg, T, WORLD), "clocks": clocks.summary(),
+            "last_argmax": int(np.argmax(lg))}
+    if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
+        from oracle import bindings
+        n = min(T, 64)
+        if bindings.ref_available():
+            ref, kind = bindings.RefModel(d, n + 2), "reference"
+        else:
+            ref, kind = bindings.OracleModel(d, n + 2), "port"
+        t0 = time.perf_counter()
+        ref.prefill(ids[:n])
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(n / secs, 3), "unit": "tok/s",
+                                "cores": int(os.environ.get("OMP_NUM_THREADS", HOST_CORES)), "kind": kind,
+                                "sample": f"QwenForward::prefill of the first {n} ids ({secs:.1f} s)"}
+    m.close()
+    if RANK == 0:
+        emit(line)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
 
 
 def measured_peaks():
@@ -407,10 +553,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode")
+    ap.add_argument("--seq-len", type=int, default=8192, help="prefill workload: prompt length")
+    ap.add_argument("--model", default=None, help="prefill workload: synthetic shape name")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)
+    if args.workload == "prefill":
+        return run_prefill(args)
     return run_ours(args)
 
 

@@ -33,6 +33,11 @@ constexpr int kWarpsA = 8;
 constexpr int kAttnThreads = kWarpsA * 32;
 constexpr int kMinChunk = 32;  // positions per split at least
 
+// Barrier over the kAttnThreads threads that run an item (named barrier 2), so that a
+// larger CTA can run the item on its first kAttnThreads threads only.
+__device__ __forceinline__ void attn_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+static_assert(kAttnThreads == 256, "attn_sync counts 256 threads");
+
 __device__ __forceinline__ void load8(const void* base, int kv_bf16, size_t off, float* o) {
     if (kv_bf16) {
         const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + off);
@@ -178,7 +183,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
             }
         }
     }
-    __syncthreads();
+    attn_sync();
     mark(0);
 
     float qr[GRP][8];
@@ -247,7 +252,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     for (int g = 0; g < GRP; ++g) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) wacc[warp][lane * 8 + e] = acc[g][e];
-        __syncthreads();
+        attn_sync();
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kWarpsA; ++w) M = fmaxf(M, wm[w][g]);
@@ -261,7 +266,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
         cm[g] = M;
         cl[g] = L;
         co[g] = o;
-        __syncthreads();
+        attn_sync();
     }
 
     mark(2);
@@ -288,14 +293,14 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     }
     // publish: every thread's partial is ordered before thread 0's release fence by the
     // CTA barrier; the CTA that takes the last ticket fences again before reading
-    __syncthreads();
+    attn_sync();
     if (t == 0) {
         __threadfence();
         const unsigned tk = atomicAdd(&p.counters[kv], 1u);
         s_last = (tk == (unsigned)n_act - 1) ? 1 : 0;
         if (s_last) __threadfence();
     }
-    __syncthreads();
+    attn_sync();
     if (!s_last) return;
     float gate[GRP];
 #pragma unroll
@@ -308,7 +313,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     const bool staged = npairs <= kWarpsA * kHD / 2;
     if (staged) {
         for (int i = t; i < npairs; i += kAttnThreads) ml_s[i] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + pair0 + i);
-        __syncthreads();
+        attn_sync();
     }
     auto ml_of = [&](int s2, int g) -> float2 {
         return staged ? ml_s[s2 * GRP + g] : __ldcg(reinterpret_cast<const float2*>(p.part_ml) + pair0 + (size_t)s2 * GRP + g);

@@ -5,14 +5,15 @@
 // Why: at batch 1 every projection is a small GEMV (1-17 MB). As separate kernels each
 // one pays a launch plus several dependent memory round trips after its input is ready,
 // and can keep only ~64 KB of weights in flight per SM in registers. Here one CTA per SM
-// lives for the whole step, and every warp streams the weight rows it owns -- for the
-// current GEMV phase and, ahead of time, for the following ones -- through its own ring
-// of 4 KB shared-memory slots filled by 1-D bulk TMA copies (cp.async.bulk; eight
-// issuing warps per SM with 4 KB copies sustain ~6.4 TB/s). Before blocking on a phase
-// barrier a warp tops its ring up, so HBM keeps streaming while the grid waits, while
-// the GDN recurrence and the attention run, and while activations are exchanged.
-// Weights never depend on activations; only x (the GEMV input vector) and the small
-// mixer phases wait for the barrier.
+// lives for the whole step. Eight consumer warps compute; each owns a contiguous range
+// of every GEMV's rows and reads them from its own ring of 4 KB shared-memory slots. A
+// ninth, producer warp fills the rings with 1-D bulk TMA copies (cp.async.bulk, L2
+// evict-first): its lane w walks consumer w's rows of every GEMV phase of the step in
+// order and refills a slot as soon as the consumer releases it (empty / full mbarrier
+// pair per slot). The producer never waits for a phase barrier -- weights never depend
+// on activations -- so HBM keeps streaming while the grid waits, while the GDN recurrence
+// and the attention run and while activations are exchanged, and the consumers never
+// spend time issuing copies (an issuing thread is held ~0.4 us per copy).
 //
 // Phase types (descriptors built once on the host, in global memory, staged per phase
 // in shared memory):
@@ -25,10 +26,12 @@
 // Each phase body is a separate non-inlined function so that it gets its own register
 // allocation (one inlined body would spill the others' hot loops).
 //
-// Barrier: every CTA adds 1 to a 64-bit arrival counter after a phase; phase p may start
-// when the counter reaches p * NC. The last CTA to finish the step resets it. All waits
-// are bounded (they post an error code and stop the step instead of hanging), and the
-// kernel is launched cooperatively, so all CTAs are co-resident.
+// Barrier: every CTA adds 1 to a 64-bit arrival counter after a phase (release); phase p
+// may start when the counter reaches p * NC (acquire). The last CTA to finish the step
+// resets it. CTA-level synchronisation inside the step is a named barrier over the 256
+// consumer threads (the producer warp runs its own loop). All waits are bounded (they
+// post an error code and stop the step instead of hanging), and the kernel is launched
+// cooperatively, so all CTAs are co-resident.
 #include "attn_body.cuh"
 #include "gdn_body.cuh"
 
@@ -37,8 +40,9 @@
 
 namespace qwc {
 
-constexpr int kSW = 8;                 // warps per CTA
-constexpr int kSThreads = kSW * 32;
+constexpr int kSW = 8;                 // consumer warps per CTA (each owns GEMV rows)
+constexpr int kSThreads = kSW * 32;    // consumer threads
+constexpr int kBlockThreads = kSThreads + 32;  // + the producer warp
 constexpr int kChunkBytes = 4096;      // one ring slot = one bulk copy
 constexpr int kGroupBytes = 512;       // 32 lanes x 16 B
 constexpr int kGroupsPerChunk = kChunkBytes / kGroupBytes;
@@ -50,24 +54,20 @@ struct PhaseBrief {
     int rows, in_dim;
 };
 
-// Per-warp ring cursors, kept in shared memory between phases.
+// Consumer cursor of one warp's ring, kept in shared memory between phases.
 struct RingState {
-    const uint8_t* src;   // start of this warp's rows in the phase being issued
-    long long off;        // bytes of that range already issued
-    long long bytes;      // size of that range (-1: not computed yet)
-    int ip;               // phase being issued
-    int issued;           // chunks issued so far
-    int islot;            // slot of the next chunk to issue
     int consumed;         // chunks consumed so far
     int cslot;            // slot of the next chunk to consume
-    uint32_t cpar;        // mbarrier parity of that slot
+    uint32_t cpar;        // full-barrier parity of that slot
 };
 
 // Block-shared bookkeeping of the step kernel.
 struct StepShared {
     uint8_t* ring;        // [kSW][nslot][kChunkBytes]
     float* xs;            // GEMV input vector
-    uint64_t* full;       // [kSW][nslot] mbarriers
+    uint64_t* full;       // [kSW][nslot] mbarriers: slot filled (producer -> consumer)
+    uint64_t* empty;      // [kSW][nslot] mbarriers: slot released (consumer -> producer)
+    int issued[kSW];      // chunks the producer issued per consumer warp
     PhaseBrief* brief;    // [nphases]
     StepPhase* ph;        // staged descriptor of the current phase
     RingState rings[kSW];
@@ -86,7 +86,7 @@ static __host__ __device__ inline StepSmem step_smem_plan(int nslot, int xs_max,
     s.ring = 0;
     s.xs = (size_t)kSW * nslot * kChunkBytes;
     s.bars = s.xs + (((size_t)xs_max * 4 + 127) / 128) * 128;
-    s.brief = s.bars + (((size_t)kSW * nslot * 8 + 15) / 16) * 16;
+    s.brief = s.bars + (((size_t)2 * kSW * nslot * 8 + 15) / 16) * 16;
     s.phase = s.brief + (((size_t)nphases * sizeof(PhaseBrief) + 127) / 128) * 128;
     s.total = s.phase + ((sizeof(StepPhase) + 127) / 128) * 128;
     return s;
@@ -124,73 +124,76 @@ __device__ __forceinline__ void trace_mark(const StepParams& sp, int c, int p, i
         sp.trace[((size_t)c * sp.nphases + p) * 8 + k] = (long long)globaltimer_ns();
 }
 
-// Issue bulk copies of this warp's weight stream (register copy r of its cursors) until
-// `limit` chunks are issued. All lanes run it (uniform values); lane 31 issues.
-__device__ __forceinline__ void ring_issue(RingState& r, const StepShared& S, const StepParams& sp, int c,
-                                           int nc, int limit) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nslot = sp.nslot;
-    uint8_t* my_ring = S.ring + (size_t)warp * nslot * kChunkBytes;
-    uint64_t* my_full = S.full + warp * nslot;
-    while (r.issued < limit) {
-        while (r.ip < sp.nphases) {
-            if (r.bytes < 0) {
-                const PhaseBrief bf = S.brief[r.ip];
-                if (bf.W) {
-                    int a, b;
-                    warp_rows(bf.rows, c, nc, warp, a, b);
-                    r.bytes = (long long)(b - a) * bf.in_dim * 2;
-                    r.src = reinterpret_cast<const uint8_t*>(bf.W + (size_t)a * bf.in_dim);
-                } else {
-                    r.bytes = 0;
-                }
-                r.off = 0;
-            }
-            if (r.off < r.bytes) break;
-            ++r.ip;
-            r.bytes = -1;
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Barrier over the 256 consumer threads (named barrier 3); the producer warp is not in it.
+__device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 3, 256;" ::: "memory"); }
+
+// mbarrier wait that also gives up once another CTA has posted an error
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, const StepParams& sp, int err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (unsigned it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0 && step_aborted(sp)) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            post_error(sp.dev_err, err);
+            return false;
         }
-        if (r.ip >= sp.nphases) return;
-        const uint32_t len = (uint32_t)min((long long)kChunkBytes, r.bytes - r.off);
-        const int slot = r.islot;
-        if (++r.islot == nslot) r.islot = 0;
-        if (lane == 31) {
-            // Lane 31 issues, so that the lane-0 threads that fence and signal the grid
-            // barriers never have bulk copies of their own in flight.
-            // The slot was last read through the generic proxy by this warp.
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive_expect_tx(&my_full[slot], len);
-            // weights are read once per step: evict them first, keep activations, KV rows
-            // and partial results resident in L2
-            bulk_g2s_hint(my_ring + (size_t)slot * kChunkBytes, r.src + r.off, len, &my_full[slot],
-                          l2_policy_evict_first());
-        }
-        r.off += len;
-        ++r.issued;
     }
 }
 
-__device__ __noinline__ void ring_topup(StepShared& S, const StepParams sp, int c, int nc) {
-    const int warp = threadIdx.x >> 5;
-    RingState r = S.rings[warp];
-    ring_issue(r, S, sp, c, nc, r.consumed + sp.nslot);
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) S.rings[warp] = r;
-    __syncwarp();
+// Producer warp: lane w streams consumer warp w's rows of every GEMV phase of the step,
+// in phase order, into that warp's ring, refilling a slot as soon as it is released.
+__device__ __noinline__ void producer(StepShared& S, const StepParams sp, int c, int nc) {
+    const int w = threadIdx.x & 31;
+    if (w >= kSW) return;
+    const int nslot = sp.nslot;
+    uint8_t* ring = S.ring + (size_t)w * nslot * kChunkBytes;
+    uint64_t* full = S.full + w * nslot;
+    uint64_t* empty = S.empty + w * nslot;
+    const uint64_t pol = l2_policy_evict_first();
+    int issued = 0;
+    bool ok = true;
+    for (int p = 0; p < sp.nphases && ok; ++p) {
+        const PhaseBrief bf = S.brief[p];
+        if (!bf.W) continue;
+        int a, b;
+        warp_rows(bf.rows, c, nc, w, a, b);
+        const long long bytes = (long long)(b - a) * bf.in_dim * 2;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(bf.W + (size_t)a * bf.in_dim);
+        for (long long off = 0; off < bytes; off += kChunkBytes) {
+            const int slot = issued % nslot;
+            const uint32_t ph = (uint32_t)((issued / nslot) & 1);
+            if (!mbar_wait_or_abort(&empty[slot], ph ^ 1u, sp, DEV_GEMV_EMPTY_TIMEOUT)) {
+                ok = false;
+                break;
+            }
+            const uint32_t len = (uint32_t)min((long long)kChunkBytes, bytes - off);
+            mbar_arrive_expect_tx(&full[slot], len);
+            bulk_g2s_hint(ring + (size_t)slot * kChunkBytes, src + off, len, &full[slot], pol);
+            ++issued;
+        }
+    }
+    S.issued[w] = issued;
 }
 
-// Grid barrier: all CTAs finished phase p-1. Leaves S.abort CTA-uniform.
+// Grid barrier: all CTAs finished phase p-1 (acquire of the arrival counter, which every
+// CTA bumps with a release after its CTA barrier). Leaves S.abort CTA-uniform.
 __device__ __noinline__ void grid_wait(StepShared& S, const StepParams sp, int p, int c, int nc) {
     const int tid = threadIdx.x;
     if (tid == 0 && p > 0) {
         const unsigned long long target = (unsigned long long)p * nc;
-        const volatile unsigned long long* ctr = sp.bar;
-        if (*ctr < target) {
-            // Poll with a short sleep: ~150 CTAs spinning back-to-back on one L2 line
-            // would delay the arrivals (and every atomic near that line) they wait for.
+        if (ld_acquire_u64(sp.bar) < target) {
             const unsigned long long t0 = globaltimer_ns();
-            while (*ctr < target) {
-                __nanosleep(100);
+            while (ld_acquire_u64(sp.bar) < target) {
                 if (step_aborted(sp)) break;
                 if (globaltimer_ns() - t0 > kWaitLimitNs) {
                     post_error(sp.dev_err, DEV_STEP_BARRIER_TIMEOUT);
@@ -198,10 +201,9 @@ __device__ __noinline__ void grid_wait(StepShared& S, const StepParams sp, int p
                 }
             }
         }
-        __threadfence();
     }
     if (tid == 0) S.abort = step_aborted(sp) ? 1 : 0;
-    __syncthreads();
+    cta_sync();
     trace_mark(sp, c, p, 1);
 }
 
@@ -214,6 +216,13 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
     float* const y = ph.g.y;
     float* const xs = S.xs;
     const float eps = ph.g.eps;
+
+    // ---- norm weights do not depend on the previous phase: load them before the barrier
+    constexpr int kV = 4096 / (4 * kSThreads);  // float4 per thread: x_len <= 4096 (checked on the host)
+    float4 wv[kV];
+    if (pro == PRO_RMSNORM || pro == PRO_EMBED_RMSNORM) load_vec4<kV>(ph.g.norm_w, xlen, tid, kSThreads, wv);
+    grid_wait(S, sp, p, c, nc);
+    if (S.abort) return;
 
     // ---- prologue: x into shared memory, every load issued before any use
     if (pro == PRO_GATED_NORM) {
@@ -246,7 +255,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
                 if (i < D) xs[(size_t)h * D + i] = wv4[k] * (ov[k] * inv) * silu_f(zv[k]);
             }
         }
-        __syncthreads();
+        cta_sync();
     } else {
         const float* src = ph.g.x;
         if (pro == PRO_EMBED_RMSNORM) {
@@ -262,11 +271,10 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
                 xs[i] = v;
                 if (c == 0) hout[i] = v;
             }
-            __syncthreads();
+            cta_sync();
             src = xs;
         }
-        // x (and the norm weight) in registers: one round trip per 4096 elements
-        constexpr int kV = 4;
+        // x in registers: one round trip per kV * 4 * kSThreads elements
         const int n4 = xlen >> 2;
         float4* xs4 = reinterpret_cast<float4*>(xs);
         if (pro == PRO_PLAIN) {
@@ -280,9 +288,8 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
                 }
             }
         } else {  // RMSNORM (xlen <= 4096: checked when the phases are built)
-            float4 xv[kV], wv[kV];
+            float4 xv[kV];
             load_vec4<kV>(src, xlen, tid, kSThreads, xv);
-            load_vec4<kV>(ph.g.norm_w, xlen, tid, kSThreads, wv);
             double ss = 0.0;
 #pragma unroll
             for (int k = 0; k < kV; ++k)
@@ -291,7 +298,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             if (lane == 0) S.red_d[warp] = ss;
-            __syncthreads();
+            cta_sync();
             ss = 0.0;
 #pragma unroll
             for (int w = 0; w < kSW; ++w) ss += S.red_d[w];
@@ -309,7 +316,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
                 }
             }
         }
-        __syncthreads();
+        cta_sync();
     }
     trace_mark(sp, c, p, 2);
 
@@ -321,6 +328,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
     const int nslot = sp.nslot;
     const uint8_t* my_ring = S.ring + (size_t)warp * nslot * kChunkBytes;
     uint64_t* my_full = S.full + warp * nslot;
+    uint64_t* my_empty = S.empty + warp * nslot;
     float best = -INFINITY;
     int best_idx = 0x7fffffff;
     int row = a;
@@ -354,7 +362,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
     };
     auto next_chunk = [&](const uint4*& wv) -> bool {
         const unsigned long long tw = sp.trace ? globaltimer_ns() : 0ull;
-        if (!mbar_wait_bounded(&my_full[r.cslot], r.cpar, sp.dev_err, DEV_GEMV_FULL_TIMEOUT)) return false;
+        if (!mbar_wait_or_abort(&my_full[r.cslot], r.cpar, sp, DEV_GEMV_FULL_TIMEOUT)) return false;
         if (sp.trace) {
             waited_ns += (long long)(globaltimer_ns() - tw);
             ++nchunks;
@@ -363,10 +371,10 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
         return true;
     };
     auto release_chunk = [&]() {
+        __syncwarp();  // every lane's reads of the slot are done
+        if (lane == 0) mbar_arrive(&my_empty[r.cslot]);
         ++r.consumed;
         if (++r.cslot == nslot) { r.cslot = 0; r.cpar ^= 1u; }
-        __syncwarp();
-        ring_issue(r, S, sp, c, nc, r.consumed + nslot);
     };
     // Specialised stream: GPR groups per row, x (XG groups) in registers. Chunks hold 8
     // groups and start on a row boundary (GPR divides 8), so each group's x slice,
@@ -483,7 +491,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
         // CTA argmax (larger wins, ties -> lower index), then the grid ticket
         const GemvParams& g = ph.g;
         if (lane == 0) { S.rv[warp] = best; S.ri[warp] = best_idx; }
-        __syncthreads();
+        cta_sync();
         if (tid == 0) {
             float bv = S.rv[0];
             int bi = S.ri[0];
@@ -494,7 +502,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
             __threadfence();
             S.s_last = (atomicAdd(g.am_counter, 1u) == (unsigned)nc - 1) ? 1 : 0;
         }
-        __syncthreads();
+        cta_sync();
         if (S.s_last) {
             __threadfence();
             float bv = -INFINITY;
@@ -510,9 +518,9 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
             }
-            __syncthreads();
+            cta_sync();
             if (lane == 0) { S.rv[warp] = bv; S.ri[warp] = bi; }
-            __syncthreads();
+            cta_sync();
             if (tid == 0) {
                 bv = S.rv[0];
                 bi = S.ri[0];
@@ -559,56 +567,41 @@ __device__ __noinline__ void attn_phase(StepShared& S, const StepParams sp, int 
     const AttnDecodeParams at = S.ph->a;
     const int items = at.NKV * at.nsplit;
     long long* marks = sp.trace ? sp.trace + ((size_t)c * sp.nphases + p) * 8 + 4 : nullptr;
+    if (threadIdx.x >= kAttnThreads) return;  // the item runs on warps 0-7
     for (int it = c; it < items; it += nc) attn_decode_item<GRP>(at, it % at.NKV, it / at.NKV, marks);
 }
 
-__device__ __noinline__ void ring_drain(StepShared& S, const StepParams sp) {
-    // Every issued copy has been consumed on the normal path; after an error, wait
-    // (bounded) for the copies still in flight before the CTA may exit.
-    const int warp = threadIdx.x >> 5;
-    RingState r = S.rings[warp];
-    uint64_t* my_full = S.full + warp * sp.nslot;
-    bool ok = true;
-    for (int k = r.consumed; k < r.issued && ok; ++k) {
-        ok = mbar_wait_bounded(&my_full[r.cslot], r.cpar, sp.dev_err, DEV_GEMV_DRAIN_TIMEOUT);
-        if (++r.cslot == sp.nslot) { r.cslot = 0; r.cpar ^= 1u; }
-    }
-}
-
 template <int GRP>
-__global__ void __launch_bounds__(kSThreads, 1) k_decode_step(const StepParams sp) {
+__global__ void __launch_bounds__(kBlockThreads, 1) k_decode_step(const StepParams sp) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ StepShared S;
     const int tid = threadIdx.x;
     const int c = blockIdx.x, nc = gridDim.x;
     const StepSmem plan = step_smem_plan(sp.nslot, sp.xs_max, sp.nphases);
+    const int nbar = kSW * sp.nslot;
 
     if (tid == 0) {
         S.ring = smem;
         S.xs = reinterpret_cast<float*>(smem + plan.xs);
         S.full = reinterpret_cast<uint64_t*>(smem + plan.bars);
+        S.empty = S.full + nbar;
         S.brief = reinterpret_cast<PhaseBrief*>(smem + plan.brief);
         S.ph = reinterpret_cast<StepPhase*>(smem + plan.phase);
         S.abort = 0;
     }
     if (tid < kSW) {
         RingState r;
-        r.src = nullptr;
-        r.off = 0;
-        r.bytes = -1;
-        r.ip = 0;
-        r.issued = 0;
-        r.islot = 0;
         r.consumed = 0;
         r.cslot = 0;
         r.cpar = 0;
         S.rings[tid] = r;
+        S.issued[tid] = 0;
     }
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.bars);
-    if (tid < kSW * sp.nslot) mbar_init(&full[tid], 1);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.bars);
+    for (int q = tid; q < 2 * nbar; q += kBlockThreads) mbar_init(&bars[q], 1);
     if (tid == 0) fence_mbar_init();
     PhaseBrief* brief = reinterpret_cast<PhaseBrief*>(smem + plan.brief);
-    for (int q = tid; q < sp.nphases; q += kSThreads) {
+    for (int q = tid; q < sp.nphases; q += kBlockThreads) {
         const StepPhase& g = sp.phases[q];
         PhaseBrief bf;
         bf.W = g.type == PH_GEMV ? g.g.W : nullptr;
@@ -618,35 +611,48 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode_step(const StepParams s
     }
     __syncthreads();
 
-    StepPhase* ph = reinterpret_cast<StepPhase*>(smem + plan.phase);
-    for (int p = 0; p < sp.nphases; ++p) {
-        trace_mark(sp, c, p, 0);
-        // stage this phase's descriptor (the previous phase ended with a CTA barrier)
-        {
-            const int4* src = reinterpret_cast<const int4*>(sp.phases + p);
-            int4* dst = reinterpret_cast<int4*>(ph);
-            for (int q = tid; q < (int)(sizeof(StepPhase) / 16); q += kSThreads) dst[q] = src[q];
-        }
-        ring_topup(S, sp, c, nc);  // keep HBM busy across the barrier
-        __syncthreads();
-        const int type = ph->type;
-        if (type == PH_GDN) {
-            gdn_phase(S, sp, p, c, nc);
-        } else {
-            grid_wait(S, sp, p, c, nc);
-            if (type == PH_ATTN) attn_phase<GRP>(S, sp, p, c, nc);
-            else if (!S.abort) gemv_phase(S, sp, p, c, nc);
-        }
-        trace_mark(sp, c, p, 3);
-        if (p + 1 < sp.nphases) {
-            __syncthreads();  // (also ends every read of the staged descriptor)
-            if (tid == 0) {
-                __threadfence();
-                atomicAdd(sp.bar, 1ull);
+    if (tid >= kSThreads) {
+        producer(S, sp, c, nc);
+    } else {
+        StepPhase* ph = reinterpret_cast<StepPhase*>(smem + plan.phase);
+        for (int p = 0; p < sp.nphases; ++p) {
+            trace_mark(sp, c, p, 0);
+            // stage this phase's descriptor (the previous phase ended with a CTA barrier)
+            {
+                const int4* src = reinterpret_cast<const int4*>(sp.phases + p);
+                int4* dst = reinterpret_cast<int4*>(ph);
+                for (int q = tid; q < (int)(sizeof(StepPhase) / 16); q += kSThreads) dst[q] = src[q];
+            }
+            cta_sync();
+            const int type = ph->type;
+            if (type == PH_GDN) {
+                gdn_phase(S, sp, p, c, nc);
+            } else if (type == PH_ATTN) {
+                grid_wait(S, sp, p, c, nc);
+                attn_phase<GRP>(S, sp, p, c, nc);
+            } else {
+                gemv_phase(S, sp, p, c, nc);  // waits for the grid after its weight-only loads
+            }
+            trace_mark(sp, c, p, 3);
+            if (p + 1 < sp.nphases) {
+                cta_sync();  // (also ends every read of the staged descriptor)
+                if (tid == 0) red_release_add_u64(sp.bar, 1ull);  // orders this CTA's writes before it
             }
         }
     }
-    ring_drain(S, sp);
+    __syncthreads();
+    // After an error, copies the producer issued may still be in flight: wait for them
+    // (bounded) before the CTA exits. On the normal path every issued copy was consumed.
+    if (tid >= kSThreads && tid - kSThreads < kSW) {
+        const int w = tid - kSThreads;
+        const RingState r = S.rings[w];
+        int slot = r.cslot;
+        uint32_t par = r.cpar;
+        for (int k = r.consumed; k < S.issued[w]; ++k) {
+            if (!mbar_wait_bounded(&S.full[w * sp.nslot + slot], par, sp.dev_err, DEV_GEMV_DRAIN_TIMEOUT)) break;
+            if (++slot == sp.nslot) { slot = 0; par ^= 1u; }
+        }
+    }
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -676,7 +682,7 @@ static cudaError_t launch_step_t(const StepParams& sp, int grid, cudaStream_t s)
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kSThreads);
+    cfg.blockDim = dim3(kBlockThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -701,7 +707,7 @@ template <int GRP>
 static int max_grid_t(size_t smem) {
     int per_sm = 0;
     cudaFuncSetAttribute(k_decode_step<GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_step<GRP>, kSThreads, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_step<GRP>, kBlockThreads, smem) != cudaSuccess)
         return 0;
     return per_sm >= 1 ? num_sms() : 0;  // one CTA per SM
 }

@@ -743,9 +743,8 @@ static int setup_persistent(qwc_handle* h) {
     std::vector<StepPhase> phases;
     make_phases(h, h->st, nsplit, phases, h->step_kinds);
     const int np = (int)phases.size();
-    // Ring depth: two or three 4 KB slots per warp (64-96 KB per SM) already sustain
-    // full HBM bandwidth; deeper rings only queue latency-critical loads (barrier polls,
-    // activations, KV rows) behind prefetched weights.
+    // Ring depth: three 4 KB slots per consumer warp (96 KB per SM) measured fastest with
+    // the producer warp; deeper rings queue latency-critical loads behind weights.
     int nslot = std::min(step_slots(xs_max, grp, np), 3);
     if (const char* e = std::getenv("QWC_STEP_SLOTS")) nslot = std::max(2, std::min(step_slots(xs_max, grp, np), std::atoi(e)));
     const int grid = decode_step_max_grid(grp, nslot, xs_max, np);

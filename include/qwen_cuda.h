@@ -215,7 +215,8 @@ int qwc_profile_step(qwc_handle* h, int cap, int* kind, float* ms, int64_t* byte
  * at the current position, recording device timestamps (ns) per CTA and phase. out
  * receives: [0] grid size G, [1] phase count P, [2..2+P) the QWC_K_* kind of each phase,
  * then G*P*8 values, CTA-major, phase-minor: stamps of phase start, barrier passed,
- * GEMV prologue done, phase end; then for GEMV phases the ns spent waiting on weight
+ * GEMV prologue done, phase end (every warp of the CTA done, just before it arrives at
+ * the next grid barrier); then for GEMV phases the ns warp 0 spent waiting on weight
  * slots and the slot count, for attention phases stamps after its prologue, main loop,
  * warp merge and split combine.
  * Returns the number of int64 values needed (when cap is too small nothing runs), or an

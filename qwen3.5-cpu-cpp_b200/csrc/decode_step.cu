@@ -207,6 +207,190 @@ __device__ __noinline__ void grid_wait(StepShared& S, const StepParams sp, int p
     trace_mark(sp, c, p, 1);
 }
 
+// ---------------------------------------------------------------------- GEMV streams
+// One warp's weight stream of a GEMV phase: read-only context and the cursor state that
+// persists across phases. The stream functions are separate non-inlined templates (one
+// per epilogue / shape) so that each gets its own register allocation; they copy what
+// they need into registers on entry and write the state back on exit.
+struct StreamCtx {
+    const uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    const float* xs;
+    float* y;
+    int nslot, b, bytes, in, xlen;
+    bool trace;
+};
+struct StreamState {
+    RingState r;
+    int row, res_base;
+    float res, best;
+    int best_idx;
+    long long waited_ns;
+    int nchunks;
+};
+
+// Registers of a stream: the cursor and the epilogue state.
+struct StreamRegs {
+    const uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    float* y;
+    int nslot, b, lane;
+    bool trace;
+    RingState r;
+    int row, res_base;
+    float res, best;
+    int best_idx;
+    long long waited_ns;
+    int nchunks;
+
+    __device__ __forceinline__ StreamRegs(const StreamCtx& cx, const StreamState& st) {
+        ring = cx.ring; full = cx.full; empty = cx.empty; y = cx.y;
+        nslot = cx.nslot; b = cx.b; trace = cx.trace; lane = threadIdx.x & 31;
+        r = st.r; row = st.row; res_base = st.res_base; res = st.res; best = st.best;
+        best_idx = st.best_idx; waited_ns = st.waited_ns; nchunks = st.nchunks;
+    }
+    __device__ __forceinline__ void save(StreamState& st) const {
+        st.r = r; st.row = row; st.res_base = res_base; st.res = res; st.best = best;
+        st.best_idx = best_idx; st.waited_ns = waited_ns; st.nchunks = nchunks;
+    }
+    __device__ __forceinline__ bool next_chunk(const uint4*& wv, const StepParams& sp) {
+        const unsigned long long tw = trace ? globaltimer_ns() : 0ull;
+        if (!mbar_wait_or_abort(&full[r.cslot], r.cpar, sp, DEV_GEMV_FULL_TIMEOUT)) return false;
+        if (trace) {
+            waited_ns += (long long)(globaltimer_ns() - tw);
+            ++nchunks;
+        }
+        wv = reinterpret_cast<const uint4*>(ring + (size_t)r.cslot * kChunkBytes);
+        return true;
+    }
+    __device__ __forceinline__ void release_chunk() {
+        __syncwarp();  // every lane's reads of the slot are done
+        if (lane == 0) mbar_arrive(&empty[r.cslot]);
+        ++r.consumed;
+        if (++r.cslot == nslot) { r.cslot = 0; r.cpar ^= 1u; }
+    }
+    // epilogue of one finished row (lane 0 stores); residuals prefetched 32 rows at a time
+    template <int EPI>
+    __device__ __forceinline__ void finish_row(float sum, float su) {
+        float resv = 0.f;
+        if constexpr (EPI == EPI_RESIDUAL) {
+            if (row - res_base >= 32) {
+                res_base += 32;
+                res = (res_base + lane < b) ? y[res_base + lane] : 0.f;
+            }
+            resv = __shfl_sync(0xffffffffu, res, row - res_base);
+        }
+        if (lane == 0) {
+            if constexpr (EPI == EPI_STORE) y[row] = sum;
+            else if constexpr (EPI == EPI_RESIDUAL) y[row] = resv + sum;
+            else if constexpr (EPI == EPI_SWIGLU) y[row] = silu_f(sum) * su;
+            else {
+                y[row] = sum;
+                if (sum > best) { best = sum; best_idx = row; }
+            }
+        }
+        ++row;
+    }
+};
+
+// Specialised stream: GPR groups per row, x (XG groups of 256) in registers. Chunks hold 8
+// groups and start on a row boundary (GPR divides 8), so each group's x slice, gate/up
+// half and row end are compile-time.
+template <int EPI, int GPR, int XG>
+__device__ __noinline__ void stream_fast_fn(const StreamCtx& cx, StreamState& state, const StepParams sp) {
+    StreamRegs R(cx, state);
+    const int lane = R.lane;
+    const int bytes = cx.bytes;
+    float xr[XG][8];
+#pragma unroll
+    for (int k = 0; k < XG; ++k) {
+        const float4 v0 = *reinterpret_cast<const float4*>(cx.xs + k * 256 + lane * 8);
+        const float4 v1 = *reinterpret_cast<const float4*>(cx.xs + k * 256 + lane * 8 + 4);
+        xr[k][0] = v0.x; xr[k][1] = v0.y; xr[k][2] = v0.z; xr[k][3] = v0.w;
+        xr[k][4] = v1.x; xr[k][5] = v1.y; xr[k][6] = v1.z; xr[k][7] = v1.w;
+    }
+    float acc = 0.f, acc_u = 0.f;
+    for (int off = 0; off < bytes; off += kChunkBytes) {
+        const uint4* wv;
+        if (!R.next_chunk(wv, sp)) break;
+        const int ng = min(kChunkBytes, bytes - off) / kGroupBytes;
+        uint4 w[kGroupsPerChunk];
+#pragma unroll
+        for (int gi = 0; gi < kGroupsPerChunk; ++gi)
+            w[gi] = gi < ng ? wv[gi * 32 + lane] : make_uint4(0u, 0u, 0u, 0u);
+        float pt[kGroupsPerChunk];
+#pragma unroll
+        for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
+            const float* xx = xr[gi % XG];
+            float d = 0.f;
+            d = fmaf(bf16lo(w[gi].x), xx[0], d);
+            d = fmaf(bf16hi(w[gi].x), xx[1], d);
+            d = fmaf(bf16lo(w[gi].y), xx[2], d);
+            d = fmaf(bf16hi(w[gi].y), xx[3], d);
+            d = fmaf(bf16lo(w[gi].z), xx[4], d);
+            d = fmaf(bf16hi(w[gi].z), xx[5], d);
+            d = fmaf(bf16lo(w[gi].w), xx[6], d);
+            d = fmaf(bf16hi(w[gi].w), xx[7], d);
+            pt[gi] = d;
+        }
+#pragma unroll
+        for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
+            if (gi < ng) {
+                const int qq = gi % GPR;  // position of the group in its row
+                if (EPI == EPI_SWIGLU && qq >= XG) acc_u += pt[gi];
+                else acc += pt[gi];
+                if (qq == GPR - 1) {
+                    const float sum = warp_sum(acc);
+                    const float su = EPI == EPI_SWIGLU ? warp_sum(acc_u) : 0.f;
+                    R.template finish_row<EPI>(sum, su);
+                    acc = 0.f;
+                    acc_u = 0.f;
+                }
+            }
+        }
+        R.release_chunk();
+    }
+    R.save(state);
+}
+
+// Generic stream: x from shared memory, row position tracked at run time.
+template <int EPI>
+__device__ __noinline__ void stream_generic_fn(const StreamCtx& cx, StreamState& state, const StepParams sp) {
+    StreamRegs R(cx, state);
+    const int lane = R.lane;
+    const int bytes = cx.bytes, xlen = cx.xlen;
+    const float* xs = cx.xs;
+    const int gpr = cx.in >> 8;
+    int q = 0;
+    float acc = 0.f, acc_u = 0.f;
+    for (int off = 0; off < bytes; off += kChunkBytes) {
+        const uint4* wv;
+        if (!R.next_chunk(wv, sp)) break;
+        const int ng = min(kChunkBytes, bytes - off) / kGroupBytes;
+#pragma unroll 4
+        for (int gi = 0; gi < ng; ++gi) {
+            const uint4 w = wv[gi * 32 + lane];
+            const int col = q * 256 + lane * 8;
+            if (EPI == EPI_SWIGLU && col >= xlen) acc_u = dot8s(w, xs + (col - xlen), acc_u);
+            else acc = dot8s(w, xs + col, acc);
+            if (q == gpr - 1) {
+                const float sum = warp_sum(acc);
+                const float su = EPI == EPI_SWIGLU ? warp_sum(acc_u) : 0.f;
+                R.template finish_row<EPI>(sum, su);
+                acc = 0.f;
+                acc_u = 0.f;
+                q = 0;
+            } else {
+                ++q;
+            }
+        }
+        R.release_chunk();
+    }
+    R.save(state);
+}
+
 // ---------------------------------------------------------------------- GEMV phase
 __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int p, int c, int nc) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -323,168 +507,50 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
     // ---- this warp's weight stream
     int a, b;
     warp_rows(ph.g.rows, c, nc, warp, a, b);
-    const int bytes = (b - a) * in * 2;
-    RingState r = S.rings[warp];
-    const int nslot = sp.nslot;
-    const uint8_t* my_ring = S.ring + (size_t)warp * nslot * kChunkBytes;
-    uint64_t* my_full = S.full + warp * nslot;
-    uint64_t* my_empty = S.empty + warp * nslot;
-    float best = -INFINITY;
-    int best_idx = 0x7fffffff;
-    int row = a;
-    int res_base = a;
-    float res = 0.f;
-    if (epi == EPI_RESIDUAL) res = (a + lane < b) ? y[a + lane] : 0.f;
-    long long waited_ns = 0;
-    int nchunks = 0;
-
-    // epilogue of one finished row (lane 0 stores); residuals prefetched 32 rows at a time
-    auto finish_row = [&](auto epi_tag, float sum, float su) {
-        constexpr int EPI = decltype(epi_tag)::value;
-        float resv = 0.f;
-        if constexpr (EPI == EPI_RESIDUAL) {
-            if (row - res_base >= 32) {
-                res_base += 32;
-                res = (res_base + lane < b) ? y[res_base + lane] : 0.f;
-            }
-            resv = __shfl_sync(0xffffffffu, res, row - res_base);
-        }
-        if (lane == 0) {
-            if constexpr (EPI == EPI_STORE) y[row] = sum;
-            else if constexpr (EPI == EPI_RESIDUAL) y[row] = resv + sum;
-            else if constexpr (EPI == EPI_SWIGLU) y[row] = silu_f(sum) * su;
-            else {
-                y[row] = sum;
-                if (sum > best) { best = sum; best_idx = row; }
-            }
-        }
-        ++row;
-    };
-    auto next_chunk = [&](const uint4*& wv) -> bool {
-        const unsigned long long tw = sp.trace ? globaltimer_ns() : 0ull;
-        if (!mbar_wait_or_abort(&my_full[r.cslot], r.cpar, sp, DEV_GEMV_FULL_TIMEOUT)) return false;
-        if (sp.trace) {
-            waited_ns += (long long)(globaltimer_ns() - tw);
-            ++nchunks;
-        }
-        wv = reinterpret_cast<const uint4*>(my_ring + (size_t)r.cslot * kChunkBytes);
-        return true;
-    };
-    auto release_chunk = [&]() {
-        __syncwarp();  // every lane's reads of the slot are done
-        if (lane == 0) mbar_arrive(&my_empty[r.cslot]);
-        ++r.consumed;
-        if (++r.cslot == nslot) { r.cslot = 0; r.cpar ^= 1u; }
-    };
-    // Specialised stream: GPR groups per row, x (XG groups) in registers. Chunks hold 8
-    // groups and start on a row boundary (GPR divides 8), so each group's x slice,
-    // gate/up half and row end are compile-time.
-    auto stream_fast = [&](auto epi_tag, auto gpr_tag, auto xg_tag) {
-        constexpr int EPI = decltype(epi_tag)::value;
-        constexpr int GPR = decltype(gpr_tag)::value;
-        constexpr int XG = decltype(xg_tag)::value;
-        float xr[XG][8];
-#pragma unroll
-        for (int k = 0; k < XG; ++k) {
-            const float4 v0 = *reinterpret_cast<const float4*>(xs + k * 256 + lane * 8);
-            const float4 v1 = *reinterpret_cast<const float4*>(xs + k * 256 + lane * 8 + 4);
-            xr[k][0] = v0.x; xr[k][1] = v0.y; xr[k][2] = v0.z; xr[k][3] = v0.w;
-            xr[k][4] = v1.x; xr[k][5] = v1.y; xr[k][6] = v1.z; xr[k][7] = v1.w;
-        }
-        float acc = 0.f, acc_u = 0.f;
-        for (int off = 0; off < bytes; off += kChunkBytes) {
-            const uint4* wv;
-            if (!next_chunk(wv)) return;
-            const int ng = min(kChunkBytes, bytes - off) / kGroupBytes;
-            uint4 w[kGroupsPerChunk];
-#pragma unroll
-            for (int gi = 0; gi < kGroupsPerChunk; ++gi)
-                w[gi] = gi < ng ? wv[gi * 32 + lane] : make_uint4(0u, 0u, 0u, 0u);
-            float pt[kGroupsPerChunk];
-#pragma unroll
-            for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
-                const float* xx = xr[gi % XG];
-                float d = 0.f;
-                d = fmaf(bf16lo(w[gi].x), xx[0], d);
-                d = fmaf(bf16hi(w[gi].x), xx[1], d);
-                d = fmaf(bf16lo(w[gi].y), xx[2], d);
-                d = fmaf(bf16hi(w[gi].y), xx[3], d);
-                d = fmaf(bf16lo(w[gi].z), xx[4], d);
-                d = fmaf(bf16hi(w[gi].z), xx[5], d);
-                d = fmaf(bf16lo(w[gi].w), xx[6], d);
-                d = fmaf(bf16hi(w[gi].w), xx[7], d);
-                pt[gi] = d;
-            }
-#pragma unroll
-            for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
-                if (gi < ng) {
-                    const int qq = gi % GPR;  // position of the group in its row
-                    if (EPI == EPI_SWIGLU && qq >= XG) acc_u += pt[gi];
-                    else acc += pt[gi];
-                    if (qq == GPR - 1) {
-                        const float sum = warp_sum(acc);
-                        const float su = EPI == EPI_SWIGLU ? warp_sum(acc_u) : 0.f;
-                        finish_row(epi_tag, sum, su);
-                        acc = 0.f;
-                        acc_u = 0.f;
-                    }
-                }
-            }
-            release_chunk();
-        }
-    };
-    // Generic stream: x from shared memory, row position tracked at run time.
-    auto stream_generic = [&](auto epi_tag) {
-        constexpr int EPI = decltype(epi_tag)::value;
-        const int gpr = in >> 8;
-        int q = 0;
-        float acc = 0.f, acc_u = 0.f;
-        for (int off = 0; off < bytes; off += kChunkBytes) {
-            const uint4* wv;
-            if (!next_chunk(wv)) return;
-            const int ng = min(kChunkBytes, bytes - off) / kGroupBytes;
-#pragma unroll 4
-            for (int gi = 0; gi < ng; ++gi) {
-                const uint4 w = wv[gi * 32 + lane];
-                const int col = q * 256 + lane * 8;
-                if (EPI == EPI_SWIGLU && col >= xlen) acc_u = dot8s(w, xs + (col - xlen), acc_u);
-                else acc = dot8s(w, xs + col, acc);
-                if (q == gpr - 1) {
-                    const float sum = warp_sum(acc);
-                    const float su = EPI == EPI_SWIGLU ? warp_sum(acc_u) : 0.f;
-                    finish_row(epi_tag, sum, su);
-                    acc = 0.f;
-                    acc_u = 0.f;
-                    q = 0;
-                } else {
-                    ++q;
-                }
-            }
-            release_chunk();
-        }
-    };
-    using I4 = std::integral_constant<int, 4>;
-    using I8 = std::integral_constant<int, 8>;
+    StreamCtx cx;
+    cx.ring = S.ring + (size_t)warp * sp.nslot * kChunkBytes;
+    cx.full = S.full + warp * sp.nslot;
+    cx.empty = S.empty + warp * sp.nslot;
+    cx.xs = xs;
+    cx.y = y;
+    cx.nslot = sp.nslot;
+    cx.b = b;
+    cx.bytes = (b - a) * in * 2;
+    cx.in = in;
+    cx.xlen = xlen;
+    cx.trace = sp.trace != nullptr;
+    StreamState st;
+    st.r = S.rings[warp];
+    st.row = a;
+    st.res_base = a;
+    st.res = (epi == EPI_RESIDUAL && a + lane < b) ? y[a + lane] : 0.f;
+    st.best = -INFINITY;
+    st.best_idx = 0x7fffffff;
+    st.waited_ns = 0;
+    st.nchunks = 0;
     const int gpr = in >> 8, xg = xlen >> 8;
-    auto run = [&](auto epi_tag) {
-        constexpr int EPI = decltype(epi_tag)::value;
-        if constexpr (EPI == EPI_SWIGLU) {
-            if (gpr == 8 && xg == 4) stream_fast(epi_tag, I8{}, I4{});
-            else stream_generic(epi_tag);
-        } else {
-            if (gpr == 4 && xg == 4) stream_fast(epi_tag, I4{}, I4{});
-            else stream_generic(epi_tag);
-        }
-    };
-    if (epi == EPI_STORE) run(std::integral_constant<int, EPI_STORE>{});
-    else if (epi == EPI_RESIDUAL) run(std::integral_constant<int, EPI_RESIDUAL>{});
-    else if (epi == EPI_SWIGLU) run(std::integral_constant<int, EPI_SWIGLU>{});
-    else run(std::integral_constant<int, EPI_ARGMAX>{});
+    const bool fast = (epi == EPI_SWIGLU) ? (gpr == 8 && xg == 4) : (gpr == 4 && xg == 4);
+    switch (epi) {
+        case EPI_STORE:
+            fast ? stream_fast_fn<EPI_STORE, 4, 4>(cx, st, sp) : stream_generic_fn<EPI_STORE>(cx, st, sp);
+            break;
+        case EPI_RESIDUAL:
+            fast ? stream_fast_fn<EPI_RESIDUAL, 4, 4>(cx, st, sp) : stream_generic_fn<EPI_RESIDUAL>(cx, st, sp);
+            break;
+        case EPI_SWIGLU:
+            fast ? stream_fast_fn<EPI_SWIGLU, 8, 4>(cx, st, sp) : stream_generic_fn<EPI_SWIGLU>(cx, st, sp);
+            break;
+        default:
+            fast ? stream_fast_fn<EPI_ARGMAX, 4, 4>(cx, st, sp) : stream_generic_fn<EPI_ARGMAX>(cx, st, sp);
+            break;
+    }
+    const float best = st.best;
+    const int best_idx = st.best_idx;
     __syncwarp();
-    if (lane == 0) S.rings[warp] = r;
+    if (lane == 0) S.rings[warp] = st.r;
     if (sp.trace && tid == 0) {
-        sp.trace[((size_t)c * sp.nphases + p) * 8 + 4] = waited_ns;
-        sp.trace[((size_t)c * sp.nphases + p) * 8 + 5] = nchunks;
+        sp.trace[((size_t)c * sp.nphases + p) * 8 + 4] = st.waited_ns;
+        sp.trace[((size_t)c * sp.nphases + p) * 8 + 5] = st.nchunks;
     }
 
     if (epi == EPI_ARGMAX) {
@@ -633,11 +699,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) k_decode_step(const StepPara
             } else {
                 gemv_phase(S, sp, p, c, nc);  // waits for the grid after its weight-only loads
             }
+            cta_sync();  // every warp is done (also ends every read of the staged descriptor)
             trace_mark(sp, c, p, 3);
-            if (p + 1 < sp.nphases) {
-                cta_sync();  // (also ends every read of the staged descriptor)
-                if (tid == 0) red_release_add_u64(sp.bar, 1ull);  // orders this CTA's writes before it
-            }
+            if (p + 1 < sp.nphases && tid == 0) red_release_add_u64(sp.bar, 1ull);  // orders this CTA's writes before it
         }
     }
     __syncthreads();

@@ -247,6 +247,13 @@ int qwc_create_tp(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensor
 int qwc_create_from_dir_tp(const char* model_dir, int max_context, int kv_dtype, int device, int rank,
                            int world, const void* unique_id, qwc_handle** out);
 
+/* After qwc_prefill on a tensor-parallel group: gathers every rank's shard of the decode
+ * state (GDN state and conv ring of its heads, KV of its kv heads for the T prefilled
+ * positions) into `full`, a single-GPU handle of the same model on rank 0's device, over
+ * the group's NCCL communicator; `full` then decodes from position T (qwc_step).
+ * Collective: every rank calls it, rank 0 with `full`, the others with NULL. */
+int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full);
+
 /* ---------------------------------------------------------------- kernel level */
 
 /* matmul(const WeightView&, ...) (src/forward_pass.cpp:65-75) on device memory:

@@ -29,6 +29,7 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
            "qwc_gemv_bf16", "qwc_gemm_bf16",
            "qwc_tp_shard_of", "qwc_tp_unique_id", "qwc_create_tp", "qwc_create_from_dir_tp",
+           "qwc_tp_gather_state",
            "qwc_gdn_decode_step", "qwc_gdn_prefill", "qwc_gdn_prefill_workspace",
            "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
@@ -275,6 +276,13 @@ class Model:
         G, P = int(buf[0]), int(buf[1])
         kinds = [KERNEL_KINDS[int(k)] for k in buf[2:2 + P]]
         return kinds, buf[2 + P:].reshape(G, P, 8)
+
+    def tp_gather_state(self, full: "Model | None"):
+        """qwc_tp_gather_state: collective over the tensor-parallel group; rank 0 passes
+        its single-GPU Model, which then continues decoding after the prefilled prompt."""
+        fn = lib().qwc_tp_gather_state
+        fn.argtypes = [C.c_void_p, C.c_void_p]
+        check(fn(self._h, full._h if full is not None else None), self._h)
 
     def prefill(self, ids, logits: bool = True):
         """Prefill that seeds the decode state; returns the last position's logits."""

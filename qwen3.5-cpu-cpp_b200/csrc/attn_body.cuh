@@ -273,7 +273,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     auto gate_of = [&](int h) -> float {
         return decode ? p.proj[(size_t)h * HD2 + kHD + t] : p.gate_in[(size_t)h * kHD + t];
     };
-    if (n_act == 1) {
+    if (n_act == 1 && !p.defer_combine) {
 #pragma unroll
         for (int g = 0; g < GRP; ++g) {
             const int h = kv * GRP + g;
@@ -291,6 +291,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
             p.part_ml[(pbase + g) * 2 + 1] = cl[g];
         }
     }
+    if (p.defer_combine) return;  // the next phase combines (after its grid barrier)
     // publish: every thread's partial is ordered before thread 0's release fence by the
     // CTA barrier; the CTA that takes the last ticket fences again before reading
     attn_sync();

@@ -409,7 +409,40 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
     if (S.abort) return;
 
     // ---- prologue: x into shared memory, every load issued before any use
-    if (pro == PRO_GATED_NORM) {
+    if (pro == PRO_ATTN_COMBINE) {
+        // The attention phase left one partial (max, sum, unnormalised output) per split;
+        // warp h combines q head h (lane l: dims 8l..8l+7) exactly as the split-K combine
+        // of the attention kernel does, then applies the sigmoid gate.
+        const GemvParams& g = ph.g;
+        const int grp = g.nq / g.nkv;
+        const int n_ctx = *g.pos + 1;
+        int n_act = (n_ctx + kMinChunk - 1) / kMinChunk;
+        if (n_act > g.nsplit) n_act = g.nsplit;
+        for (int h = warp; h < g.nq; h += kSW) {
+            const int kv = h / grp, gg = h % grp;
+            const float* gt = g.x + (size_t)h * 2 * kHD + kHD + lane * 8;  // gate of head h
+            const float4 ga = *reinterpret_cast<const float4*>(gt), gb = *reinterpret_cast<const float4*>(gt + 4);
+            float M = -INFINITY;
+            for (int s2 = 0; s2 < n_act; ++s2)
+                M = fmaxf(M, __ldcg(&g.part_ml[((size_t)(kv * g.nsplit + s2) * grp + gg) * 2]));
+            float L = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+            for (int s2 = 0; s2 < n_act; ++s2) {
+                const size_t pi = (size_t)(kv * g.nsplit + s2) * grp + gg;
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(g.part_ml) + pi);
+                const float4* po = reinterpret_cast<const float4*>(g.part_o + pi * kHD + lane * 8);
+                const float4 va = __ldcg(po), vb = __ldcg(po + 1);
+                const float f = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
+                L += ml.y * f;
+                o[0] += va.x * f; o[1] += va.y * f; o[2] += va.z * f; o[3] += va.w * f;
+                o[4] += vb.x * f; o[5] += vb.y * f; o[6] += vb.z * f; o[7] += vb.w * f;
+            }
+            const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xs[(size_t)h * kHD + lane * 8 + e] = (o[e] / L) * sigmoid_f(gv[e]);
+        }
+        cta_sync();
+    } else if (pro == PRO_GATED_NORM) {
         // one warp per head of gn_dim values: w * (o * inv_head) * silu(z)
         const int D = ph.g.gn_dim, nh = xlen / D;
         const float* x0 = ph.g.x;

@@ -514,7 +514,7 @@ struct StepProfile {
 // The decode step as a list of phases (one per kernel of the per-kernel path, one per
 // grid-barrier phase of the persistent kernel), with the profiling kind of each.
 static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std::vector<StepPhase>& out,
-                        std::vector<int>& kinds) {
+                        std::vector<int>& kinds, bool defer_attn = false) {
     const int H = h->H;
     out.clear();
     kinds.clear();
@@ -572,6 +572,7 @@ static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std
             a.rot = h->ROT;
             a.nsplit = attn_nsplit;
             a.eps = h->eps;
+            a.defer_combine = defer_attn ? 1 : 0;
             out.push_back(ph);
             kinds.push_back(QWC_K_ATTN);
             GemvParams o = gp_base(h);
@@ -581,7 +582,18 @@ static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std
             o.x_len = lw.out_in;
             o.x = h->mix;
             o.y = h->hidden;
-            gemv(PRO_PLAIN, EPI_RESIDUAL, o, QWC_K_MIX_OUT);
+            int opro = PRO_PLAIN;
+            if (defer_attn) {  // o_proj combines the attention partials in its prologue
+                opro = PRO_ATTN_COMBINE;
+                o.x = h->proj;  // the gates
+                o.part_o = h->part_o;
+                o.part_ml = h->part_ml;
+                o.pos = h->pos;
+                o.nsplit = attn_nsplit;
+                o.nq = h->NQ;
+                o.nkv = h->NKV;
+            }
+            gemv(opro, EPI_RESIDUAL, o, QWC_K_MIX_OUT);
         } else {
             StepPhase ph;
             ph.type = PH_GDN;
@@ -741,7 +753,8 @@ static int setup_persistent(qwc_handle* h) {
     // attention items are spread one per CTA: at most grid / NKV splits
     const int nsplit = std::max(1, std::min(h->nsplit, grid0 / h->NKV));
     std::vector<StepPhase> phases;
-    make_phases(h, h->st, nsplit, phases, h->step_kinds);
+    // the o_proj phase combines the split attention partials when a warp per q head fits
+    make_phases(h, h->st, nsplit, phases, h->step_kinds, /*defer_attn=*/h->NQ <= 8);
     const int np = (int)phases.size();
     // Ring depth: three 4 KB slots per consumer warp (96 KB per SM) measured fastest with
     // the producer warp; deeper rings queue latency-critical loads behind weights.
@@ -1362,6 +1375,102 @@ extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_o
     CU(cudaMemcpyAsync(h->pos, &h->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, h->stream));
     CU(cudaStreamSynchronize(h->stream));
     h->pos_host = T;
+    return QWC_OK;
+}
+
+// After a tensor-parallel prefill: every rank sends its shard of the decode state (GDN
+// state and conv ring of its heads, the first T positions of its kv heads) to rank 0,
+// which places them into a single-GPU handle on the same device; that handle then
+// decodes from position T. Collective: every rank of the group calls it, rank 0 with its
+// single-GPU handle, the others with null. All ranks walk the pieces in the same order,
+// so the NCCL sends and receives pair up.
+extern "C" int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full) {
+    if (!tp || tp->tp_world < 2 || !tp->nccl)
+        return fail(tp, QWC_E_INVALID, "qwc_tp_gather_state: needs a tensor-parallel handle");
+    qwc_handle* h = tp;  // errors are reported on the tensor-parallel handle
+    const bool root = tp->tp_rank == 0;
+    const int T = tp->pos_host, W = tp->tp_world;
+    if (root) {
+        if (!full || full->tp_world != 1 || full->device != tp->device)
+            return fail(tp, QWC_E_INVALID, "qwc_tp_gather_state: rank 0 needs a single-GPU handle on its device");
+        if (full->H != tp->H || full->L != tp->L || full->KH != tp->gKH || full->VH != tp->gVH ||
+            full->NKV != tp->gNKV || full->NQ != tp->gNQ || full->kv_dtype != tp->kv_dtype)
+            return fail(tp, QWC_E_SHAPE, "qwc_tp_gather_state: the handles hold different models");
+        if (T > full->max_ctx) return fail(tp, QWC_E_CONTEXT, "qwc_tp_gather_state: prefix longer than max_context");
+    } else if (full) {
+        return fail(tp, QWC_E_INVALID, "qwc_tp_gather_state: only rank 0 passes a destination handle");
+    }
+    CU(cudaSetDevice(tp->device));
+    std::vector<qwc_tp_shard> sh(W);
+    for (int r = 0; r < W; ++r) {
+        int rc = qwc_tp_shard_of(&tp->cfg, r, W, &sh[r]);
+        if (rc) return rc;
+    }
+    const int DK = tp->DK, DV = tp->DV, HD = tp->HD, kvb = tp->kv_bytes;
+    const size_t hs = (size_t)DK * DV;  // one head of GDN state, floats
+    // one piece: bytes at src (on rank `from`) to dst (on rank 0)
+    int rc = QWC_OK;
+    auto piece = [&](int from, const void* src, void* dst, size_t bytes) {
+        if (rc || bytes == 0) return;
+        if (from == 0) {
+            if (root && cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, tp->stream) != cudaSuccess)
+                rc = fail(tp, QWC_E_CUDA, "qwc_tp_gather_state: copy failed");
+            return;
+        }
+        ncclResult_t r = ncclSuccess;
+        if (root) r = ncclRecv(dst, bytes, ncclUint8, from, tp->nccl, tp->stream);
+        else if (tp->tp_rank == from) r = ncclSend(src, bytes, ncclUint8, 0, tp->nccl, tp->stream);
+        if (r != ncclSuccess) rc = fail(tp, QWC_E_CUDA, std::string("qwc_tp_gather_state: ") + ncclGetErrorString(r));
+    };
+    const qwc_tp_shard& me = sh[tp->tp_rank];
+    ncclGroupStart();
+    for (int gi = 0; gi < tp->n_gdn; ++gi) {
+        for (int r = 0; r < W; ++r) {
+            const bool mine = r == tp->tp_rank;
+            // GDN state: the rank's v heads, one contiguous block
+            const float* s_src = mine ? tp->st.gdn_state + (size_t)gi * me.n_vh * hs : nullptr;
+            float* s_dst = root ? full->st.gdn_state + (size_t)gi * full->VH * hs + (size_t)sh[r].vh0 * hs : nullptr;
+            piece(r, s_src, s_dst, (size_t)sh[r].n_vh * hs * 4);
+            // conv ring [C][4]: q channels, k channels, v channels of the rank's heads
+            const size_t KDl = (size_t)sh[r].n_kh * DK, VDl = (size_t)sh[r].n_vh * DV, Cl = 2 * KDl + VDl;
+            const float* c_src = mine ? tp->st.conv_ring + (size_t)gi * Cl * 4 : nullptr;
+            float* c_dst = root ? full->st.conv_ring + (size_t)gi * full->C * 4 : nullptr;
+            const size_t q0 = (size_t)sh[r].kh0 * DK, k0 = (size_t)tp->gKD + q0,
+                         v0 = 2 * (size_t)tp->gKD + (size_t)sh[r].vh0 * DV;
+            piece(r, mine ? c_src : nullptr, root ? c_dst + q0 * 4 : nullptr, KDl * 16);
+            piece(r, mine ? c_src + KDl * 4 : nullptr, root ? c_dst + k0 * 4 : nullptr, KDl * 16);
+            piece(r, mine ? c_src + 2 * KDl * 4 : nullptr, root ? c_dst + v0 * 4 : nullptr, VDl * 16);
+        }
+    }
+    const size_t kvl_tp = (size_t)2 * tp->NKV * tp->max_ctx * HD * kvb;
+    const size_t kvl_full = root ? (size_t)2 * full->NKV * full->max_ctx * HD * kvb : 0;
+    for (int ai = 0; ai < tp->n_attn; ++ai) {
+        for (int which = 0; which < 2; ++which) {
+            for (int kv = 0; kv < tp->gNKV; ++kv) {
+                int from = -1;  // the first rank holding this kv head sends it
+                for (int r = 0; r < W && from < 0; ++r)
+                    if (kv >= sh[r].kv0 && kv < sh[r].kv0 + sh[r].n_kv) from = r;
+                const bool mine = from == tp->tp_rank;
+                const uint8_t* src = mine ? static_cast<const uint8_t*>(tp->st.kv) + kvl_tp * ai + which * (kvl_tp / 2) +
+                                                (size_t)(kv - me.kv0) * tp->max_ctx * HD * kvb
+                                          : nullptr;
+                uint8_t* dst = root ? static_cast<uint8_t*>(full->st.kv) + kvl_full * ai + which * (kvl_full / 2) +
+                                          (size_t)kv * full->max_ctx * HD * kvb
+                                    : nullptr;
+                piece(from, src, dst, (size_t)T * HD * kvb);
+            }
+        }
+    }
+    const ncclResult_t ge = ncclGroupEnd();
+    if (rc) return rc;
+    if (ge != ncclSuccess) return fail(tp, QWC_E_CUDA, std::string("qwc_tp_gather_state: ") + ncclGetErrorString(ge));
+    CU(cudaStreamSynchronize(tp->stream));
+    if (root) {
+        full->h_pin[4] = T;
+        CU(cudaMemcpyAsync(full->pos, &full->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, full->stream));
+        CU(cudaStreamSynchronize(full->stream));
+        full->pos_host = T;
+    }
     return QWC_OK;
 }
 

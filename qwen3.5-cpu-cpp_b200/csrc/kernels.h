@@ -17,6 +17,8 @@ enum GemvPro : int {
     PRO_RMSNORM = 1,      // x = rmsnorm(x_in) * (1 + w)            (forward_pass.cpp:77-84)
     PRO_EMBED_RMSNORM = 2,// x_in = embedding row of tokens[*pos]; CTA 0 stores it in hidden
     PRO_GATED_NORM = 3,   // x = w * (o * rsqrt(mean_head(o^2)+eps)) * silu(z)  (:86-93)
+    PRO_ATTN_COMBINE = 4, // x = the split-K attention partials combined, * sigmoid(gate)
+                          // (persistent step only; attn_step :134-150)
 };
 enum GemvEpi : int {
     EPI_STORE = 0,        // y[r] = acc
@@ -54,6 +56,11 @@ struct GemvParams {
     int max_ctx = 0;
     int slots_per_warp = 6;         // ring depth (set by the launcher)
     int* dev_err = nullptr;         // device error word (bounded waits, bad token)
+    // PRO_ATTN_COMBINE: partials of the attention phase (AttnDecodeParams with
+    // defer_combine), gate = x (the attention projection, [q | gate] per head), pos
+    const float* part_o = nullptr;
+    const float* part_ml = nullptr;
+    int nsplit = 1, nq = 0, nkv = 0;
 };
 
 size_t gemv_smem_bytes(const GemvParams& p);
@@ -102,6 +109,8 @@ struct AttnDecodeParams {
     float* out = nullptr;           // [NQ][HD]
     int NQ = 0, NKV = 0, rot = 64, nsplit = 1;
     float eps = 1e-6f;
+    int defer_combine = 0;          // every split only publishes its partial; the consumer
+                                    // of `out` combines them (PRO_ATTN_COMBINE)
 };
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t s, bool pdl);
 int attn_nsplit_for(int max_ctx);

@@ -70,3 +70,70 @@ def test_tp_prefill_matches_single_gpu_and_oracle(pkg, oracle, tmp_path, shape, 
     assert rel_l2(last, got[-1]) < 1e-5
     want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=True)
     assert rel_l2(got[-1], want.reshape(-1)[-s.vocab_size:]) < 2e-3
+
+
+def _gather_main(rank, world, port, d, ids, n_new, max_ctx, out_dir):
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    abi = __graft_entry__.load_package().abi
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        box = [abi.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        full = abi.Model(d, max_context=max_ctx, device=rank) if rank == 0 else None
+        m = abi.Model(d, max_context=max_ctx, device=rank, rank=rank, world=world, unique_id=box[0])
+        last = m.prefill(ids)
+        m.tp_gather_state(full)
+        if rank == 0:
+            assert full.position() == len(ids)
+            tok, toks, lgs = int(np.argmax(last)), [], []
+            for _ in range(n_new):
+                lg, am = full.step(tok)
+                lgs.append(lg)
+                toks.append(am)
+                tok = am
+            np.save(os.path.join(out_dir, "toks.npy"), np.array(toks))
+            np.save(os.path.join(out_dir, "lgs.npy"), np.stack(lgs))
+            np.save(os.path.join(out_dir, "last.npy"), last)
+            full.close()
+        dist.barrier()
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shape,world", [("tiny", 2), ("small-0.8b-widths", 2), ("small-0.8b-widths", 4)])
+def test_tp_prefill_then_decode_on_rank0(pkg, oracle, tmp_path, shape, world):
+    """Config 5's flow: tensor-parallel prefill, state gathered to rank 0, greedy decode
+    there; same tokens and logits as a single-GPU prefill + decode and as the oracle."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    T, n_new = 150, 12
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=23)
+    mp.start_processes(_gather_main, args=(world, _free_port(), d, ids, n_new, T + n_new + 8, str(tmp_path)),
+                       nprocs=world, start_method="spawn")
+    toks, lgs = np.load(tmp_path / "toks.npy"), np.load(tmp_path / "lgs.npy")
+    one = pkg.abi.Model(d, max_context=T + n_new + 8)
+    tok = int(np.argmax(one.prefill(ids)))
+    want_toks = []
+    for i in range(n_new):
+        lg, am = one.step(tok)
+        assert rel_l2(lgs[i], lg) < 1e-4, i
+        want_toks.append(am)
+        tok = am
+    one.close()
+    assert toks.tolist() == want_toks
+    orc = oracle.OracleModel(d, T + n_new + 8)
+    ref = None
+    for t in ids:
+        ref = orc.step(int(t))
+    tok = int(np.argmax(ref))
+    for i in range(n_new):
+        ref = orc.step(tok)
+        assert rel_l2(lgs[i], ref) < 2e-3, i
+        tok = int(np.argmax(ref))
+        assert tok == toks[i]

@@ -31,6 +31,15 @@ prompt tokens / device time (max over ranks). Roofline: tensor, the algorithmic 
 the forward pass (2 x projection parameters per token, causal attention
 4 NQ HD (t+1) per token per attention layer, GDN 7 DK DV per head per token per GDN layer,
 the lm_head for the last token) against the measured bf16 peak.
+
+--workload gdn-op / attn-op time the mixer ops of configs[1] and configs[2] through the
+kernel-level C ABI on device buffers: the GDN core (16 heads, 128/128, conv K=4; seeded
+N(0,1) inputs rounded to bf16 values, A_log ~ U(0, ln 16)) as a 4096-token chunked prefill
+(qwc_gdn_prefill) followed by 256 single-token steps (qwc_gdn_decode_step); the gated
+attention decode (8 q / 2 kv heads, HD 256, a bf16 KV cache of 32768 positions ~ N(0,1),
+gates ~ N(0,1)) for 512 one-query steps (qwc_attention_decode). HBM roofline of a decode
+step: GDN 2 MiB of state read + written; attention 64 MiB of K and V. The CPU baseline is
+the oracle's C restatement of the same op on a bounded sample.
 """
 import argparse
 import json
@@ -331,6 +340,174 @@ def run_prefill(args):
     return 0
 
 
+def _op_line(args, metric, value, unit, config, extra):
+    line = {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": config}
+    line.update(extra)
+    return line
+
+
+def run_gdn_op(args):
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    abi = pkg.abi
+    KH = VH = 16
+    DK = DV = 128
+    C = 2 * KH * DK + VH * DV
+    T, ND = 4096, 256
+    rng = np.random.default_rng(2)
+    bf = lambda a: pkg.synth.bf16_bits_to_f32(pkg.synth.f32_to_bf16_bits(a.astype(np.float32)))
+    mixed = bf(rng.standard_normal((T + ND, C)))
+    a = rng.standard_normal((T + ND, VH)).astype(np.float32)
+    b = rng.standard_normal((T + ND, VH)).astype(np.float32)
+    conv_w = (rng.standard_normal((C, 4)) * 0.1).astype(np.float32)
+    A_log = rng.uniform(0, np.log(16), VH).astype(np.float32)
+    dt = np.zeros(VH, np.float32)
+    neg = (-np.exp(A_log)).astype(np.float32)
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    d_mixed, d_a, d_b, d_w, d_neg, d_dt = dev(mixed), dev(a), dev(b), dev(conv_w), dev(neg), dev(dt)
+    d_ring = torch.zeros((C, 4), device="cuda")
+    d_state = torch.zeros((VH, DK, DV), device="cuda")
+    d_out = torch.empty((T + ND, VH * DV), device="cuda")
+    ws_b = abi.gdn_prefill_workspace(KH, VH, T)
+    ws = torch.empty(ws_b, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def prefill():
+        abi.gdn_prefill(d_mixed.data_ptr(), d_a.data_ptr(), d_b.data_ptr(), d_w.data_ptr(), d_neg.data_ptr(),
+                        d_dt.data_ptr(), d_ring.data_ptr(), d_state.data_ptr(), d_out.data_ptr(), KH, VH, T, 0,
+                        ws.data_ptr(), ws_b, stream.cuda_stream)
+
+    def decode(t, sh):
+        abi.gdn_decode_step(d_mixed[t].data_ptr(), d_a[t].data_ptr(), d_b[t].data_ptr(), d_w.data_ptr(),
+                            d_neg.data_ptr(), d_dt.data_ptr(), d_ring.data_ptr(), d_state.data_ptr(),
+                            d_out[t].data_ptr(), KH, VH, t, sh)
+
+    # the 256 single-token steps as one CUDA graph (one launch each, no host gaps)
+    for t in range(T, T + 4):
+        decode(t, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        sh = torch.cuda.current_stream().cuda_stream
+        for t in range(T, T + ND):
+            decode(t, sh)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(args.warmup):
+        d_ring.zero_(); d_state.zero_()
+        prefill()
+        graph.replay()
+    pf_ms = dec_ms = 0.0
+    for _ in range(args.steps):
+        d_ring.zero_(); d_state.zero_()
+        torch.cuda.synchronize()
+        e[0].record(stream)
+        prefill()
+        e[1].record(stream)
+        graph.replay()
+        e[2].record(stream)
+        torch.cuda.synchronize()
+        pf_ms += e[0].elapsed_time(e[1])
+        dec_ms += e[1].elapsed_time(e[2])
+    pf_ms /= args.steps
+    us_step = dec_ms / args.steps / ND * 1000
+    peak, src = measured_peaks()
+    dec_bytes = 2 * VH * DK * DV * 4 + C * 4 + 2 * VH * 4 + VH * DV * 4 + 2 * C * 4 * 4
+    from oracle import bindings
+    n = 256
+    st, cs, want = np.zeros((VH, DK, DV), np.float32), np.zeros((C, 3), np.float32), np.empty((n, VH, DV), np.float32)
+    t0 = time.perf_counter()
+    bindings.orc_lib().orc_gdn_core(n, KH, VH, DK, DV, 4, np.ascontiguousarray(mixed[:n]), conv_w,
+                                    np.ascontiguousarray(a[:n]), np.ascontiguousarray(b[:n]), A_log, dt, st, cs, want)
+    cpu = n / (time.perf_counter() - t0)
+    line = _op_line(args, "GDN op prefill tok/s", T / (pf_ms / 1000), "tok/s",
+                    {"workload": "configs[1]: GDN mixer op, T=4096 prefill then 256 decode steps", "heads": VH,
+                     "dk": DK, "dv": DV, "conv": 4, "l2": "state 1 MiB per head set, inputs 100+ MB"},
+                    {"ms_per_step": round(pf_ms, 3),
+                     "decode": {"us_per_step": round(us_step, 2), "achieved_gbs": round(dec_bytes / (us_step * 1e3), 1),
+                                "peak_gbs": peak, "frac": round(dec_bytes / (us_step * 1e3) / peak, 4),
+                                "bytes_per_step": dec_bytes, "peak_source": src},
+                     "roofline": {"bound": "hbm", "kernel": "k_gdn_decode (decode step)",
+                                  "achieved": round(dec_bytes / (us_step * 1e3), 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(dec_bytes / (us_step * 1e3) / peak, 4), "peak_source": src,
+                                  "traffic": None},
+                     "e2e": None, "gpu_launches": args.steps * (4 + ND),
+                     "cpu_baseline": {"value": round(cpu, 1), "unit": "tok/s", "cores": 1, "kind": "port",
+                                      "sample": f"orc_gdn_core over {n} tokens (the oracle's C restatement)"}})
+    emit(line)
+    return 0
+
+
+def run_attn_op(args):
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    abi = pkg.abi
+    NQ, NKV, HD, CTX, NS = 8, 2, 256, 32768, 512
+    g = torch.Generator(device="cuda").manual_seed(3)
+    K = torch.randn(NKV, CTX, HD, device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn(NKV, CTX, HD, device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn(NS, NQ, HD, device="cuda", generator=g) * 0.0625
+    gate = torch.randn(NS, NQ, HD, device="cuda", generator=g)
+    out = torch.empty(NS, NQ, HD, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def one(i, sh):
+        abi.attention_decode(q[i].data_ptr(), gate[i].data_ptr(), K.data_ptr(), V.data_ptr(), 1, NQ, NKV, CTX, CTX,
+                             out[i].data_ptr(), sh)
+
+    for i in range(8):  # first call sizes the split-K workspace (allocated once)
+        one(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        sh = torch.cuda.current_stream().cuda_stream
+        for i in range(NS):
+            one(i, sh)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ms = 0.0
+    for _ in range(args.steps):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms += e0.elapsed_time(e1)
+    us = ms / args.steps / NS * 1000
+    bytes_step = 2 * NKV * CTX * HD * 2 + 3 * NQ * HD * 4
+    peak, src = measured_peaks()
+    from oracle import bindings
+    kc = K.float()[:, :CTX].transpose(0, 1).contiguous().cpu().numpy()
+    vc = V.float()[:, :CTX].transpose(0, 1).contiguous().cpu().numpy()
+    want = np.empty((NQ, HD), np.float32)
+    qn, gn = q[0].cpu().numpy(), gate[0].cpu().numpy()
+    reps = 4
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        bindings.orc_lib().orc_attention(NQ, NKV, HD, CTX, qn, gn, kc, vc, want)
+    cpu = reps / (time.perf_counter() - t0)
+    err = float(np.linalg.norm(out[0].cpu().numpy() - want) / np.linalg.norm(want))
+    line = _op_line(args, "attention decode op steps/s", 1e6 / us, "steps/s",
+                    {"workload": "configs[2]: gated attention decode, 8q/2kv, HD 256, bf16 KV 32768, 512 steps",
+                     "kv_cache": "bf16", "context": CTX, "l2": "KV 64 MiB per step (inputs larger than L2 in total)"},
+                    {"ms_per_step": round(us / 1000, 5),
+                     "roofline": {"bound": "hbm", "kernel": "k_attn_decode (split-K flash decode)",
+                                  "achieved": round(bytes_step / (us * 1e3), 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(bytes_step / (us * 1e3) / peak, 4), "peak_source": src,
+                                  "traffic": None, "bytes_per_step": bytes_step},
+                     "e2e": None, "gpu_launches": args.steps * NS, "rel_l2_vs_oracle": err,
+                     "cpu_baseline": {"value": round(cpu, 3), "unit": "steps/s", "cores": 1, "kind": "port",
+                                      "sample": f"orc_attention over {CTX} positions, {reps} steps"}})
+    emit(line)
+    return 0
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -553,7 +730,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "prefill", "gdn-op", "attn-op"), default="decode")
     ap.add_argument("--seq-len", type=int, default=8192, help="prefill workload: prompt length")
     ap.add_argument("--model", default=None, help="prefill workload: synthetic shape name")
     args = ap.parse_args()
@@ -562,6 +739,10 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "gdn-op":
+        return run_gdn_op(args)
+    if args.workload == "attn-op":
+        return run_attn_op(args)
     return run_ours(args)
 
 

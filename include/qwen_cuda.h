@@ -314,7 +314,8 @@ int qwc_attention_decode(const float* q, const float* gate, const void* k_cache,
  * library reserves on every GPU that loads it (held until the process exits), and calls
  * no cudaMalloc, cudaFree or other allocating routine.
  *  - Limit: the workspace, 256 B + NQ * nsplit * 1032 B (nsplit = number of context
- *    splits, at most 296 on a B200, about n_ctx / 64), must fit 4 MiB; larger requests
+ *    splits, n_ctx / 32 rounded up, at most 2 per SM: 296 on a B200), must fit 4 MiB;
+ *    larger requests
  *    return QWC_E_INVALID with the sizes in qwc_last_error(NULL). NKV <= 64.
  *  - The first call on each device looks up the array's device address (with that
  *    device current); make that first call before any stream capture.

@@ -319,28 +319,40 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     auto ml_of = [&](int s2, int g) -> float2 {
         return staged ? ml_s[s2 * GRP + g] : __ldcg(reinterpret_cast<const float2*>(p.part_ml) + pair0 + (size_t)s2 * GRP + g);
     };
+    // every head's partials are loaded together (GRP x 8 in flight); per head the sums run
+    // over the splits in order
+    float M[GRP], L[GRP], o[GRP];
 #pragma unroll
     for (int g = 0; g < GRP; ++g) {
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < n_act; ++s2) M = fmaxf(M, ml_of(s2, g).x);
-        float L = 0.f, o = 0.f;
-        for (int s0 = 0; s0 < n_act; s0 += 8) {
-            float po[8];
+        M[g] = -INFINITY;
+        for (int s2 = 0; s2 < n_act; ++s2) M[g] = fmaxf(M[g], ml_of(s2, g).x);
+        L[g] = 0.f;
+        o[g] = 0.f;
+    }
+    for (int s0 = 0; s0 < n_act; s0 += 8) {
+        float po[GRP][8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)  // eight partial outputs in flight
-                po[u] = s0 + u < n_act ? __ldcg(&p.part_o[((pair0 + (size_t)(s0 + u) * GRP + g)) * kHD + t]) : 0.f;
+        for (int g = 0; g < GRP; ++g)
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                po[g][u] = s0 + u < n_act ? __ldcg(&p.part_o[((pair0 + (size_t)(s0 + u) * GRP + g)) * kHD + t]) : 0.f;
+#pragma unroll
+        for (int g = 0; g < GRP; ++g) {
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 if (s0 + u < n_act) {
                     const float2 ml = ml_of(s0 + u, g);
-                    const float f = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
-                    L += ml.y * f;
-                    o += po[u] * f;
+                    const float f = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M[g]);
+                    L[g] += ml.y * f;
+                    o[g] += po[g][u] * f;
                 }
             }
         }
+    }
+#pragma unroll
+    for (int g = 0; g < GRP; ++g) {
         const int h = kv * GRP + g;
-        p.out[(size_t)h * kHD + t] = (o / L) * sigmoid_f(gate[g]);
+        p.out[(size_t)h * kHD + t] = (o[g] / L[g]) * sigmoid_f(gate[g]);
     }
     if (t == 0) p.counters[kv] = 0u;
     mark(3);

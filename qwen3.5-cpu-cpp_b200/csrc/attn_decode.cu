@@ -10,10 +10,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodePa
     attn_decode_item<GRP>(p, blockIdx.x, blockIdx.y);
 }
 
-int attn_nsplit_for(int max_ctx) {
-    // enough splits to cover the SMs at long context, each >= kMinChunk positions
+int attn_nsplit_for(int max_ctx, int nkv) {
+    // splits of >= kMinChunk positions, at most one CTA per SM over all kv heads: more
+    // splits shorten each CTA's loop but lengthen the serial combine of the partials
     int want = (max_ctx + kMinChunk - 1) / kMinChunk;
-    int cap = 2 * num_sms();
+    int cap = num_sms() / (nkv > 0 ? nkv : 1);
     return want < 1 ? 1 : (want > cap ? cap : want);
 }
 

@@ -7,6 +7,8 @@
 #include <mutex>
 
 #include "kernels.h"
+
+#include <algorithm>
 #include "qwen_cuda.h"
 
 namespace {
@@ -61,8 +63,10 @@ extern "C" int qwc_attention_decode_noalloc(const float* q, const float* gate, c
         qwc::set_api_error("qwc_attention_decode_noalloc: invalid argument");
         return QWC_E_INVALID;
     }
-    // same split count as qwc_attention_decode, so both give the same result
-    const int nsplit = qwc::attn_nsplit_for(n_ctx);
+    // this entry keeps its own split rule (positions / 32, at most 2 per SM), in which its
+    // documented workspace limit is stated; the result matches qwc_attention_decode to
+    // rounding (the partials are grouped differently)
+    const int nsplit = std::max(1, std::min((n_ctx + 31) / 32, 2 * qwc::num_sms()));
     const size_t rows = (size_t)NQ * nsplit;  // NKV * nsplit * GRP partial rows
     const size_t off_ml = 256;
     const size_t off_o = round256(off_ml + rows * 2 * sizeof(float));

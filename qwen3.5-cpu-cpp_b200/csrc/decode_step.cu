@@ -426,7 +426,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
             for (int s2 = 0; s2 < n_act; ++s2)
                 M = fmaxf(M, __ldcg(&g.part_ml[((size_t)(kv * g.nsplit + s2) * grp + gg) * 2]));
             float L = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
+#pragma unroll 8
             for (int s2 = 0; s2 < n_act; ++s2) {
                 const size_t pi = (size_t)(kv * g.nsplit + s2) * grp + gg;
                 const float2 ml = __ldcg(reinterpret_cast<const float2*>(g.part_ml) + pi);

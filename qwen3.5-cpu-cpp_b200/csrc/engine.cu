@@ -968,7 +968,7 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
         return bail(fail(h, QWC_E_OOM, "KV cache allocation failed"));
 
     // scratch arena
-    h->nsplit = attn_nsplit_for(max_context);
+    h->nsplit = attn_nsplit_for(max_context, h->NKV);
     const int grp = h->NQ / h->NKV;
     Arena s;
     auto carve = [&](size_t bytes) { return s.take(bytes); };
@@ -1746,7 +1746,7 @@ extern "C" int qwc_attention_decode(const float* q, const float* gate, const voi
     p.n_ctx_val = n_ctx;
     p.NQ = NQ;
     p.NKV = NKV;
-    p.nsplit = attn_nsplit_for(n_ctx);
+    p.nsplit = attn_nsplit_for(n_ctx, NKV);
     p.out = out;
     const int grp = NQ / NKV;
     const size_t need_o = (size_t)NKV * p.nsplit * grp * 256;

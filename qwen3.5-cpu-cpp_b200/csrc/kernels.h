@@ -113,7 +113,7 @@ struct AttnDecodeParams {
                                     // of `out` combines them (PRO_ATTN_COMBINE)
 };
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t s, bool pdl);
-int attn_nsplit_for(int max_ctx);
+int attn_nsplit_for(int max_ctx, int nkv);
 
 // ------------------------------------------------------------------ persistent step
 // One launch = one decode step: a list of phases run by a cooperative grid of one CTA

@@ -116,6 +116,11 @@ struct qwc_handle {
           *pf_vc = nullptr, *pf_glog = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
     float *pf_u = nullptr, *pf_w = nullptr, *pf_qg = nullptr, *pf_kd = nullptr, *pf_p = nullptr, *pf_gc = nullptr;
     uint16_t *pf_xa = nullptr, *pf_xb = nullptr;
+    uint16_t* pf_vsplit = nullptr;  // [NKV][chunk][512] V of the chunk as bf16 pairs
+    // tensor-core attention: per attention layer K [NKV][ctx][512] and V^T [NKV][512][ctx]
+    // as bf16 pairs, for the positions of one batched pass
+    uint16_t* pf_kvs = nullptr;
+    size_t pf_kvs_bytes = 0;
 
     // tensor parallelism: this handle holds `shard` of a tp_world-rank group; the working
     // sizes above (KH, VH, KD, VD, C, NQ, NKV, I) are the shard's, g_* the whole model's
@@ -809,6 +814,7 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     cudaFree(h->scratch);
     cudaFree(h->step_phases);
     cudaFree(h->pf_ws);
+    cudaFree(h->pf_kvs);
     if (h->nccl) ncclCommDestroy(h->nccl);
     if (h->h_pin) cudaFreeHost(h->h_pin);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -1156,6 +1162,13 @@ static int pf_build_maps(qwc_handle* h) {
     return QWC_OK;
 }
 
+// Causal attention of the batched pass on the tensor cores (default) or, with
+// QWC_PREFILL_ATTN=simt, the fp32 CUDA-core kernel.
+static bool pf_attn_tc() {
+    const char* e = std::getenv("QWC_PREFILL_ATTN");
+    return !(e && std::strcmp(e, "simt") == 0);
+}
+
 static int pf_workspace(qwc_handle* h, int cap) {
     if (h->pf_cap >= cap) return QWC_OK;
     cudaFree(h->pf_ws);
@@ -1181,7 +1194,8 @@ static int pf_workspace(qwc_handle* h, int cap) {
                  o_u = carve(c * h->VD * 4), o_w = carve(c * h->VD * 4), o_qg = carve(c * h->VD * 4),
                  o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 64 * 64 * 4),
                  o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4), o_part = carve(c * h->H * 4),
-                 o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2);
+                 o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2),
+                 o_vs = carve(c * h->NKV * 2 * h->HD * 2);
     if (cudaMalloc(&h->pf_ws, off) != cudaSuccess) {
         h->pf_ws = nullptr;
         return fail(h, QWC_E_OOM, "prefill workspace allocation failed");
@@ -1207,6 +1221,7 @@ static int pf_workspace(qwc_handle* h, int cap) {
     h->pf_logits = reinterpret_cast<float*>(b + o_log);
     h->pf_xa = reinterpret_cast<uint16_t*>(b + o_xa);
     h->pf_xb = reinterpret_cast<uint16_t*>(b + o_xb);
+    h->pf_vsplit = reinterpret_cast<uint16_t*>(b + o_vs);
     h->pf_cap = cap;
     return QWC_OK;
 }
@@ -1257,6 +1272,22 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
     if (rc) return rc;
     const int H = h->H;
     const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
+    // tensor-core attention operands for positions [0, p0 + T): K and V^T pairs per layer
+    const bool attn_tc = pf_attn_tc() && h->HD == 256 && h->n_attn > 0;
+    const int ctx_pad = (p0 + T + 63) / 64 * 64;
+    const size_t kvs_layer = (size_t)2 * h->NKV * ctx_pad * 2 * h->HD;  // elements
+    if (attn_tc && h->pf_kvs_bytes < kvs_layer * 2 * h->n_attn) {
+        cudaFree(h->pf_kvs);
+        h->pf_kvs = nullptr;
+        h->pf_kvs_bytes = 0;
+        if (cudaMalloc(&h->pf_kvs, kvs_layer * 2 * h->n_attn) != cudaSuccess) {
+            h->pf_kvs = nullptr;
+            return fail(h, QWC_E_OOM, "prefill attention operand allocation failed");
+        }
+        h->pf_kvs_bytes = kvs_layer * 2 * h->n_attn;
+        // every entry holds a finite value: positions past the prompt meet zero weights
+        CU(cudaMemsetAsync(h->pf_kvs, 0, h->pf_kvs_bytes, h->stream));
+    }
     for (int c0 = 0; c0 < T; c0 += chunk) {
         const int Tc = std::min(chunk, T - c0), pc = p0 + c0;
         CU(cudaMemcpyAsync(h->pf_ids, ids + c0, (size_t)Tc * 4, cudaMemcpyHostToDevice, h->stream));
@@ -1290,6 +1321,13 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 a.eps = h->eps;
                 a.xs = h->pf_xa;
                 a.ldxs = h->pf_lda;
+                if (attn_tc) {
+                    a.ksplit = h->pf_kvs + kvs_layer * lw.idx;
+                    a.vt = a.ksplit + kvs_layer / 2;
+                    a.vsplit = h->pf_vsplit;
+                    a.ctx_pad = ctx_pad;
+                    a.err = h->dev_err;
+                }
                 CU(pf_attention(a, h->stream));
             } else {
                 PfGdnArgs g;

@@ -164,6 +164,8 @@ struct TcGemmParams {
 // Tensor map of a row-major bf16 matrix [rows][cols] with row stride ld (elements), in
 // 128 x 64 boxes with the 128-byte swizzle. Returns 0 on success.
 int tc_make_map(CUtensorMap* map, const void* base, long rows, long cols, long ld);
+// The same with boxes of `box_rows` rows (x 64 columns).
+int tc_make_map_box(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_rows);
 cudaError_t launch_tc_gemm(const CUtensorMap& mapW, const CUtensorMap& mapX, const TcGemmParams& p, cudaStream_t s);
 
 // ------------------------------------------------------------------ prefill kernels
@@ -216,8 +218,29 @@ struct PfAttnArgs {
     float eps = 1e-6f;
     uint16_t* xs = nullptr;       // output [T][ldxs], K = NQ*HD
     long ldxs = 0;
+    // tensor-core attention operands (bf16 pairs): K split [NKV][ctx_pad][512] and V^T
+    // split [NKV][2][256][ctx_pad] of this layer (persist across chunks), V split scratch
+    // [NKV][T][512] of the chunk
+    uint16_t* ksplit = nullptr;
+    uint16_t* vt = nullptr;
+    uint16_t* vsplit = nullptr;
+    int ctx_pad = 0;
+    int* err = nullptr;
 };
 cudaError_t pf_attention(const PfAttnArgs& a, cudaStream_t s);
+struct PfFattnArgs {
+    const float* qbuf = nullptr;
+    const float* proj = nullptr;
+    long ldp = 0;
+    uint16_t* xs = nullptr;
+    long ldxs = 0;
+    const uint16_t* ksplit = nullptr;
+    uint16_t* vt = nullptr;
+    const uint16_t* vsplit = nullptr;
+    int T = 0, p0 = 0, NQ = 0, NKV = 0, ctx_pad = 0;
+    int* err = nullptr;
+};
+cudaError_t pf_fattn(const PfFattnArgs& a, cudaStream_t s);
 cudaError_t pf_add(float* y, const float* x, size_t n, cudaStream_t s);  // y += x (16-byte aligned)
 
 // Records a handle-less failure message (what qwc_last_error(NULL) returns).

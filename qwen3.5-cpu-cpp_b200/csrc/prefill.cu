@@ -486,7 +486,25 @@ struct PfAttnPrep {
     void* v_cache;
     int kv_bf16, max_ctx, p0, NQ, NKV, rot;
     float eps;
+    // tensor-core attention operands (null: not written): K as bf16 pairs
+    // [NKV][ctx_pad][hi 256 | lo 256], V likewise [NKV][T][hi | lo] for this chunk
+    uint16_t* ksplit;
+    uint16_t* vsplit;
+    int ctx_pad, T;
 };
+// 8 values -> bf16 hi at dst[0..8), lo at dst[256..264) (16-byte stores)
+__device__ __forceinline__ void store_split8(uint16_t* dst, const float (&x)[8]) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint16_t h0 = f2bf(x[2 * e]), h1 = f2bf(x[2 * e + 1]);
+        const uint16_t l0 = f2bf(x[2 * e] - bf16lo(h0)), l1 = f2bf(x[2 * e + 1] - bf16lo(h1));
+        hw[e] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lw[e] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+    }
+    *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(dst + kHD) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
 __global__ void __launch_bounds__(kPT) k_pf_attn_prep(const PfAttnPrep p) {
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = p.p0 + t;
@@ -510,6 +528,15 @@ __global__ void __launch_bounds__(kPT) k_pf_attn_prep(const PfAttnPrep p) {
             const int kv = v < p.NQ + p.NKV ? v - p.NQ : v - p.NQ - p.NKV;
             void* cache = v < p.NQ + p.NKV ? p.k_cache : p.v_cache;
             const size_t off = ((size_t)kv * p.max_ctx + pos) * kHD + lane * 8;
+            if (p.ksplit) {
+                // the split carries the value the cache holds (bf16-rounded for a bf16 cache)
+                float y[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = p.kv_bf16 ? bf16lo(f2bf(x[e])) : x[e];
+                uint16_t* dst = v < p.NQ + p.NKV ? p.ksplit + ((size_t)kv * p.ctx_pad + pos) * 2 * kHD
+                                                 : p.vsplit + ((size_t)kv * p.T + t) * 2 * kHD;
+                store_split8(dst + lane * 8, y);
+            }
             if (p.kv_bf16) {
                 uint4 u;
                 u.x = (uint32_t)f2bf(x[0]) | ((uint32_t)f2bf(x[1]) << 16);
@@ -784,11 +811,32 @@ cudaError_t pf_gated_norm_split(const float* o, long ldo, const float* z, long l
 }
 cudaError_t pf_attention(const PfAttnArgs& a, cudaStream_t s) {
     if (a.rot > kHD || a.rot % 16 || a.NKV <= 0 || a.NQ % a.NKV) return cudaErrorInvalidValue;
+    const bool tc = a.ksplit != nullptr;
+    if (tc && (!a.vt || !a.vsplit || a.ctx_pad % 64 || a.p0 + a.T > a.ctx_pad)) return cudaErrorInvalidValue;
     PfAttnPrep pp{a.proj, a.ldp, a.qn1, a.kn1, a.rope_cs, a.qbuf, a.k_cache, a.v_cache,
-                  a.kv_bf16, a.max_ctx, a.p0, a.NQ, a.NKV, a.rot, a.eps};
+                  a.kv_bf16, a.max_ctx, a.p0, a.NQ, a.NKV, a.rot, a.eps,
+                  a.ksplit, a.vsplit, a.ctx_pad, a.T};
     k_pf_attn_prep<<<a.T, kPT, 0, s>>>(pp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    if (tc) {
+        PfFattnArgs f;
+        f.qbuf = a.qbuf;
+        f.proj = a.proj;
+        f.ldp = a.ldp;
+        f.xs = a.xs;
+        f.ldxs = a.ldxs;
+        f.ksplit = a.ksplit;
+        f.vt = a.vt;
+        f.vsplit = a.vsplit;
+        f.T = a.T;
+        f.p0 = a.p0;
+        f.NQ = a.NQ;
+        f.NKV = a.NKV;
+        f.ctx_pad = a.ctx_pad;
+        f.err = a.err;
+        return pf_fattn(f, s);
+    }
     PfAttn at{a.qbuf, a.proj, a.ldp, a.k_cache, a.v_cache, a.kv_bf16, a.max_ctx, a.p0, a.T, a.NQ, a.NKV, a.xs, a.ldxs};
     const int grp = a.NQ / a.NKV;
     auto go = [&](auto kern, int bqt) -> cudaError_t {

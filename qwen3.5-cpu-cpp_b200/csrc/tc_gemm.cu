@@ -271,12 +271,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 2-D bf16 tensor map over a row-major [rows][cols] matrix (row stride ld elements),
 // boxes of 128 rows x 64 columns in the 128-byte swizzle; out-of-range rows read as zero.
 int tc_make_map(CUtensorMap* map, const void* base, long rows, long cols, long ld) {
+    return tc_make_map_box(map, base, rows, cols, ld, kTM);
+}
+
+int tc_make_map_box(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return -1;
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || rows <= 0 || cols <= 0 || ld < cols) return -2;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)kTM};
+    if (box_rows <= 0 || box_rows > 256) return -2;
+    const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -82,3 +82,46 @@ def test_prefill_is_repeatable_and_resets_state(pkg):
     assert np.array_equal(a, b)
     assert m.position() == len(ids)
     m.close()
+
+
+@pytest.fixture
+def attn_impl():
+    """Switch the batched pass's attention between the tcgen05 kernel (default) and the
+    fp32 CUDA-core kernel; restores the environment afterwards."""
+    old = os.environ.get("QWC_PREFILL_ATTN")
+
+    def use(name):
+        if name == "tc":
+            os.environ.pop("QWC_PREFILL_ATTN", None)
+        else:
+            os.environ["QWC_PREFILL_ATTN"] = name
+
+    yield use
+    if old is None:
+        os.environ.pop("QWC_PREFILL_ATTN", None)
+    else:
+        os.environ["QWC_PREFILL_ATTN"] = old
+
+
+@pytest.mark.parametrize("chunk", [128, 4096], indirect=True)
+@pytest.mark.parametrize("shape,T", [("tiny", 333), ("tiny-rep", 64), ("small-0.8b-widths", 203)])
+def test_tensor_core_attention_matches_simt_and_oracle(pkg, oracle, chunk, attn_impl, shape, T):
+    """The tcgen05 flash attention (bf16-pair operands, three products) against the fp32
+    kernel and the oracle: GQA groups of 2 and 4 query heads, ragged lengths (a partial
+    last key block, a partial last query block), one chunk and several."""
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=31)
+    last = s.vocab_size > 4096  # wide vocabulary: the last position's logits only
+    m = pkg.abi.Model(d, max_context=T + 8)
+    attn_impl("tc")
+    got = m.forward_logits(ids, last_only=last).reshape(-1, s.vocab_size)
+    attn_impl("simt")
+    simt = m.forward_logits(ids, last_only=last).reshape(-1, s.vocab_size)
+    m.close()
+    want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=last).reshape(-1, s.vocab_size)
+    assert got.shape == want.shape == simt.shape
+    for i in range(got.shape[0]):
+        assert rel_l2(got[i], want[i]) < LOGIT_TOL, i
+        assert rel_l2(got[i], simt[i]) < LOGIT_TOL, i
+    assert (got.argmax(1) == simt.argmax(1)).mean() > 0.99

@@ -7,41 +7,49 @@
 //   S = Qh Kh + Qh Kl + Ql Kh,     O += Ph Vh + Ph Vl + Pl Vh,
 // with fp32 accumulation in tensor memory: the dropped lo x lo term is ~2^-16 relative.
 //
-// CTA = (kv head, block of 128 query rows = GRP q heads x 128/GRP tokens), 160 threads:
-//   warps 0-3  one query row per thread (= its TMEM lane): load and split the row's q,
-//              online softmax over each 64-key block read from TMEM (tcgen05.ld), P as bf16
-//              pairs into shared memory (128-byte swizzle, K-major), O rescaled in TMEM
-//              (tcgen05.ld / st) when the row max grows; at the end O / l * sigmoid(gate)
-//              written as the hi/lo input of o_proj.
-//   warp 4     allocates 512 TMEM columns (S: 64, O: 256); one lane issues the TMA loads
-//              (no multicast) and the MMAs: per key block K (split, 64 KB) -> 48 MMAs
-//              M=128 N=64 K=16 -> S; the same 64 KB buffer then takes V^T (split) -> after
-//              the softmax warps publish P, 12 MMAs M=128 N=256 K=16 -> O.
-// Shared memory: Q pairs 128 KB (resident), K / V^T block 64 KB, P pairs 32 KB.
+// CTA = (kv head, block of 128 query rows = GRP q heads x 128/GRP tokens), 224 threads:
+//   warps 0-3  one query row per thread (= its TMEM lane): split the row's q (hi to shared
+//              memory, lo to tensor memory); per 64-key block read S from TMEM, online
+//              softmax in the log2 domain, write P as bf16 pairs back over S in TMEM. The
+//              running max is raised (and O rescaled in TMEM) only when a block's max
+//              exceeds it by more than 8 (a factor 256): P stays <= 256, and O / l is the
+//              same quotient. At the end O / l * sigmoid(gate) -> the hi/lo input of o_proj.
+//   warp 4     allocates the 512 TMEM columns; one lane issues the MMAs in the order
+//              S(0) S(1) PV(0) S(2) PV(1) ..., so that S(kb+1) runs on the tensor cores
+//              while the softmax works on block kb.
+//   warp 5     one lane loads K blocks (TMA, no multicast) into the K buffer once the S MMAs
+//              of the previous block have read it.
+//   warp 6     one lane loads V^T blocks into the V buffer once PV of the previous block
+//              has completed.
+// Tensor memory: S / P double buffer (2 x 64 columns: S fp32, then P hi in the first 32
+// and P lo in the next 32 as packed bf16), Q lo (128 columns), O (256 columns).
+// Shared memory: Q hi 64 KB, K block 64 KB (4 dim chunks x hi/lo), V^T block 64 KB.
 // K and V reach this kernel as bf16 pairs written by the attention prep kernel: K split
 // row-major [kv][pos][hi 256 | lo 256], V split and transposed [kv][hi|lo][256 dims][pos],
-// so that every operand is K-major. Every wait is bounded.
+// so that every shared-memory operand is K-major. Every wait is bounded.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <cuda_bf16.h>
 
 #include <algorithm>
 
 namespace qwc {
 namespace {
 
-constexpr int kM = 128, kN = 64, kHD = 256, kThreads = 160;
-constexpr uint32_t kQTile = kM * 128;         // 128 rows x 64 dims bf16
-constexpr uint32_t kQBytes = 8 * kQTile;      // 4 dim chunks x (hi, lo)
-constexpr uint32_t kKTile = kN * 128;         // 64 keys x 64 dims bf16
-constexpr uint32_t kKVBytes = 8 * kKTile;     // K: 4 chunks x (hi, lo); V^T: (hi, lo) x 256 x 64
-constexpr uint32_t kPTile = kM * 128;         // 128 rows x 64 keys bf16
-constexpr size_t kSmem = kQBytes + kKVBytes + 2 * kPTile + 1024 + 256;
+constexpr int kM = 128, kN = 64, kHD = 256, kThreads = 224;
+constexpr uint32_t kQTile = kM * 128;     // 128 rows x 64 dims bf16
+constexpr uint32_t kQBytes = 4 * kQTile;  // Q hi: 4 dim chunks
+constexpr uint32_t kKTile = kN * 128;     // 64 keys x 64 dims bf16
+constexpr uint32_t kKVBytes = 8 * kKTile; // K: 4 chunks x (hi, lo); V^T: (hi, lo) x 256 x 64
+constexpr size_t kSmem = kQBytes + 2 * kKVBytes + 1024 + 256;
 constexpr int kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256;
+constexpr uint32_t kColS = 0, kColQl = 128, kColO = 256;  // S / P buffer b at kColS + 64 b
 constexpr uint32_t kIdescS =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
 constexpr uint32_t kIdescO =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kHD >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
+constexpr float kRescaleLog2 = 8.0f;
 static_assert(kSmem <= 232448, "shared memory of the attention CTA");
 
 __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -55,11 +63,20 @@ __device__ __forceinline__ uint64_t desc128(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
            (2ull << 61);
 }
-__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// D[tmem] (+)= A[tmem: row i in lane i, K packed two bf16 per column] * B[smem desc]
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(acc)
         : "memory");
 }
 __device__ __forceinline__ void commit(uint64_t* bar) {
@@ -68,50 +85,32 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
+__device__ __forceinline__ void ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void st16(uint32_t taddr, const float (&v)[16]) {
+__device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t* r) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15, %16};" ::"r"(taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
-__device__ __forceinline__ uint16_t bf16r(float f) {
-    uint32_t u = __float_as_uint(f);
-    u += 0x7fffu + ((u >> 16) & 1u);
-    return (uint16_t)(u >> 16);
-}
-__device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+__device__ __forceinline__ void st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Write 8 consecutive values (K index 8s .. 8s+7) of row `row` into a K-major 128-byte
-// swizzled tile as bf16 hi and lo: 16-byte segment s of the row lives at s ^ (row % 8).
-__device__ __forceinline__ void put8(uint8_t* hi_tile, uint8_t* lo_tile, int row, int s, const float (&v)[8]) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const uint16_t h0 = bf16r(v[2 * e]), h1 = bf16r(v[2 * e + 1]);
-        const uint16_t l0 = bf16r(v[2 * e] - bf16f(h0)), l1 = bf16r(v[2 * e + 1] - bf16f(h1));
-        h[e] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        l[e] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-    }
-    const uint32_t off = (uint32_t)row * 128 + (uint32_t)((s ^ (row & 7)) * 16);
-    *reinterpret_cast<uint4*>(hi_tile + off) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(lo_tile + off) = make_uint4(l[0], l[1], l[2], l[3]);
+// (a, b) -> bf16 hi pair and lo pair, each packed with a in the low half
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
 struct FAParams {
@@ -129,32 +128,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* Qs = sm;
-    uint8_t* KV = sm + kQBytes;
-    uint8_t* Ph = KV + kKVBytes;
-    uint8_t* Pl = Ph + kPTile;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(Pl + kPTile);
-    uint64_t* kv_full = bar + 0;
-    uint64_t* kv_free = bar + 1;
-    uint64_t* s_full = bar + 2;
-    uint64_t* p_full = bar + 3;
-    uint64_t* pv_done = bar + 4;
-    uint64_t* mma_done = bar + 5;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 6);
+    uint8_t* Kb = sm + kQBytes;
+    uint8_t* Vb = Kb + kKVBytes;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(Vb + kKVBytes);
+    uint64_t* k_full = bar + 0;
+    uint64_t* k_free = bar + 1;
+    uint64_t* v_full = bar + 2;
+    uint64_t* pv_done = bar + 3;  // also: V buffer free
+    uint64_t* s_full = bar + 4;   // [2]
+    uint64_t* p_full = bar + 6;   // [2]
+    uint64_t* mma_done = bar + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 9);
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kv = blockIdx.x, qb = blockIdx.y;
-    const int bqt = kM / p.grp;  // tokens per CTA
+    const int kv = blockIdx.x;
+    const int qb = gridDim.y - 1 - blockIdx.y;  // longest causal rows first
+    const int bqt = kM / p.grp;                 // tokens per CTA
     const int t_last = min((qb + 1) * bqt, p.T) - 1;
     const int nkb = (p.p0 + t_last) / kN + 1;  // causal: key blocks up to the last query
-    const float scale = 1.0f / sqrtf((float)kHD);
 
     if (threadIdx.x == 0) {
-        mbar_init(kv_full, 1);
-        mbar_init(kv_free, 1);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 4);
+        mbar_init(k_full, 1);
+        mbar_init(k_free, 1);
+        mbar_init(v_full, 1);
         mbar_init(pv_done, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(&p_full[0], 4);
+        mbar_init(&p_full[1], 4);
         mbar_init(mma_done, 1);
         *s_abort = 0;
         fence_mbar_init();
@@ -164,168 +166,226 @@ __global__ void __launch_bounds__(kThreads, 1)
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
     // query rows: thread rho (< 128) = TMEM lane rho; row rho = (head g, token i)
     const int rho = threadIdx.x;
     const int g = rho / bqt, ti = qb * bqt + (rho % bqt);
     const int h = kv * p.grp + g;
     const bool valid = warp < 4 && ti < p.T;
     const int qpos = p.p0 + ti;
+    const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     if (warp < 4) {
         const float* q = p.qbuf + ((size_t)(valid ? ti : 0) * p.NQ + h) * kHD;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int gq = 0; gq < 8; ++gq) {  // 32 dims per step
+            uint32_t lo[16];
 #pragma unroll
-            for (int s = 0; s < 8; ++s) {
+            for (int s4 = 0; s4 < 4; ++s4) {
                 float v[8];
                 if (valid) {
-                    const float4 a = *reinterpret_cast<const float4*>(q + c * 64 + s * 8);
-                    const float4 b = *reinterpret_cast<const float4*>(q + c * 64 + s * 8 + 4);
+                    const float4 a = *reinterpret_cast<const float4*>(q + gq * 32 + s4 * 8);
+                    const float4 b = *reinterpret_cast<const float4*>(q + gq * 32 + s4 * 8 + 4);
                     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
                 } else {
 #pragma unroll
                     for (int e = 0; e < 8; ++e) v[e] = 0.f;
                 }
-                put8(Qs + (c * 2) * kQTile, Qs + (c * 2 + 1) * kQTile, rho, s, v);
+                uint32_t hi[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split2(v[2 * e], v[2 * e + 1], hi[e], lo[s4 * 4 + e]);
+                // 16-byte segment s of a 128-byte swizzled row lives at s ^ (row % 8)
+                const int c = gq >> 1, seg = (gq & 1) * 4 + s4;
+                *reinterpret_cast<uint4*>(Qs + c * kQTile + rho * 128 + ((seg ^ (rho & 7)) * 16)) =
+                    make_uint4(hi[0], hi[1], hi[2], hi[3]);
             }
+            st16(trow + kColQl + gq * 16, lo);
         }
+        st_wait();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
     }
     fence_before();
     __syncthreads();
     fence_after();
-    const uint32_t tmem = *tmem_slot;
     auto aborted = [&]() { return *reinterpret_cast<volatile int*>(s_abort) != 0; };
     auto give_up = [&](int code) {
         post_error(p.err, code);
         *reinterpret_cast<volatile int*>(s_abort) = 1;
     };
 
-    if (warp == 4) {
+    if (warp == 5) {
         if (lane == 0) {
-            // -------------------------------------------------- TMA + MMA issuer
-            const uint32_t q0 = smem_u32(Qs), kv0 = smem_u32(KV), ph0 = smem_u32(Ph), pl0 = smem_u32(Pl);
-            int pending = -1;  // parity of a kv_full phase whose TMA loads may still be in flight
+            // -------------------------------------------------- K loader
+            int pending = -1;  // parity of a k_full phase whose loads may still be in flight
             for (int kb = 0; kb < nkb && !aborted(); ++kb) {
-                const uint32_t par = (uint32_t)(kb & 1);
-                // K block (the buffer is free: the previous PV MMAs have completed)
-                if (kb > 0 && !mbar_wait_bounded(pv_done, par ^ 1u, p.err, DEV_TC_MMA_TIMEOUT)) { give_up(DEV_TC_MMA_TIMEOUT); break; }
-                mbar_arrive_expect_tx(kv_full, kKVBytes);
+                if (kb > 0 && !mbar_wait_bounded(k_free, (uint32_t)((kb - 1) & 1), p.err, DEV_TC_PRODUCER_TIMEOUT)) {
+                    give_up(DEV_TC_PRODUCER_TIMEOUT);
+                    break;
+                }
+                mbar_arrive_expect_tx(k_full, kKVBytes);
                 for (int c = 0; c < 4; ++c)
                     for (int hl = 0; hl < 2; ++hl)
-                        tma2d(KV + (c * 2 + hl) * kKTile, &mapK, hl * kHD + c * 64, kv * p.ctx_pad + kb * kN, kv_full);
-                pending = 0;
-                if (!mbar_wait_bounded(kv_full, 0u, p.err, DEV_TC_MMA_TIMEOUT)) { give_up(DEV_TC_MMA_TIMEOUT); break; }
-                pending = -1;
+                        tma2d(Kb + (c * 2 + hl) * kKTile, &mapK, hl * kHD + c * 64, kv * p.ctx_pad + kb * kN, k_full);
+                pending = kb & 1;
+            }
+            // one load at most is outstanding (the previous one was consumed before this issue)
+            if (pending >= 0) mbar_wait_bounded(k_full, (uint32_t)pending, p.err, DEV_TC_DRAIN_TIMEOUT);
+        }
+    } else if (warp == 6) {
+        if (lane == 0) {
+            // -------------------------------------------------- V^T loader
+            int pending = -1;
+            for (int kb = 0; kb < nkb && !aborted(); ++kb) {
+                if (kb > 0 && !mbar_wait_bounded(pv_done, (uint32_t)((kb - 1) & 1), p.err, DEV_TC_PRODUCER_TIMEOUT)) {
+                    give_up(DEV_TC_PRODUCER_TIMEOUT);
+                    break;
+                }
+                mbar_arrive_expect_tx(v_full, kKVBytes);
+                // hi rows d at [0, 32 KB), lo at [32, 64 KB)
+                for (int hl = 0; hl < 2; ++hl)
+                    for (int dc = 0; dc < 4; ++dc)
+                        tma2d(Vb + hl * 4 * kKTile + dc * kKTile, &mapVt, kb * kN, (kv * 2 + hl) * kHD + dc * 64, v_full);
+                pending = kb & 1;
+            }
+            if (pending >= 0) mbar_wait_bounded(v_full, (uint32_t)pending, p.err, DEV_TC_DRAIN_TIMEOUT);
+        }
+    } else if (warp == 4) {
+        if (lane == 0) {
+            // -------------------------------------------------- MMA issuer
+            const uint32_t q0 = smem_u32(Qs), k0 = smem_u32(Kb), v0 = smem_u32(Vb);
+            auto issue_s = [&](int kb) -> bool {
+                if (!mbar_wait_bounded(k_full, (uint32_t)(kb & 1), p.err, DEV_TC_MMA_TIMEOUT)) return false;
                 fence_after();
-                // S = Qh Kh + Qh Kl + Ql Kh over 4 dim chunks x 4 k-steps
+                const uint32_t d = tmem + kColS + 64u * (uint32_t)(kb & 1);
+#pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const uint64_t ah = desc128(q0 + (c * 2) * kQTile), al = desc128(q0 + (c * 2 + 1) * kQTile);
-                    const uint64_t bh = desc128(kv0 + (c * 2) * kKTile), bl = desc128(kv0 + (c * 2 + 1) * kKTile);
+                    const uint64_t ah = desc128(q0 + c * kQTile);
+                    const uint64_t bh = desc128(k0 + (c * 2) * kKTile), bl = desc128(k0 + (c * 2 + 1) * kKTile);
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks) {
                         const uint64_t adv = (uint64_t)((ks * 32) >> 4);
-                        mma(tmem + kColS, ah + adv, bh + adv, kIdescS, (c | ks) != 0 ? 1u : 0u);
-                        mma(tmem + kColS, ah + adv, bl + adv, kIdescS, 1u);
-                        mma(tmem + kColS, al + adv, bh + adv, kIdescS, 1u);
+                        const uint32_t al = tmem + kColQl + (uint32_t)(c * 32 + ks * 8);
+                        mma_ss(d, ah + adv, bh + adv, kIdescS, (c | ks) != 0 ? 1u : 0u);
+                        mma_ss(d, ah + adv, bl + adv, kIdescS, 1u);
+                        mma_ts(d, al, bh + adv, kIdescS, 1u);
                     }
                 }
-                commit(s_full);
-                commit(kv_free);
-                if (!mbar_wait_bounded(kv_free, par, p.err, DEV_TC_MMA_TIMEOUT)) { give_up(DEV_TC_MMA_TIMEOUT); break; }
-                // V^T block into the same buffer: hi rows d at [0, 32 KB), lo at [32, 64 KB)
-                mbar_arrive_expect_tx(kv_full, kKVBytes);
-                for (int hl = 0; hl < 2; ++hl)
-                    for (int dc = 0; dc < 4; ++dc)
-                        tma2d(KV + hl * 4 * kKTile + dc * kKTile, &mapVt, kb * kN, (kv * 2 + hl) * kHD + dc * 64, kv_full);
-                pending = 1;
-                if (!mbar_wait_bounded(kv_full, 1u, p.err, DEV_TC_MMA_TIMEOUT)) { give_up(DEV_TC_MMA_TIMEOUT); break; }
-                pending = -1;
-                if (!mbar_wait_bounded(p_full, par, p.err, DEV_TC_MMA_TIMEOUT)) { give_up(DEV_TC_MMA_TIMEOUT); break; }
+                commit(&s_full[kb & 1]);
+                commit(k_free);
+                return true;
+            };
+            bool ok = issue_s(0);
+            for (int kb = 0; ok && kb < nkb; ++kb) {
+                if (aborted()) { ok = false; break; }
+                if (kb + 1 < nkb && !(ok = issue_s(kb + 1))) break;
+                if (!mbar_wait_bounded(&p_full[kb & 1], (uint32_t)((kb >> 1) & 1), p.err, DEV_TC_MMA_TIMEOUT) ||
+                    !mbar_wait_bounded(v_full, (uint32_t)(kb & 1), p.err, DEV_TC_MMA_TIMEOUT)) {
+                    ok = false;
+                    break;
+                }
                 fence_after();
-                // O += Ph Vh + Ph Vl + Pl Vh over 4 k-steps of 16 keys
-                const uint64_t vh = desc128(kv0), vl = desc128(kv0 + 4 * kKTile);
-                const uint64_t pa = desc128(ph0), pb = desc128(pl0);
+                // O += Ph Vh + Ph Vl + Pl Vh over 4 k-steps of 16 keys; P hi / lo in TMEM
+                const uint32_t pb = tmem + kColS + 64u * (uint32_t)(kb & 1);
+                const uint64_t vh = desc128(v0), vl = desc128(v0 + 4 * kKTile);
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
                     const uint64_t adv = (uint64_t)((ks * 32) >> 4);
-                    mma(tmem + kColO, pa + adv, vh + adv, kIdescO, (kb | ks) != 0 ? 1u : 0u);
-                    mma(tmem + kColO, pa + adv, vl + adv, kIdescO, 1u);
-                    mma(tmem + kColO, pb + adv, vh + adv, kIdescO, 1u);
+                    const uint32_t ph = pb + (uint32_t)(ks * 8), pl = pb + 32u + (uint32_t)(ks * 8);
+                    mma_ts(tmem + kColO, ph, vh + adv, kIdescO, (kb | ks) != 0 ? 1u : 0u);
+                    mma_ts(tmem + kColO, ph, vl + adv, kIdescO, 1u);
+                    mma_ts(tmem + kColO, pl, vh + adv, kIdescO, 1u);
                 }
                 commit(pv_done);
             }
-            // before the CTA exits: the loads in flight have landed and every MMA has completed
-            if (pending >= 0) mbar_wait_bounded(kv_full, (uint32_t)pending, p.err, DEV_TC_DRAIN_TIMEOUT);
+            if (!ok) give_up(DEV_TC_MMA_TIMEOUT);
+            // before the CTA exits every MMA has completed
             commit(mma_done);
             mbar_wait_bounded(mma_done, 0u, p.err, DEV_TC_DRAIN_TIMEOUT);
         }
     } else {
         // -------------------------------------------------- softmax rows
-        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-        float m = -INFINITY, l = 0.f;
+        const float scale2 = 1.4426950408889634f / sqrtf((float)kHD);  // log2(e) / sqrt(HD)
+        float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
-            const uint32_t par = (uint32_t)(kb & 1);
-            ok = mbar_wait_bounded(s_full, par, p.err, DEV_TC_EPI_TIMEOUT);
+            const int b = kb & 1;
+            ok = mbar_wait_bounded(&s_full[b], (uint32_t)((kb >> 1) & 1), p.err, DEV_TC_EPI_TIMEOUT);
             ok = __all_sync(0xffffffffu, ok && !aborted());
             if (!ok) {
                 if (lane == 0) give_up(DEV_TC_EPI_TIMEOUT);
                 break;
             }
             fence_after();
+            const uint32_t sb = trow + kColS + 64u * (uint32_t)b;
+            uint32_t r[4][16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ld16_nowait(sb + c * 16, r[c]);
+            ld_wait();
             float s[64];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float v[16];
-                ld16(trow + kColS + c * 16, v);
-#pragma unroll
-                for (int e = 0; e < 16; ++e) s[c * 16 + e] = v[e];
-            }
             float mx = -INFINITY;
+            const int key0 = kb * kN;
+            const bool full = valid && key0 + kN - 1 <= qpos;
 #pragma unroll
             for (int j = 0; j < 64; ++j) {
-                const int key = kb * kN + j;
-                s[j] = (valid && key <= qpos) ? s[j] * scale : -INFINITY;
+                const float x = __uint_as_float(r[j >> 4][j & 15]) * scale2;
+                s[j] = (full || (valid && key0 + j <= qpos)) ? x : -INFINITY;
                 mx = fmaxf(mx, s[j]);
             }
-            const float mn = fmaxf(m, mx);
-            const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+            const bool need = mx > m + kRescaleLog2;
+            float corr = 1.f;
+            if (need) {
+                corr = (m == -INFINITY) ? 0.f : exp2f(m - mx);
+                m = mx;
+            }
+            const float mref = (m == -INFINITY) ? 0.f : m;
             float sum = 0.f;
+            uint32_t ph[32], pl[32];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                s[j] = (s[j] == -INFINITY) ? 0.f : expf(s[j] - mn);
-                sum += s[j];
+            for (int j = 0; j < 64; j += 2) {
+                const float a = exp2f(s[j] - mref), c2 = exp2f(s[j + 1] - mref);
+                sum += a + c2;
+                split2(a, c2, ph[j >> 1], pl[j >> 1]);
             }
             l = l * corr + sum;
-            m = mn;
-            // P as bf16 pairs (the previous PV MMAs, which read P, completed before S did)
-#pragma unroll
-            for (int sg = 0; sg < 8; ++sg) {
-                float v[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = s[sg * 8 + e];
-                put8(Ph, Pl, rho, sg, v);
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            // rescale O when a row's max grew (warp-uniform: tcgen05.ld / st are warp-wide)
-            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll 1
-                for (int c = 0; c < kHD / 16; ++c) {
-                    float v[16];
-                    ld16(trow + kColO + c * 16, v);
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) v[e] *= corr;
-                    st16(trow + kColO + c * 16, v);
+            if (kb > 0) {
+                // every completion of pv_done is confirmed in order, so that each parity
+                // wait names one phase; PV(kb - 1) done also frees O for the rescale
+                ok = mbar_wait_bounded(pv_done, (uint32_t)((kb - 1) & 1), p.err, DEV_TC_EPI_TIMEOUT);
+                ok = __all_sync(0xffffffffu, ok && !aborted());
+                if (!ok) {
+                    if (lane == 0) give_up(DEV_TC_EPI_TIMEOUT);
+                    break;
                 }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                if (__any_sync(0xffffffffu, need)) {
+                    fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < kHD / 16; ++c) {
+                        uint32_t o[16];
+                        ld16_nowait(trow + kColO + c * 16, o);
+                        ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                        st16(trow + kColO + c * 16, o);
+                    }
+                }
             }
+            // P over S(kb): hi in columns 0-31, lo in 32-63 of the buffer
+            st16(sb, &ph[0]);
+            st16(sb + 16, &ph[16]);
+            st16(sb + 32, &pl[0]);
+            st16(sb + 48, &pl[16]);
+            st_wait();
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[b]);
         }
-        if (ok && nkb > 0) {
+        if (ok) {
             ok = mbar_wait_bounded(pv_done, (uint32_t)((nkb - 1) & 1), p.err, DEV_TC_EPI_TIMEOUT);
             ok = __all_sync(0xffffffffu, ok && !aborted());
+            if (!ok && lane == 0) give_up(DEV_TC_EPI_TIMEOUT);
         }
         if (ok) {
             fence_after();
@@ -335,17 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float inv_l = 1.0f / l;
 #pragma unroll 1
             for (int c = 0; c < kHD / 16; ++c) {
-                float v[16];
-                ld16(trow + kColO + c * 16, v);
+                uint32_t o[16];
+                ld16_nowait(trow + kColO + c * 16, o);
+                ld_wait();
                 if (valid) {
                     uint32_t hw[8], lw[8];
 #pragma unroll
                     for (int e = 0; e < 16; e += 2) {
-                        const float x0 = v[e] * inv_l * sigmoid_f(gate[c * 16 + e]);
-                        const float x1 = v[e + 1] * inv_l * sigmoid_f(gate[c * 16 + e + 1]);
-                        const uint16_t h0 = bf16r(x0), h1 = bf16r(x1);
-                        hw[e / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                        lw[e / 2] = (uint32_t)bf16r(x0 - bf16f(h0)) | ((uint32_t)bf16r(x1 - bf16f(h1)) << 16);
+                        const float x0 = __uint_as_float(o[e]) * inv_l * sigmoid_f(gate[c * 16 + e]);
+                        const float x1 = __uint_as_float(o[e + 1]) * inv_l * sigmoid_f(gate[c * 16 + e + 1]);
+                        split2(x0, x1, hw[e / 2], lw[e / 2]);
                     }
                     uint4* dh = reinterpret_cast<uint4*>(row + h * kHD + c * 16);
                     uint4* dl = reinterpret_cast<uint4*>(row + K + h * kHD + c * 16);

@@ -147,6 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int bqt = kM / p.grp;                 // tokens per CTA
     const int t_last = min((qb + 1) * bqt, p.T) - 1;
     const int nkb = (p.p0 + t_last) / kN + 1;  // causal: key blocks up to the last query
+    // Each CTA walks its key blocks from a different start (the online softmax does not
+    // depend on the order), so that the CTAs of a kv head do not all read the same block
+    // from L2 at the same time.
+    const int rot = (qb * 13 + kv * 7) % nkb;
+    auto blk = [&](int kb) { return kb + rot < nkb ? kb + rot : kb + rot - nkb; };
 
     if (threadIdx.x == 0) {
         mbar_init(k_full, 1);
@@ -228,7 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(k_full, kKVBytes);
                 for (int c = 0; c < 4; ++c)
                     for (int hl = 0; hl < 2; ++hl)
-                        tma2d(Kb + (c * 2 + hl) * kKTile, &mapK, hl * kHD + c * 64, kv * p.ctx_pad + kb * kN, k_full);
+                        tma2d(Kb + (c * 2 + hl) * kKTile, &mapK, hl * kHD + c * 64, kv * p.ctx_pad + blk(kb) * kN,
+                              k_full);
                 pending = kb & 1;
             }
             // one load at most is outstanding (the previous one was consumed before this issue)
@@ -247,7 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // hi rows d at [0, 32 KB), lo at [32, 64 KB)
                 for (int hl = 0; hl < 2; ++hl)
                     for (int dc = 0; dc < 4; ++dc)
-                        tma2d(Vb + hl * 4 * kKTile + dc * kKTile, &mapVt, kb * kN, (kv * 2 + hl) * kHD + dc * 64, v_full);
+                        tma2d(Vb + hl * 4 * kKTile + dc * kKTile, &mapVt, blk(kb) * kN, (kv * 2 + hl) * kHD + dc * 64,
+                              v_full);
                 pending = kb & 1;
             }
             if (pending >= 0) mbar_wait_bounded(v_full, (uint32_t)pending, p.err, DEV_TC_DRAIN_TIMEOUT);
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ld_wait();
             float s[64];
             float mx = -INFINITY;
-            const int key0 = kb * kN;
+            const int key0 = blk(kb) * kN;
             const bool full = valid && key0 + kN - 1 <= qpos;
 #pragma unroll
             for (int j = 0; j < 64; ++j) {

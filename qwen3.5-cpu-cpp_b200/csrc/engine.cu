@@ -115,6 +115,7 @@ struct qwc_handle {
     float *pf_hid = nullptr, *pf_proj = nullptr, *pf_o = nullptr, *pf_qn = nullptr, *pf_kn = nullptr,
           *pf_vc = nullptr, *pf_glog = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
     float *pf_u = nullptr, *pf_w = nullptr, *pf_qg = nullptr, *pf_kd = nullptr, *pf_p = nullptr, *pf_gc = nullptr;
+    float* pf_sc = nullptr;  // GDN: [VH][chunk/64][128][128] state entering each 64-token block
     uint16_t *pf_xa = nullptr, *pf_xb = nullptr;
     uint16_t* pf_vsplit = nullptr;  // [NKV][chunk][512] V of the chunk as bf16 pairs
     // tensor-core attention: per attention layer K [NKV][ctx][512] and V^T [NKV][512][ctx]
@@ -1195,7 +1196,8 @@ static int pf_workspace(qwc_handle* h, int cap) {
                  o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 64 * 64 * 4),
                  o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4), o_part = carve(c * h->H * 4),
                  o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2),
-                 o_vs = carve(c * h->NKV * 2 * h->HD * 2);
+                 o_vs = carve(c * h->NKV * 2 * h->HD * 2),
+                 o_sc = carve((size_t)h->VH * ((c + 63) / 64) * 128 * 128 * 4);
     if (cudaMalloc(&h->pf_ws, off) != cudaSuccess) {
         h->pf_ws = nullptr;
         return fail(h, QWC_E_OOM, "prefill workspace allocation failed");
@@ -1222,6 +1224,7 @@ static int pf_workspace(qwc_handle* h, int cap) {
     h->pf_xa = reinterpret_cast<uint16_t*>(b + o_xa);
     h->pf_xb = reinterpret_cast<uint16_t*>(b + o_xb);
     h->pf_vsplit = reinterpret_cast<uint16_t*>(b + o_vs);
+    h->pf_sc = reinterpret_cast<float*>(b + o_sc);
     h->pf_cap = cap;
     return QWC_OK;
 }
@@ -1350,6 +1353,7 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 g.KD = h->pf_kd;
                 g.P = h->pf_p;
                 g.gC = h->pf_gc;
+                g.Sc = h->pf_sc;
                 g.beta = h->pf_beta;
                 g.state = sv.gdn_state + (size_t)lw.idx * h->VH * h->DK * h->DV;
                 g.out = h->pf_o;

@@ -195,6 +195,7 @@ struct PfGdnArgs {
     float* KD = nullptr;          // scratch [VH][T][128]
     float* P = nullptr;           // scratch [VH][ceil(T/64)][64][64]
     float* gC = nullptr;          // scratch [VH][ceil(T/64)]
+    float* Sc = nullptr;          // scratch [VH][ceil(T/64)][128][128] state entering each chunk
     float* state = nullptr;       // [VH][DK][DV], read then updated
     float* out = nullptr;         // [T][VD]
     int T = 0, p0 = 0, KH = 0, VH = 0, C = 0, VD = 0;

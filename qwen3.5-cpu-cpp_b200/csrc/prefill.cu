@@ -168,8 +168,9 @@ __global__ void k_pf_conv_ring(const float* proj, long ldp, int T, int p0, int C
 //   S_C = gamma_C S0 + sum_i Kd_i e_i^T,  Kd_i = b_i exp(G_C - G_i) k_i
 // Every exponent is a difference G_i - G_j <= 0 (or a G_i <= 0), so nothing overflows.
 // Kernel A (parallel over chunks and heads) builds U, W, Gamma Q, Kd, P and gamma_C;
-// kernel B (sequential over chunks, parallel over heads and 32-column slices of S) applies
-// E = U - W S, O = (Gamma Q) S + P E, S = gamma_C S + Kd^T E in fp32 on CUDA cores.
+// kernel B1 (sequential over chunks, parallel over heads and 16-column slices of S) applies
+// E = U - W S, S = gamma_C S + Kd^T E and keeps the state entering each chunk; kernel B2
+// (parallel over chunks and heads) forms O = (Gamma Q) S_c + P E. fp32 on CUDA cores.
 constexpr int kGC = 64;            // tokens per chunk
 constexpr int kGP = 128 + 4;       // padded row stride of 128-wide shared tiles
 constexpr int kGLP = kGC + 1;      // padded row stride of 64 x 64 shared tiles
@@ -187,6 +188,7 @@ struct PfGdnChunk {
     float* KD;           // [VH][T][128]  b_i exp(G_C - G_i) k_i
     float* P;            // [VH][nch][64][64]
     float* gC;           // [VH][nch]
+    float* Sc;           // [VH][nch][DK][DV] state entering each chunk
     float* state;        // [VH][DK][DV]
     float* out;          // [T][VD]
     int T, KH, VH, VD;
@@ -314,129 +316,172 @@ __global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
     }
 }
 
-// Kernel B: (value head, 32-column slice of S) per CTA of 256 threads, chunks in order.
-constexpr int kGS = 32;              // columns of S per CTA
-constexpr int kGSP = kGS + 4;        // padded stride of [.][32] tiles
-constexpr size_t kGdnBSmem = (size_t)(3 * kGC * kGP + kGC * kGLP + 128 * kGSP + 2 * kGC * kGSP) * 4;
-__global__ void __launch_bounds__(256) k_pf_gdn_chunk_b(const PfGdnChunk p) {
+// Kernel B1: the state recurrence across chunks, S_{c+1} = gamma_C S_c + Kd^T (U - W S_c).
+// Columns of S evolve independently, so each CTA owns a (value head, 16-column slice) and
+// walks the chunks in order; the next chunk's W, Kd and U slice are fetched (cp.async)
+// while the current one is applied. It writes the state entering every chunk (for the
+// output kernel B2), E = U - W S_c in place of U, and the final state.
+constexpr int kGS1 = 16;             // columns of S per CTA
+constexpr int kGS1P = kGS1 + 4;      // padded stride of [.][16] tiles
+constexpr int kB1Buf = 2 * kGC * kGP + kGC * kGS1P;  // floats per chunk buffer: W, Kd, U slice
+constexpr size_t kGdnB1Smem = (size_t)(2 * kB1Buf + 128 * kGS1P + kGC * kGS1P) * 4;
+__device__ __forceinline__ void cp16(float* dst, const float* src, bool pred) {
+    const uint32_t d = smem_u32(dst);
+    const int n = pred ? 16 : 0;  // 0: zero fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+__global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
     extern __shared__ __align__(16) float sb[];
-    float* Wsm = sb;                    // [64][132]
-    float* Qsm = Wsm + kGC * kGP;       // [64][132]
-    float* Ksm = Qsm + kGC * kGP;       // [64][132]
-    float* Psm = Ksm + kGC * kGP;       // [64][65]
-    float* Ssm = Psm + kGC * kGLP;      // [128][36]
-    float* Usm = Ssm + 128 * kGSP;      // [64][36] U slice, then E
-    float* Osm = Usm + kGC * kGSP;      // [64][36]
-    const int vh = blockIdx.x / (128 / kGS), sl = blockIdx.x % (128 / kGS), tid = threadIdx.x;
+    float* Ssm = sb + 2 * kB1Buf;        // [128][20]
+    float* Esm = Ssm + 128 * kGS1P;      // [64][20]
+    const int vh = blockIdx.x / (128 / kGS1), sl = blockIdx.x % (128 / kGS1), tid = threadIdx.x;
     const int nch = (p.T + kGC - 1) / kGC;
-    float* Sg = p.state + (size_t)vh * 128 * 128 + sl * kGS;
-    for (int e = tid; e < 128 * (kGS / 4); e += 256) {
-        const int r = e / (kGS / 4), c4 = (e % (kGS / 4)) * 4;
-        *reinterpret_cast<float4*>(Ssm + r * kGSP + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
+    float* Sg = p.state + (size_t)vh * 128 * 128 + sl * kGS1;
+    for (int e = tid; e < 128 * (kGS1 / 4); e += 256) {
+        const int r = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
+        *reinterpret_cast<float4*>(Ssm + r * kGS1P + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
     }
-    // output tiles: rows 2*(tid>>3) .. +1, columns 4*(tid&7) .. +3 (64 x 32)
-    const int oi = (tid >> 3) * 2, oc = (tid & 7) * 4;
-    // state tiles: rows 4*(tid>>3) .. +3, columns 4*(tid&7) .. +3 (128 x 32)
-    const int sr = (tid >> 3) * 4;
+    auto fetch = [&](int c) {
+        float* B = sb + (c & 1) * kB1Buf;
+        const int t0 = c * kGC, n = min(kGC, p.T - t0);
+        const size_t hrow = ((size_t)vh * p.T + t0) * 128;
+        for (int e = tid; e < kGC * 32; e += 256) {
+            const int i = e >> 5, c4 = (e & 31) * 4;
+            const size_t off = hrow + (size_t)(i < n ? i : 0) * 128 + c4;
+            cp16(B + i * kGP + c4, p.W + off, i < n);
+            cp16(B + kGC * kGP + i * kGP + c4, p.KD + off, i < n);
+        }
+        for (int e = tid; e < kGC * (kGS1 / 4); e += 256) {
+            const int i = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
+            cp16(B + 2 * kGC * kGP + i * kGS1P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * kGS1 + c4, i < n);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch(0);
+    // E tile: row tid >> 2, columns 4 (tid & 3) .. +3; state tile: row tid >> 1, columns 8 (tid & 1) .. +7
+    const int ei = tid >> 2, ec = (tid & 3) * 4;
+    const int sr = tid >> 1, sc = (tid & 1) * 8;
     for (int c = 0; c < nch; ++c) {
         const int t0 = c * kGC, n = min(kGC, p.T - t0);
         const size_t hrow = ((size_t)vh * p.T + t0) * 128;
-        __syncthreads();  // previous chunk fully consumed
-        for (int e = tid; e < kGC * 32; e += 256) {
-            const int i = e >> 5, c4 = (e & 31) * 4;
-            float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = w4, k4 = w4;
-            if (i < n) {
-                w4 = *reinterpret_cast<const float4*>(p.W + hrow + (size_t)i * 128 + c4);
-                q4 = *reinterpret_cast<const float4*>(p.QG + hrow + (size_t)i * 128 + c4);
-                k4 = *reinterpret_cast<const float4*>(p.KD + hrow + (size_t)i * 128 + c4);
-            }
-            *reinterpret_cast<float4*>(Wsm + i * kGP + c4) = w4;
-            *reinterpret_cast<float4*>(Qsm + i * kGP + c4) = q4;
-            *reinterpret_cast<float4*>(Ksm + i * kGP + c4) = k4;
+        if (c + 1 < nch) {
+            fetch(c + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        const float* Pg = p.P + ((size_t)vh * nch + c) * kGC * kGC;
-        for (int e = tid; e < kGC * kGC; e += 256) Psm[(e >> 6) * kGLP + (e & 63)] = Pg[e];
-        for (int e = tid; e < kGC * (kGS / 4); e += 256) {
-            const int i = e / (kGS / 4), c4 = (e % (kGS / 4)) * 4;
-            float4 u4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i < n) u4 = *reinterpret_cast<const float4*>(p.U + hrow + (size_t)i * 128 + sl * kGS + c4);
-            *reinterpret_cast<float4*>(Usm + i * kGSP + c4) = u4;
+        __syncthreads();  // chunk c's operands and the state are visible to every thread
+        const float* Wsm = sb + (c & 1) * kB1Buf;
+        const float* Ksm = Wsm + kGC * kGP;
+        const float* Usm = Ksm + kGC * kGP;
+        // the state entering chunk c, for the output kernel
+        float* Scg = p.Sc + ((size_t)vh * nch + c) * 128 * 128 + sl * kGS1;
+        for (int e = tid; e < 128 * (kGS1 / 4); e += 256) {
+            const int r = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
+            *reinterpret_cast<float4*>(Scg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + c4);
         }
-        const float gC = p.gC[(size_t)vh * nch + c];
-        __syncthreads();
-        // E = U - W S and the (Gamma Q) S part of O
+        // E = U - W S
         {
-            float e2[2][4], o2[2][4];
-#pragma unroll
-            for (int a = 0; a < 2; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) { e2[a][b] = 0.f; o2[a][b] = 0.f; }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
             for (int r = 0; r < 128; ++r) {
-                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGSP + oc);
-#pragma unroll
-                for (int a = 0; a < 2; ++a) {
-                    const float w = Wsm[(oi + a) * kGP + r], q = Qsm[(oi + a) * kGP + r];
-                    e2[a][0] += w * s4.x; e2[a][1] += w * s4.y; e2[a][2] += w * s4.z; e2[a][3] += w * s4.w;
-                    o2[a][0] += q * s4.x; o2[a][1] += q * s4.y; o2[a][2] += q * s4.z; o2[a][3] += q * s4.w;
-                }
+                const float w = Wsm[ei * kGP + r];
+                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + ec);
+                acc[0] += w * s4.x; acc[1] += w * s4.y; acc[2] += w * s4.z; acc[3] += w * s4.w;
             }
-#pragma unroll
-            for (int a = 0; a < 2; ++a) {
-                float4* u = reinterpret_cast<float4*>(Usm + (oi + a) * kGSP + oc);
-                const float4 uv = *u;
-                *u = make_float4(uv.x - e2[a][0], uv.y - e2[a][1], uv.z - e2[a][2], uv.w - e2[a][3]);
-                *reinterpret_cast<float4*>(Osm + (oi + a) * kGSP + oc) = make_float4(o2[a][0], o2[a][1], o2[a][2], o2[a][3]);
-            }
+            const float4 u4 = *reinterpret_cast<const float4*>(Usm + ei * kGS1P + ec);
+            const float4 e4 = make_float4(u4.x - acc[0], u4.y - acc[1], u4.z - acc[2], u4.w - acc[3]);
+            *reinterpret_cast<float4*>(Esm + ei * kGS1P + ec) = e4;
+            if (ei < n) *reinterpret_cast<float4*>(p.U + hrow + (size_t)ei * 128 + sl * kGS1 + ec) = e4;
         }
-        __syncthreads();  // E complete (in Usm); S still the chunk's input state
-        // O += P E, written out; S = gamma_C S + Kd^T E
+        __syncthreads();  // E complete; every read of S for E done
+        // S = gamma_C S + Kd^T E (each thread reads and writes only its own S entries here)
         {
-            float o2[2][4];
-#pragma unroll
-            for (int a = 0; a < 2; ++a) {
-                const float4 ov = *reinterpret_cast<const float4*>(Osm + (oi + a) * kGSP + oc);
-                o2[a][0] = ov.x; o2[a][1] = ov.y; o2[a][2] = ov.z; o2[a][3] = ov.w;
-            }
-            for (int j = 0; j <= oi + 1 && j < kGC; ++j) {
-                const float4 e4 = *reinterpret_cast<const float4*>(Usm + j * kGSP + oc);
-#pragma unroll
-                for (int a = 0; a < 2; ++a) {
-                    const float pv = Psm[(oi + a) * kGLP + j];
-                    o2[a][0] += pv * e4.x; o2[a][1] += pv * e4.y; o2[a][2] += pv * e4.z; o2[a][3] += pv * e4.w;
-                }
-            }
-#pragma unroll
-            for (int a = 0; a < 2; ++a) {
-                const int i = oi + a;
-                if (i < n)
-                    *reinterpret_cast<float4*>(p.out + (size_t)(t0 + i) * p.VD + vh * 128 + sl * kGS + oc) =
-                        make_float4(o2[a][0], o2[a][1], o2[a][2], o2[a][3]);
-            }
-            float s4[4][4];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                const float4 sv = *reinterpret_cast<const float4*>(Ssm + (sr + a) * kGSP + oc);
-                s4[a][0] = gC * sv.x; s4[a][1] = gC * sv.y; s4[a][2] = gC * sv.z; s4[a][3] = gC * sv.w;
-            }
+            const float gC = p.gC[(size_t)vh * nch + c];
+            float acc[8];
+            const float4 s0 = *reinterpret_cast<const float4*>(Ssm + sr * kGS1P + sc);
+            const float4 s1 = *reinterpret_cast<const float4*>(Ssm + sr * kGS1P + sc + 4);
+            acc[0] = gC * s0.x; acc[1] = gC * s0.y; acc[2] = gC * s0.z; acc[3] = gC * s0.w;
+            acc[4] = gC * s1.x; acc[5] = gC * s1.y; acc[6] = gC * s1.z; acc[7] = gC * s1.w;
             for (int i = 0; i < n; ++i) {
-                const float4 e4 = *reinterpret_cast<const float4*>(Usm + i * kGSP + oc);
-                const float4 k4 = *reinterpret_cast<const float4*>(Ksm + i * kGP + sr);
-                const float kr[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    s4[a][0] += kr[a] * e4.x; s4[a][1] += kr[a] * e4.y; s4[a][2] += kr[a] * e4.z; s4[a][3] += kr[a] * e4.w;
-                }
+                const float kd = Ksm[i * kGP + sr];
+                const float4 e0 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc);
+                const float4 e1 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc + 4);
+                acc[0] += kd * e0.x; acc[1] += kd * e0.y; acc[2] += kd * e0.z; acc[3] += kd * e0.w;
+                acc[4] += kd * e1.x; acc[5] += kd * e1.y; acc[6] += kd * e1.z; acc[7] += kd * e1.w;
             }
-            __syncthreads();  // every read of the old S (above, other threads) is done
+            *reinterpret_cast<float4*>(Ssm + sr * kGS1P + sc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            *reinterpret_cast<float4*>(Ssm + sr * kGS1P + sc + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        }
+        __syncthreads();  // new S visible; chunk c's buffer free for the fetch of chunk c + 2
+    }
+    for (int e = tid; e < 128 * (kGS1 / 4); e += 256) {
+        const int r = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
+        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + c4);
+    }
+}
+
+// Kernel B2: outputs of every chunk in parallel, O = (Gamma Q) S_c + P E; CTA = (chunk,
+// value head, 64-column half), 4 x 4 output tile per thread.
+constexpr int kGOP = 64 + 4;
+constexpr size_t kGdnB2Smem = (size_t)(128 * kGOP + kGC * kGP + kGC * kGLP + kGC * kGOP) * 4;
+__global__ void __launch_bounds__(256) k_pf_gdn_out(const PfGdnChunk p) {
+    extern __shared__ __align__(16) float so[];
+    float* Ssm = so;                     // [128][68]
+    float* Qsm = Ssm + 128 * kGOP;       // [64][132]
+    float* Psm = Qsm + kGC * kGP;        // [64][65]
+    float* Esm = Psm + kGC * kGLP;       // [64][68]
+    const int c = blockIdx.x, vh = blockIdx.y, half = blockIdx.z, tid = threadIdx.x;
+    const int nch = gridDim.x;
+    const int t0 = c * kGC, n = min(kGC, p.T - t0);
+    const size_t hrow = ((size_t)vh * p.T + t0) * 128;
+    const float* Scg = p.Sc + ((size_t)vh * nch + c) * 128 * 128 + half * 64;
+    for (int e = tid; e < 128 * 16; e += 256) {
+        const int r = e >> 4, c4 = (e & 15) * 4;
+        *reinterpret_cast<float4*>(Ssm + r * kGOP + c4) = *reinterpret_cast<const float4*>(Scg + (size_t)r * 128 + c4);
+    }
+    for (int e = tid; e < kGC * 32; e += 256) {
+        const int i = e >> 5, c4 = (e & 31) * 4;
+        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n) q4 = *reinterpret_cast<const float4*>(p.QG + hrow + (size_t)i * 128 + c4);
+        *reinterpret_cast<float4*>(Qsm + i * kGP + c4) = q4;
+    }
+    for (int e = tid; e < kGC * 16; e += 256) {
+        const int i = e >> 4, c4 = (e & 15) * 4;
+        float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n) e4 = *reinterpret_cast<const float4*>(p.U + hrow + (size_t)i * 128 + half * 64 + c4);
+        *reinterpret_cast<float4*>(Esm + i * kGOP + c4) = e4;
+    }
+    const float* Pg = p.P + ((size_t)vh * nch + c) * kGC * kGC;
+    for (int e = tid; e < kGC * kGC; e += 256) Psm[(e >> 6) * kGLP + (e & 63)] = Pg[e];
+    __syncthreads();
+    const int oi = (tid >> 4) * 4, oc = (tid & 15) * 4;
+    float acc[4][4];
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
-                *reinterpret_cast<float4*>(Ssm + (sr + a) * kGSP + oc) = make_float4(s4[a][0], s4[a][1], s4[a][2], s4[a][3]);
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int r = 0; r < 128; ++r) {
+        const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGOP + oc);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const float q = Qsm[(oi + a) * kGP + r];
+            acc[a][0] += q * s4.x; acc[a][1] += q * s4.y; acc[a][2] += q * s4.z; acc[a][3] += q * s4.w;
         }
     }
-    __syncthreads();
-    for (int e = tid; e < 128 * (kGS / 4); e += 256) {
-        const int r = e / (kGS / 4), c4 = (e % (kGS / 4)) * 4;
-        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * kGSP + c4);
+    for (int j = 0; j <= oi + 3; ++j) {  // P is lower triangular (zero above the diagonal)
+        const float4 e4 = *reinterpret_cast<const float4*>(Esm + j * kGOP + oc);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const float pv = Psm[(oi + a) * kGLP + j];
+            acc[a][0] += pv * e4.x; acc[a][1] += pv * e4.y; acc[a][2] += pv * e4.z; acc[a][3] += pv * e4.w;
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int i = oi + a;
+        if (i < n)
+            *reinterpret_cast<float4*>(p.out + (size_t)(t0 + i) * p.VD + vh * 128 + half * 64 + oc) =
+                make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
     }
 }
 
@@ -762,23 +807,28 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
                  a.glog, a.beta, a.p0, a.KH, a.VH, a.C, a.VD};
     k_pf_gdn_prep<<<a.T, kPT, 0, s>>>(pp);
     k_pf_conv_ring<<<(a.C + 255) / 256, 256, 0, s>>>(a.proj, a.ldp, a.T, a.p0, a.C, a.ring);
-    PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.state, a.out,
+    if (!a.Sc) return cudaErrorInvalidValue;
+    PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.Sc, a.state, a.out,
                   a.T, a.KH, a.VH, a.VD};
     {
         cudaError_t e = cudaFuncSetAttribute(k_pf_gdn_chunk_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnASmem);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_pf_gdn_chunk_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnBSmem);
+            e = cudaFuncSetAttribute(k_pf_gdn_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnB1Smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_pf_gdn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnB2Smem);
         if (e != cudaSuccess) return e;
     }
     const int nch = (a.T + kGC - 1) / kGC;
     k_pf_gdn_chunk_a<<<dim3(nch, a.VH), 256, kGdnASmem, s>>>(ck);
-    k_pf_gdn_chunk_b<<<a.VH * (128 / kGS), 256, kGdnBSmem, s>>>(ck);
+    k_pf_gdn_state<<<a.VH * (128 / kGS1), 256, kGdnB1Smem, s>>>(ck);
+    k_pf_gdn_out<<<dim3(nch, a.VH, 2), 256, kGdnB2Smem, s>>>(ck);
     return cudaGetLastError();
 }
 size_t pf_gdn_workspace_bytes(int KH, int VH, int T) {
     const size_t t = (size_t)T, nch = (t + kGC - 1) / kGC, KD = (size_t)KH * 128, VD = (size_t)VH * 128;
     auto r = [](size_t b) { return (b + 255) / 256 * 256; };
-    return 2 * r(t * KD * 4) + 5 * r(t * VD * 4) + 2 * r(t * VH * 4) + r(VH * nch * kGC * kGC * 4) + r(VH * nch * 4);
+    return 2 * r(t * KD * 4) + 5 * r(t * VD * 4) + 2 * r(t * VH * 4) + r(VH * nch * kGC * kGC * 4) + r(VH * nch * 4) +
+           r(VH * nch * 128 * 128 * 4);
 }
 int pf_gdn_carve(PfGdnArgs& a, void* ws, size_t bytes) {
     const size_t t = (size_t)a.T, nch = (t + kGC - 1) / kGC, KD = (size_t)a.KH * 128, VD = (size_t)a.VH * 128;
@@ -801,6 +851,7 @@ int pf_gdn_carve(PfGdnArgs& a, void* ws, size_t bytes) {
     a.beta = take(t * a.VH);
     a.P = take(a.VH * nch * kGC * kGC);
     a.gC = take(a.VH * nch);
+    a.Sc = take(a.VH * nch * 128 * 128);
     return 0;
 }
 

@@ -114,8 +114,9 @@ struct qwc_handle {
     int* pf_ids = nullptr;
     float *pf_hid = nullptr, *pf_proj = nullptr, *pf_o = nullptr, *pf_qn = nullptr, *pf_kn = nullptr,
           *pf_vc = nullptr, *pf_glog = nullptr, *pf_beta = nullptr, *pf_qbuf = nullptr, *pf_logits = nullptr;
-    float *pf_u = nullptr, *pf_w = nullptr, *pf_qg = nullptr, *pf_kd = nullptr, *pf_p = nullptr, *pf_gc = nullptr;
-    float* pf_sc = nullptr;  // GDN: [VH][chunk/64][128][128] state entering each 64-token block
+    float *pf_u = nullptr, *pf_w = nullptr, *pf_kd = nullptr, *pf_gc = nullptr;
+    // GDN bf16-pair operands of the tensor-core output kernel: Gamma Q, P, S^T and E^T
+    uint16_t *pf_qg = nullptr, *pf_p = nullptr, *pf_st = nullptr, *pf_et = nullptr;
     uint16_t *pf_xa = nullptr, *pf_xb = nullptr;
     uint16_t* pf_vsplit = nullptr;  // [NKV][chunk][512] V of the chunk as bf16 pairs
     // tensor-core attention: per attention layer K [NKV][ctx][512] and V^T [NKV][512][ctx]
@@ -1192,12 +1193,13 @@ static int pf_workspace(qwc_handle* h, int cap) {
                  o_o = carve(c * h->VD * 4), o_qn = carve(c * h->KD * 4), o_kn = carve(c * h->KD * 4),
                  o_vc = carve(c * h->VD * 4), o_dec = carve(c * h->VH * 4), o_beta = carve(c * h->VH * 4),
                  o_qbuf = carve(c * h->NQ * h->HD * 4), o_log = carve((size_t)kPfLogitRows * h->V * 4),
-                 o_u = carve(c * h->VD * 4), o_w = carve(c * h->VD * 4), o_qg = carve(c * h->VD * 4),
-                 o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 64 * 64 * 4),
+                 o_u = carve(c * h->VD * 4), o_w = carve(c * h->VD * 4), o_qg = carve((c + 63) / 64 * 64 * h->VD * 4),
+                 o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 2 * 64 * 64 * 2),
                  o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4), o_part = carve(c * h->H * 4),
                  o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2),
                  o_vs = carve(c * h->NKV * 2 * h->HD * 2),
-                 o_sc = carve((size_t)h->VH * ((c + 63) / 64) * 128 * 128 * 4);
+                 o_st = carve((size_t)h->VH * ((c + 63) / 64) * 2 * 128 * 128 * 2),
+                 o_et = carve((size_t)h->VH * ((c + 63) / 64) * 2 * 128 * 64 * 2);
     if (cudaMalloc(&h->pf_ws, off) != cudaSuccess) {
         h->pf_ws = nullptr;
         return fail(h, QWC_E_OOM, "prefill workspace allocation failed");
@@ -1213,9 +1215,9 @@ static int pf_workspace(qwc_handle* h, int cap) {
     h->pf_glog = reinterpret_cast<float*>(b + o_dec);
     h->pf_u = reinterpret_cast<float*>(b + o_u);
     h->pf_w = reinterpret_cast<float*>(b + o_w);
-    h->pf_qg = reinterpret_cast<float*>(b + o_qg);
+    h->pf_qg = reinterpret_cast<uint16_t*>(b + o_qg);
     h->pf_kd = reinterpret_cast<float*>(b + o_kd);
-    h->pf_p = reinterpret_cast<float*>(b + o_p);
+    h->pf_p = reinterpret_cast<uint16_t*>(b + o_p);
     h->pf_gc = reinterpret_cast<float*>(b + o_gc);
     h->pf_part = reinterpret_cast<float*>(b + o_part);
     h->pf_beta = reinterpret_cast<float*>(b + o_beta);
@@ -1224,7 +1226,8 @@ static int pf_workspace(qwc_handle* h, int cap) {
     h->pf_xa = reinterpret_cast<uint16_t*>(b + o_xa);
     h->pf_xb = reinterpret_cast<uint16_t*>(b + o_xb);
     h->pf_vsplit = reinterpret_cast<uint16_t*>(b + o_vs);
-    h->pf_sc = reinterpret_cast<float*>(b + o_sc);
+    h->pf_st = reinterpret_cast<uint16_t*>(b + o_st);
+    h->pf_et = reinterpret_cast<uint16_t*>(b + o_et);
     h->pf_cap = cap;
     return QWC_OK;
 }
@@ -1353,7 +1356,9 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 g.KD = h->pf_kd;
                 g.P = h->pf_p;
                 g.gC = h->pf_gc;
-                g.Sc = h->pf_sc;
+                g.ST = h->pf_st;
+                g.ET = h->pf_et;
+                g.err = h->dev_err;
                 g.beta = h->pf_beta;
                 g.state = sv.gdn_state + (size_t)lw.idx * h->VH * h->DK * h->DV;
                 g.out = h->pf_o;

@@ -191,11 +191,13 @@ struct PfGdnArgs {
     float* beta = nullptr;        // scratch [T][VH]
     float* U = nullptr;           // scratch [VH][T][128]  (chunked WY form)
     float* W = nullptr;           // scratch [VH][T][128]
-    float* QG = nullptr;          // scratch [VH][T][128]
+    uint16_t* QG = nullptr;       // scratch [VH][2][ceil(T/64)*64][128] bf16 pairs
     float* KD = nullptr;          // scratch [VH][T][128]
-    float* P = nullptr;           // scratch [VH][ceil(T/64)][64][64]
+    uint16_t* P = nullptr;        // scratch [VH][ceil(T/64)][2][64][64] bf16 pairs
     float* gC = nullptr;          // scratch [VH][ceil(T/64)]
-    float* Sc = nullptr;          // scratch [VH][ceil(T/64)][128][128] state entering each chunk
+    uint16_t* ST = nullptr;       // scratch [VH][ceil(T/64)][2][128][128] bf16 pairs
+    uint16_t* ET = nullptr;       // scratch [VH][ceil(T/64)][2][128][64] bf16 pairs
+    int* err = nullptr;           // device error word of the tensor-core kernel
     float* state = nullptr;       // [VH][DK][DV], read then updated
     float* out = nullptr;         // [T][VD]
     int T = 0, p0 = 0, KH = 0, VH = 0, C = 0, VD = 0;

@@ -11,6 +11,7 @@
 #include "attn_body.cuh"
 #include "common.cuh"
 #include "gdn_body.cuh"
+#include "tc_util.cuh"
 #include "kernels.h"
 
 namespace qwc {
@@ -184,15 +185,21 @@ struct PfGdnChunk {
     const float* beta;   // [T][VH]
     float* U;            // [VH][T][128]
     float* W;            // [VH][T][128]
-    float* QG;           // [VH][T][128]  gamma_i q_i
+    uint16_t* QG;        // [VH][hi|lo][Tpad][128]  gamma_i q_i as bf16 pairs
     float* KD;           // [VH][T][128]  b_i exp(G_C - G_i) k_i
-    float* P;            // [VH][nch][64][64]
+    uint16_t* P;         // [VH][nch][hi|lo][64][64] bf16 pairs
     float* gC;           // [VH][nch]
-    float* Sc;           // [VH][nch][DK][DV] state entering each chunk
+    uint16_t* ST;        // [VH][nch][hi|lo][DV][DK] transposed state entering each chunk, bf16 pairs
+    uint16_t* ET;        // [VH][nch][hi|lo][DV][64]  E^T of each chunk, bf16 pairs
     float* state;        // [VH][DK][DV]
     float* out;          // [T][VD]
     int T, KH, VH, VD;
 };
+// x -> bf16 hi and lo (x = hi + lo within 2^-17 |x|)
+__device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
+    hi = f2bf(x);
+    lo = f2bf(x - bf16lo(hi));
+}
 
 __global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
     extern __shared__ __align__(16) float sa[];
@@ -285,11 +292,23 @@ __global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
         const float fd = Bs[i] * expf(GC - Gc[i]), fg = expf(Gc[i]);
         *reinterpret_cast<float4*>(p.KD + hrow + (size_t)i * 128 + c4) =
             make_float4(fd * k4.x, fd * k4.y, fd * k4.z, fd * k4.w);
-        *reinterpret_cast<float4*>(p.QG + hrow + (size_t)i * 128 + c4) =
-            make_float4(fg * q4.x, fg * q4.y, fg * q4.z, fg * q4.w);
+        const float g4[4] = {fg * q4.x, fg * q4.y, fg * q4.z, fg * q4.w};
+        uint16_t hq[4], lq[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) split_bf16(g4[u], hq[u], lq[u]);
+        const size_t qrow = (size_t)nch * kGC;  // padded token rows of a plane
+        uint16_t* qh = p.QG + ((size_t)vh * 2 * qrow + t0 + i) * 128 + c4;
+        *reinterpret_cast<uint2*>(qh) = make_uint2(hq[0] | ((uint32_t)hq[1] << 16), hq[2] | ((uint32_t)hq[3] << 16));
+        *reinterpret_cast<uint2*>(qh + qrow * 128) =
+            make_uint2(lq[0] | ((uint32_t)lq[1] << 16), lq[2] | ((uint32_t)lq[3] << 16));
     }
-    float* Pg = p.P + ((size_t)vh * nch + c) * kGC * kGC;
-    for (int e = tid; e < kGC * kGC; e += 256) Pg[e] = Ps[(e >> 6) * kGLP + (e & 63)];
+    uint16_t* Pg = p.P + ((size_t)vh * nch + c) * 2 * kGC * kGC;
+    for (int e = tid; e < kGC * kGC; e += 256) {
+        uint16_t hp, lp;
+        split_bf16(Ps[(e >> 6) * kGLP + (e & 63)], hp, lp);
+        Pg[e] = hp;
+        Pg[kGC * kGC + e] = lp;
+    }
     if (tid == 0) p.gC[(size_t)vh * nch + c] = expf(GC);
     __syncthreads();
     for (int e = tid; e < kGC * 128; e += 256) {
@@ -319,8 +338,9 @@ __global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
 // Kernel B1: the state recurrence across chunks, S_{c+1} = gamma_C S_c + Kd^T (U - W S_c).
 // Columns of S evolve independently, so each CTA owns a (value head, 16-column slice) and
 // walks the chunks in order; the next chunk's W, Kd and U slice are fetched (cp.async)
-// while the current one is applied. It writes the state entering every chunk (for the
-// output kernel B2), E = U - W S_c in place of U, and the final state.
+// while the current one is applied. For the output kernel B2 it writes the state entering
+// every chunk and E = U - W S_c, both transposed (value dims as rows) as bf16 pairs; then
+// the final state.
 constexpr int kGS1 = 16;             // columns of S per CTA
 constexpr int kGS1P = kGS1 + 4;      // padded stride of [.][16] tiles
 constexpr int kB1Buf = 2 * kGC * kGP + kGC * kGS1P;  // floats per chunk buffer: W, Kd, U slice
@@ -362,8 +382,7 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
     const int ei = tid >> 2, ec = (tid & 3) * 4;
     const int sr = tid >> 1, sc = (tid & 1) * 8;
     for (int c = 0; c < nch; ++c) {
-        const int t0 = c * kGC, n = min(kGC, p.T - t0);
-        const size_t hrow = ((size_t)vh * p.T + t0) * 128;
+        const int n = min(kGC, p.T - c * kGC);
         if (c + 1 < nch) {
             fetch(c + 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
@@ -374,11 +393,22 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         const float* Wsm = sb + (c & 1) * kB1Buf;
         const float* Ksm = Wsm + kGC * kGP;
         const float* Usm = Ksm + kGC * kGP;
-        // the state entering chunk c, for the output kernel
-        float* Scg = p.Sc + ((size_t)vh * nch + c) * 128 * 128 + sl * kGS1;
-        for (int e = tid; e < 128 * (kGS1 / 4); e += 256) {
-            const int r = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
-            *reinterpret_cast<float4*>(Scg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + c4);
+        // the state entering chunk c, transposed (rows = value dims) as bf16 pairs, for the
+        // output kernel: thread -> value dim dv = tid / 16 of the slice, key dims 8 (tid % 16) ..
+        {
+            const int dv = tid >> 4, k0 = (tid & 15) * 8;
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                uint16_t h0, l0, h1, l1;
+                split_bf16(Ssm[(k0 + 2 * u) * kGS1P + dv], h0, l0);
+                split_bf16(Ssm[(k0 + 2 * u + 1) * kGS1P + dv], h1, l1);
+                hw[u] = h0 | ((uint32_t)h1 << 16);
+                lw[u] = l0 | ((uint32_t)l1 << 16);
+            }
+            uint16_t* st = p.ST + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + dv) * 128 + k0;
+            *reinterpret_cast<uint4*>(st) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(st + 128 * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
         // E = U - W S
         {
@@ -391,9 +421,20 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             const float4 u4 = *reinterpret_cast<const float4*>(Usm + ei * kGS1P + ec);
             const float4 e4 = make_float4(u4.x - acc[0], u4.y - acc[1], u4.z - acc[2], u4.w - acc[3]);
             *reinterpret_cast<float4*>(Esm + ei * kGS1P + ec) = e4;
-            if (ei < n) *reinterpret_cast<float4*>(p.U + hrow + (size_t)ei * 128 + sl * kGS1 + ec) = e4;
         }
         __syncthreads();  // E complete; every read of S for E done
+        // E^T of the slice as bf16 pairs (rows = value dims, 64 token columns; rows past the
+        // chunk's tokens are zero): thread -> dv = tid / 16, tokens 4 (tid % 16) ..
+        {
+            const int dv = tid >> 4, j0 = (tid & 15) * 4;
+            uint16_t hh[4], ll[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) split_bf16(Esm[(j0 + u) * kGS1P + dv], hh[u], ll[u]);
+            uint16_t* et = p.ET + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + dv) * kGC + j0;
+            *reinterpret_cast<uint2*>(et) = make_uint2(hh[0] | ((uint32_t)hh[1] << 16), hh[2] | ((uint32_t)hh[3] << 16));
+            *reinterpret_cast<uint2*>(et + 128 * kGC) =
+                make_uint2(ll[0] | ((uint32_t)ll[1] << 16), ll[2] | ((uint32_t)ll[3] << 16));
+        }
         // S = gamma_C S + Kd^T E (each thread reads and writes only its own S entries here)
         {
             const float gC = p.gC[(size_t)vh * nch + c];
@@ -420,68 +461,112 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
     }
 }
 
-// Kernel B2: outputs of every chunk in parallel, O = (Gamma Q) S_c + P E; CTA = (chunk,
-// value head, 64-column half), 4 x 4 output tile per thread.
-constexpr int kGOP = 64 + 4;
-constexpr size_t kGdnB2Smem = (size_t)(128 * kGOP + kGC * kGP + kGC * kGLP + kGC * kGOP) * 4;
-__global__ void __launch_bounds__(256) k_pf_gdn_out(const PfGdnChunk p) {
-    extern __shared__ __align__(16) float so[];
-    float* Ssm = so;                     // [128][68]
-    float* Qsm = Ssm + 128 * kGOP;       // [64][132]
-    float* Psm = Qsm + kGC * kGP;        // [64][65]
-    float* Esm = Psm + kGC * kGLP;       // [64][68]
-    const int c = blockIdx.x, vh = blockIdx.y, half = blockIdx.z, tid = threadIdx.x;
-    const int nch = gridDim.x;
-    const int t0 = c * kGC, n = min(kGC, p.T - t0);
-    const size_t hrow = ((size_t)vh * p.T + t0) * 128;
-    const float* Scg = p.Sc + ((size_t)vh * nch + c) * 128 * 128 + half * 64;
-    for (int e = tid; e < 128 * 16; e += 256) {
-        const int r = e >> 4, c4 = (e & 15) * 4;
-        *reinterpret_cast<float4*>(Ssm + r * kGOP + c4) = *reinterpret_cast<const float4*>(Scg + (size_t)r * 128 + c4);
+// Kernel B2 on the tensor cores: per (chunk, value head) the outputs, transposed,
+//   O^T [128 value dims][64 tokens] = S_c^T (Gamma Q)^T + E^T P^T,
+// each product with bf16-pair operands taken three times (hi hi + hi lo + lo hi) into an
+// fp32 accumulator in tensor memory (64 columns): 24 + 12 MMAs of M128 N64 K16. Operands
+// arrive by TMA (no multicast), all K-major with 128-byte swizzle: S_c^T [128][128] and
+// E^T [128][64] as A, Gamma Q [64 tokens][128] and P [64][64] as B. Thread = value dim
+// (its TMEM lane) in the epilogue; a warp's 32 lanes store 32 consecutive outputs.
+constexpr uint32_t kT128 = 128 * 128;  // bytes of a 128-row x 64-column bf16 tile
+constexpr uint32_t kT64 = 64 * 128;    // bytes of a 64-row x 64-column bf16 tile
+constexpr uint32_t kGdnOutBytes = 4 * kT128 + 4 * kT64 + 2 * kT128 + 2 * kT64;
+constexpr size_t kGdnOutSmem = kGdnOutBytes + 1024 + 64;
+__global__ void __launch_bounds__(128, 1)
+    k_pf_gdn_out_tc(const __grid_constant__ CUtensorMap mST, const __grid_constant__ CUtensorMap mQG,
+                    const __grid_constant__ CUtensorMap mET, const __grid_constant__ CUtensorMap mP, const PfGdnChunk p,
+                    int* err) {
+    extern __shared__ uint8_t so_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(so_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* A1 = sm;                // S^T tiles [hi|lo][key dims 0-63 | 64-127]
+    uint8_t* B1 = A1 + 4 * kT128;    // Gamma Q tiles [hi|lo][key dims 0-63 | 64-127]
+    uint8_t* A2 = B1 + 4 * kT64;     // E^T tiles [hi|lo]
+    uint8_t* B2 = A2 + 2 * kT128;    // P tiles [hi|lo]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(B2 + 2 * kT64);
+    uint64_t* full = bar;
+    uint64_t* done = bar + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+    int* s_ok = reinterpret_cast<int*>(tmem_slot + 1);
+    const int c = blockIdx.x, vh = blockIdx.y, nch = gridDim.x, tid = threadIdx.x, warp = tid >> 5;
+    const int t0 = c * kGC, n = min(kGC, p.T - t0), Tpad = nch * kGC;
+    if (tid == 0) {
+        mbar_init(full, 1);
+        mbar_init(done, 1);
+        *s_ok = 1;
+        fence_mbar_init();
     }
-    for (int e = tid; e < kGC * 32; e += 256) {
-        const int i = e >> 5, c4 = (e & 31) * 4;
-        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n) q4 = *reinterpret_cast<const float4*>(p.QG + hrow + (size_t)i * 128 + c4);
-        *reinterpret_cast<float4*>(Qsm + i * kGP + c4) = q4;
-    }
-    for (int e = tid; e < kGC * 16; e += 256) {
-        const int i = e >> 4, c4 = (e & 15) * 4;
-        float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n) e4 = *reinterpret_cast<const float4*>(p.U + hrow + (size_t)i * 128 + half * 64 + c4);
-        *reinterpret_cast<float4*>(Esm + i * kGOP + c4) = e4;
-    }
-    const float* Pg = p.P + ((size_t)vh * nch + c) * kGC * kGC;
-    for (int e = tid; e < kGC * kGC; e += 256) Psm[(e >> 6) * kGLP + (e & 63)] = Pg[e];
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 64);
+    tc::fence_before();
     __syncthreads();
-    const int oi = (tid >> 4) * 4, oc = (tid & 15) * 4;
-    float acc[4][4];
+    tc::fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(full, kGdnOutBytes);
+        const int rs = (vh * nch + c) * 2 * 128;  // hi row of S^T / E^T
+        const int rq = vh * 2 * Tpad + t0;        // hi row of Gamma Q
+        const int rp = (vh * nch + c) * 2 * kGC;  // hi row of P
+        for (int hl = 0; hl < 2; ++hl) {
+            for (int kc = 0; kc < 2; ++kc) {
+                tc::tma2d(A1 + (hl * 2 + kc) * kT128, &mST, kc * 64, rs + hl * 128, full);
+                tc::tma2d(B1 + (hl * 2 + kc) * kT64, &mQG, kc * 64, rq + hl * Tpad, full);
+            }
+            tc::tma2d(A2 + hl * kT128, &mET, 0, rs + hl * 128, full);
+            tc::tma2d(B2 + hl * kT64, &mP, 0, rp + hl * kGC, full);
+        }
+        if (mbar_wait_bounded(full, 0u, err, DEV_TC_MMA_TIMEOUT)) {
+            tc::fence_after();
+            constexpr uint32_t idesc = tc::idesc_bf16(128, 64);
+            const uint32_t a1 = smem_u32(A1), b1 = smem_u32(B1), a2 = smem_u32(A2), b2 = smem_u32(B2);
+            for (int kc = 0; kc < 2; ++kc) {
+                const uint64_t ah = tc::desc128(a1 + kc * kT128), al = tc::desc128(a1 + (2 + kc) * kT128);
+                const uint64_t bh = tc::desc128(b1 + kc * kT64), bl = tc::desc128(b1 + (2 + kc) * kT64);
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+                    tc::mma_ss(tmem, ah + adv, bh + adv, idesc, (kc | ks) != 0 ? 1u : 0u);
+                    tc::mma_ss(tmem, ah + adv, bl + adv, idesc, 1u);
+                    tc::mma_ss(tmem, al + adv, bh + adv, idesc, 1u);
+                }
+            }
+            const uint64_t ah = tc::desc128(a2), al = tc::desc128(a2 + kT128);
+            const uint64_t bh = tc::desc128(b2), bl = tc::desc128(b2 + kT64);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-    for (int r = 0; r < 128; ++r) {
-        const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGOP + oc);
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+                tc::mma_ss(tmem, ah + adv, bh + adv, idesc, 1u);
+                tc::mma_ss(tmem, ah + adv, bl + adv, idesc, 1u);
+                tc::mma_ss(tmem, al + adv, bh + adv, idesc, 1u);
+            }
+        } else {
+            *reinterpret_cast<volatile int*>(s_ok) = 0;
+            mbar_wait_bounded(full, 0u, err, DEV_TC_DRAIN_TIMEOUT);  // loads in flight land first
+        }
+        tc::commit(done);  // arrives once every MMA above has completed
+    }
+    bool ok = mbar_wait_bounded(done, 0u, err, DEV_TC_EPI_TIMEOUT);
+    ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(s_ok) != 0);
+    if (ok) {
+        tc::fence_after();
+        const int dv = warp * 32 + (tid & 31);
+        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+        float* o = p.out + (size_t)t0 * p.VD + vh * 128 + dv;
+#pragma unroll 1
+        for (int q = 0; q < 4; ++q) {
+            uint32_t r[16];
+            tc::ld16_nowait(taddr + q * 16, r);
+            tc::ld_wait();
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            const float q = Qsm[(oi + a) * kGP + r];
-            acc[a][0] += q * s4.x; acc[a][1] += q * s4.y; acc[a][2] += q * s4.z; acc[a][3] += q * s4.w;
+            for (int e = 0; e < 16; ++e) {
+                const int t = q * 16 + e;
+                if (t < n) o[(size_t)t * p.VD] = __uint_as_float(r[e]);
+            }
         }
     }
-    for (int j = 0; j <= oi + 3; ++j) {  // P is lower triangular (zero above the diagonal)
-        const float4 e4 = *reinterpret_cast<const float4*>(Esm + j * kGOP + oc);
-#pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            const float pv = Psm[(oi + a) * kGLP + j];
-            acc[a][0] += pv * e4.x; acc[a][1] += pv * e4.y; acc[a][2] += pv * e4.z; acc[a][3] += pv * e4.w;
-        }
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int i = oi + a;
-        if (i < n)
-            *reinterpret_cast<float4*>(p.out + (size_t)(t0 + i) * p.VD + vh * 128 + half * 64 + oc) =
-                make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::tmem_dealloc(tmem, 64);
     }
 }
 
@@ -807,51 +892,72 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
                  a.glog, a.beta, a.p0, a.KH, a.VH, a.C, a.VD};
     k_pf_gdn_prep<<<a.T, kPT, 0, s>>>(pp);
     k_pf_conv_ring<<<(a.C + 255) / 256, 256, 0, s>>>(a.proj, a.ldp, a.T, a.p0, a.C, a.ring);
-    if (!a.Sc) return cudaErrorInvalidValue;
-    PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.Sc, a.state, a.out,
+    if (!a.ST || !a.ET || !a.QG || !a.P) return cudaErrorInvalidValue;
+    PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.ST, a.ET, a.state, a.out,
                   a.T, a.KH, a.VH, a.VD};
     {
         cudaError_t e = cudaFuncSetAttribute(k_pf_gdn_chunk_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnASmem);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_pf_gdn_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnB1Smem);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_pf_gdn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnB2Smem);
+            e = cudaFuncSetAttribute(k_pf_gdn_out_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnOutSmem);
         if (e != cudaSuccess) return e;
     }
     const int nch = (a.T + kGC - 1) / kGC;
+    const long Tpad = (long)nch * kGC, pl = (long)a.VH * nch * 2;
+    CUtensorMap mST, mQG, mET, mP;
+    if (tc_make_map_box(&mST, a.ST, pl * 128, 128, 128, 128) || tc_make_map_box(&mQG, a.QG, 2L * a.VH * Tpad, 128, 128, 64) ||
+        tc_make_map_box(&mET, a.ET, pl * 128, kGC, kGC, 128) || tc_make_map_box(&mP, a.P, pl * kGC, kGC, kGC, 64))
+        return cudaErrorInvalidValue;
     k_pf_gdn_chunk_a<<<dim3(nch, a.VH), 256, kGdnASmem, s>>>(ck);
     k_pf_gdn_state<<<a.VH * (128 / kGS1), 256, kGdnB1Smem, s>>>(ck);
-    k_pf_gdn_out<<<dim3(nch, a.VH, 2), 256, kGdnB2Smem, s>>>(ck);
+    k_pf_gdn_out_tc<<<dim3(nch, a.VH), 128, kGdnOutSmem, s>>>(mST, mQG, mET, mP, ck, a.err);
     return cudaGetLastError();
 }
-size_t pf_gdn_workspace_bytes(int KH, int VH, int T) {
+// scratch pieces of pf_gdn in bytes, in carving order
+static void gdn_pieces(int KH, int VH, int T, size_t (&b)[13]) {
     const size_t t = (size_t)T, nch = (t + kGC - 1) / kGC, KD = (size_t)KH * 128, VD = (size_t)VH * 128;
-    auto r = [](size_t b) { return (b + 255) / 256 * 256; };
-    return 2 * r(t * KD * 4) + 5 * r(t * VD * 4) + 2 * r(t * VH * 4) + r(VH * nch * kGC * kGC * 4) + r(VH * nch * 4) +
-           r(VH * nch * 128 * 128 * 4);
+    const size_t vh = (size_t)VH;
+    const size_t v[13] = {t * KD * 4, t * KD * 4, t * VD * 4,            // qn, kn, vc
+                          t * VD * 4, t * VD * 4,                        // U, W
+                          vh * 2 * nch * kGC * 128 * 2,                  // Gamma Q pairs
+                          t * VD * 4,                                    // Kd
+                          t * vh * 4, t * vh * 4,                        // glog, beta
+                          vh * nch * 2 * kGC * kGC * 2,                  // P pairs
+                          vh * nch * 4,                                  // gamma_C
+                          vh * nch * 2 * 128 * 128 * 2,                  // S^T pairs per chunk
+                          vh * nch * 2 * 128 * kGC * 2};                 // E^T pairs per chunk
+    for (int i = 0; i < 13; ++i) b[i] = (v[i] + 255) / 256 * 256;
+}
+size_t pf_gdn_workspace_bytes(int KH, int VH, int T) {
+    size_t b[13], sum = 0;
+    gdn_pieces(KH, VH, T, b);
+    for (size_t x : b) sum += x;
+    return sum;
 }
 int pf_gdn_carve(PfGdnArgs& a, void* ws, size_t bytes) {
-    const size_t t = (size_t)a.T, nch = (t + kGC - 1) / kGC, KD = (size_t)a.KH * 128, VD = (size_t)a.VH * 128;
     if (!ws || bytes < pf_gdn_workspace_bytes(a.KH, a.VH, a.T)) return -1;
-    uint8_t* b = static_cast<uint8_t*>(ws);
-    size_t off = 0;
-    auto take = [&](size_t n) {
-        float* f = reinterpret_cast<float*>(b + off);
-        off += (n * 4 + 255) / 256 * 256;
-        return f;
-    };
-    a.qn = take(t * KD);
-    a.kn = take(t * KD);
-    a.vc = take(t * VD);
-    a.U = take(t * VD);
-    a.W = take(t * VD);
-    a.QG = take(t * VD);
-    a.KD = take(t * VD);
-    a.glog = take(t * a.VH);
-    a.beta = take(t * a.VH);
-    a.P = take(a.VH * nch * kGC * kGC);
-    a.gC = take(a.VH * nch);
-    a.Sc = take(a.VH * nch * 128 * 128);
+    size_t b[13];
+    gdn_pieces(a.KH, a.VH, a.T, b);
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    void* ptr[13];
+    for (int i = 0; i < 13; ++i) {
+        ptr[i] = base;
+        base += b[i];
+    }
+    a.qn = static_cast<float*>(ptr[0]);
+    a.kn = static_cast<float*>(ptr[1]);
+    a.vc = static_cast<float*>(ptr[2]);
+    a.U = static_cast<float*>(ptr[3]);
+    a.W = static_cast<float*>(ptr[4]);
+    a.QG = static_cast<uint16_t*>(ptr[5]);
+    a.KD = static_cast<float*>(ptr[6]);
+    a.glog = static_cast<float*>(ptr[7]);
+    a.beta = static_cast<float*>(ptr[8]);
+    a.P = static_cast<uint16_t*>(ptr[9]);
+    a.gC = static_cast<float*>(ptr[10]);
+    a.ST = static_cast<uint16_t*>(ptr[11]);
+    a.ET = static_cast<uint16_t*>(ptr[12]);
     return 0;
 }
 

@@ -168,14 +168,15 @@ __global__ void k_pf_conv_ring(const float* proj, long ldp, int T, int p0, int C
 //   o_i = gamma_i S0^T q_i + sum_{j<=i} P[i][j] e_j,  P[i][j] = exp(G_i - G_j) b_j (q_i . k_j)
 //   S_C = gamma_C S0 + sum_i Kd_i e_i^T,  Kd_i = b_i exp(G_C - G_i) k_i
 // Every exponent is a difference G_i - G_j <= 0 (or a G_i <= 0), so nothing overflows.
-// Kernel A (parallel over chunks and heads) builds U, W, Gamma Q, Kd, P and gamma_C;
-// kernel B1 (sequential over chunks, parallel over heads and 16-column slices of S) applies
-// E = U - W S, S = gamma_C S + Kd^T E and keeps the state entering each chunk; kernel B2
-// (parallel over chunks and heads) forms O = (Gamma Q) S_c + P E. fp32 on CUDA cores.
+// Kernel A (parallel over chunks and heads, tcgen05) builds U, W, Gamma Q, Kd, P and
+// gamma_C, with U = T V and W = T Gamma K from the explicit T = (I + L)^-1; kernel B1
+// (sequential over chunks, parallel over heads and 16-column slices of S, CUDA cores)
+// applies E = U - W S, S = gamma_C S + Kd^T E and keeps the state entering each chunk;
+// kernel B2 (parallel over chunks and heads, tcgen05) forms O = (Gamma Q) S_c + P E.
 constexpr int kGC = 64;            // tokens per chunk
+constexpr uint32_t kT128 = 128 * 128;  // bytes of a 128-row x 64-column bf16 tile
+constexpr uint32_t kT64 = 64 * 128;    // bytes of a 64-row x 64-column bf16 tile
 constexpr int kGP = 128 + 4;       // padded row stride of 128-wide shared tiles
-constexpr int kGLP = kGC + 1;      // padded row stride of 64 x 64 shared tiles
-constexpr size_t kGdnASmem = (size_t)(3 * kGC * kGP + 2 * kGC * kGLP + 2 * kGC) * 4;
 
 struct PfGdnChunk {
     const float* qn;     // [T][KD]
@@ -201,42 +202,59 @@ __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) 
     lo = f2bf(x - bf16lo(hi));
 }
 
-__global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
-    extern __shared__ __align__(16) float sa[];
-    float* Ks = sa;                 // [64][132] k, later Gamma K -> W
-    float* Qs = Ks + kGC * kGP;     // [64][132]
-    float* Vs = Qs + kGC * kGP;     // [64][132] v -> U
-    float* Ls = Vs + kGC * kGP;     // [64][65]
-    float* Ps = Ls + kGC * kGLP;    // [64][65]
-    float* Gc = Ps + kGC * kGLP;    // [64]
-    float* Bs = Gc + kGC;           // [64]
-    const int c = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x;
+// Kernel A on the tensor cores, CTA = (chunk, value head), 128 threads (thread = TMEM lane):
+//   1. [K; Q] (128 x 128) times K^T -> [K K^T; Q K^T] (128 x 64) in TMEM: 24 MMAs M128 N64
+//      K16 over bf16 pairs (hi hi + hi lo + lo hi);
+//   2. rows 0-63 -> L (strictly lower, decay- and beta-weighted) into shared memory, rows
+//      64-127 -> P as bf16 pairs to global (threads 64-127), while threads 0-63 each solve
+//      one column of T = (I + L)^-1 by right-looking substitution in registers;
+//   3. U^T = V^T T^T and W^T = (Gamma K)^T T^T (128 x 64 each): 2 x 12 MMAs; rows written
+//      out as U and W. Kd, Gamma Q and gamma_C are formed on the way in.
+// Shared operand tiles are K-major with 128-byte rows (64 bf16) and 128-byte swizzle.
+constexpr uint32_t kA_KQ = 4 * kT128;               // [K; Q] tiles [hi|lo][dims 0-63 | 64-127]
+constexpr uint32_t kA_T = 2 * kT64;                 // T tiles [hi|lo]
+constexpr uint32_t kA_V = 2 * kT128;                // V^T tiles [hi|lo]
+constexpr uint32_t kA_G = 2 * kT128;                // (Gamma K)^T tiles [hi|lo]
+constexpr int kLtP = kGC + 4;                       // row stride of L^T (floats)
+constexpr size_t kGdnATcSmem = kA_KQ + kA_T + kA_V + kA_G + (size_t)(kGC * kLtP + 2 * kGC) * 4 + 1024 + 64;
+// byte offset of element (row, col) in a 128-byte-swizzled K-major tile
+__device__ __forceinline__ uint32_t sw_off(int row, int col) {
+    return (uint32_t)row * 128u + (uint32_t)((((col >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1));
+}
+__global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p, int* err) {
+    extern __shared__ uint8_t sa_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sa_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* AKQ = sm;
+    uint8_t* TB = AKQ + kA_KQ;
+    uint8_t* AV = TB + kA_T;
+    uint8_t* AG = AV + kA_V;
+    float* Lt = reinterpret_cast<float*>(AG + kA_G);  // L^T: Lt[m][i] = L[i][m]
+    float* Gc = Lt + kGC * kLtP;
+    float* Bs = Gc + kGC;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(Bs + kGC);
+    uint64_t* mma1 = bar;
+    uint64_t* mma2 = bar + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+    const int c = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nch = gridDim.x;
     const int rep = p.VH / p.KH, kh = vh / rep, KD = p.KH * 128;
     const int t0 = c * kGC, n = min(kGC, p.T - t0);
-    for (int e = tid; e < kGC * 32; e += 256) {
-        const int i = e >> 5, c4 = (e & 31) * 4;
-        float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = k4, v4 = k4;
-        if (i < n) {
-            const size_t t = (size_t)(t0 + i);
-            k4 = *reinterpret_cast<const float4*>(p.kn + t * KD + kh * 128 + c4);
-            q4 = *reinterpret_cast<const float4*>(p.qn + t * KD + kh * 128 + c4);
-            v4 = *reinterpret_cast<const float4*>(p.vc + t * p.VD + vh * 128 + c4);
-        }
-        *reinterpret_cast<float4*>(Ks + i * kGP + c4) = k4;
-        *reinterpret_cast<float4*>(Qs + i * kGP + c4) = q4;
-        *reinterpret_cast<float4*>(Vs + i * kGP + c4) = v4;
+    if (tid == 0) {
+        mbar_init(mma1, 1);
+        mbar_init(mma2, 1);
+        fence_mbar_init();
     }
-    if (tid < 32) {
-        // inclusive prefix sum of g over the chunk (two values per lane)
-        const int i0 = 2 * tid;
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
+    if (warp == 1) {
+        // inclusive prefix sum of g over the chunk (two values per lane); beta
+        const int i0 = 2 * lane;
         const float ga = i0 < n ? p.glog[(size_t)(t0 + i0) * p.VH + vh] : 0.f;
         const float gb = i0 + 1 < n ? p.glog[(size_t)(t0 + i0 + 1) * p.VH + vh] : 0.f;
         float sum = ga + gb;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float up = __shfl_up_sync(0xffffffffu, sum, o);
-            if (tid >= o) sum += up;
+            if (lane >= o) sum += up;
         }
         const float excl = sum - (ga + gb);
         Gc[i0] = excl + ga;
@@ -244,94 +262,196 @@ __global__ void __launch_bounds__(256) k_pf_gdn_chunk_a(const PfGdnChunk p) {
         Bs[i0] = i0 < n ? p.beta[(size_t)(t0 + i0) * p.VH + vh] : 0.f;
         Bs[i0 + 1] = i0 + 1 < n ? p.beta[(size_t)(t0 + i0 + 1) * p.VH + vh] : 0.f;
     }
+    tc::fence_before();
     __syncthreads();
-    // KK and QK, 4 x 4 register tiles: rows 4*(tid>>4).., columns (tid&15) + 16*b
-    {
-        const int i0 = (tid >> 4) * 4, jq = tid & 15;
-        float kk[4][4], qk[4][4];
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int b = 0; b < 4; ++b) { kk[a][b] = 0.f; qk[a][b] = 0.f; }
-        for (int d = 0; d < 128; d += 4) {
-            float4 ki[4], qi[4], kj[4];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                ki[a] = *reinterpret_cast<const float4*>(Ks + (i0 + a) * kGP + d);
-                qi[a] = *reinterpret_cast<const float4*>(Qs + (i0 + a) * kGP + d);
-            }
-#pragma unroll
-            for (int b = 0; b < 4; ++b) kj[b] = *reinterpret_cast<const float4*>(Ks + (jq + 16 * b) * kGP + d);
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    kk[a][b] += ki[a].x * kj[b].x + ki[a].y * kj[b].y + ki[a].z * kj[b].z + ki[a].w * kj[b].w;
-                    qk[a][b] += qi[a].x * kj[b].x + qi[a].y * kj[b].y + qi[a].z * kj[b].z + qi[a].w * kj[b].w;
-                }
-        }
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int i = i0 + a, j = jq + 16 * b;
-                const float f = (j <= i && i < n) ? expf(Gc[i] - Gc[j]) * Bs[j] : 0.f;
-                Ls[i * kGLP + j] = j < i ? f * kk[a][b] : 0.f;
-                Ps[i * kGLP + j] = f * qk[a][b];
-            }
-    }
-    __syncthreads();
-    // outputs that need the raw k and q: Kd, Gamma Q, P, gamma_C; then Ks <- Gamma K
+    tc::fence_after();
+    const uint32_t tmem = *tmem_slot;
     const float GC = Gc[n - 1];
+    // ---- operands: [K; Q] rows (row-major), Kd and Gamma Q to global
     const size_t hrow = ((size_t)vh * p.T + t0) * 128;
-    for (int e = tid; e < kGC * 32; e += 256) {
+    const size_t qrow = (size_t)nch * kGC;
+    for (int e = tid; e < kGC * 32; e += 128) {
         const int i = e >> 5, c4 = (e & 31) * 4;
-        if (i >= n) continue;
-        const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * kGP + c4);
-        const float4 q4 = *reinterpret_cast<const float4*>(Qs + i * kGP + c4);
-        const float fd = Bs[i] * expf(GC - Gc[i]), fg = expf(Gc[i]);
-        *reinterpret_cast<float4*>(p.KD + hrow + (size_t)i * 128 + c4) =
-            make_float4(fd * k4.x, fd * k4.y, fd * k4.z, fd * k4.w);
-        const float g4[4] = {fg * q4.x, fg * q4.y, fg * q4.z, fg * q4.w};
-        uint16_t hq[4], lq[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) split_bf16(g4[u], hq[u], lq[u]);
-        const size_t qrow = (size_t)nch * kGC;  // padded token rows of a plane
-        uint16_t* qh = p.QG + ((size_t)vh * 2 * qrow + t0 + i) * 128 + c4;
-        *reinterpret_cast<uint2*>(qh) = make_uint2(hq[0] | ((uint32_t)hq[1] << 16), hq[2] | ((uint32_t)hq[3] << 16));
-        *reinterpret_cast<uint2*>(qh + qrow * 128) =
-            make_uint2(lq[0] | ((uint32_t)lq[1] << 16), lq[2] | ((uint32_t)lq[3] << 16));
+        float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = k4;
+        if (i < n) {
+            const size_t t = (size_t)(t0 + i);
+            k4 = *reinterpret_cast<const float4*>(p.kn + t * KD + kh * 128 + c4);
+            q4 = *reinterpret_cast<const float4*>(p.qn + t * KD + kh * 128 + c4);
+        }
+        uint32_t kh2[2], kl2[2], qh2[2], ql2[2];
+        tc::split2(k4.x, k4.y, kh2[0], kl2[0]);
+        tc::split2(k4.z, k4.w, kh2[1], kl2[1]);
+        tc::split2(q4.x, q4.y, qh2[0], ql2[0]);
+        tc::split2(q4.z, q4.w, qh2[1], ql2[1]);
+        const int kc = c4 >> 6, col = c4 & 63;
+        *reinterpret_cast<uint2*>(AKQ + (0 * 2 + kc) * kT128 + sw_off(i, col)) = make_uint2(kh2[0], kh2[1]);
+        *reinterpret_cast<uint2*>(AKQ + (1 * 2 + kc) * kT128 + sw_off(i, col)) = make_uint2(kl2[0], kl2[1]);
+        *reinterpret_cast<uint2*>(AKQ + (0 * 2 + kc) * kT128 + sw_off(64 + i, col)) = make_uint2(qh2[0], qh2[1]);
+        *reinterpret_cast<uint2*>(AKQ + (1 * 2 + kc) * kT128 + sw_off(64 + i, col)) = make_uint2(ql2[0], ql2[1]);
+        if (i < n) {
+            const float fd = Bs[i] * expf(GC - Gc[i]), fg = expf(Gc[i]);
+            *reinterpret_cast<float4*>(p.KD + hrow + (size_t)i * 128 + c4) =
+                make_float4(fd * k4.x, fd * k4.y, fd * k4.z, fd * k4.w);
+            uint32_t gh[2], gl[2];
+            tc::split2(fg * q4.x, fg * q4.y, gh[0], gl[0]);
+            tc::split2(fg * q4.z, fg * q4.w, gh[1], gl[1]);
+            uint16_t* qg = p.QG + ((size_t)vh * 2 * qrow + t0 + i) * 128 + c4;
+            *reinterpret_cast<uint2*>(qg) = make_uint2(gh[0], gh[1]);
+            *reinterpret_cast<uint2*>(qg + qrow * 128) = make_uint2(gl[0], gl[1]);
+        }
     }
-    uint16_t* Pg = p.P + ((size_t)vh * nch + c) * 2 * kGC * kGC;
-    for (int e = tid; e < kGC * kGC; e += 256) {
-        uint16_t hp, lp;
-        split_bf16(Ps[(e >> 6) * kGLP + (e & 63)], hp, lp);
-        Pg[e] = hp;
-        Pg[kGC * kGC + e] = lp;
+    // ---- V^T and (Gamma K)^T: thread = value / key dim, 8 tokens per 16-byte segment
+    for (int g = 0; g < 8; ++g) {
+        float v8[8], k8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = g * 8 + u;
+            const size_t t = (size_t)(t0 + (i < n ? i : 0));
+            v8[u] = i < n ? p.vc[t * p.VD + vh * 128 + tid] : 0.f;
+            k8[u] = i < n ? expf(Gc[i]) * p.kn[t * KD + kh * 128 + tid] : 0.f;
+        }
+        uint32_t vh4[4], vl4[4], kh4[4], kl4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            tc::split2(v8[2 * u], v8[2 * u + 1], vh4[u], vl4[u]);
+            tc::split2(k8[2 * u], k8[2 * u + 1], kh4[u], kl4[u]);
+        }
+        const uint32_t o = sw_off(tid, g * 8);
+        *reinterpret_cast<uint4*>(AV + o) = make_uint4(vh4[0], vh4[1], vh4[2], vh4[3]);
+        *reinterpret_cast<uint4*>(AV + kT128 + o) = make_uint4(vl4[0], vl4[1], vl4[2], vl4[3]);
+        *reinterpret_cast<uint4*>(AG + o) = make_uint4(kh4[0], kh4[1], kh4[2], kh4[3]);
+        *reinterpret_cast<uint4*>(AG + kT128 + o) = make_uint4(kl4[0], kl4[1], kl4[2], kl4[3]);
     }
     if (tid == 0) p.gC[(size_t)vh * nch + c] = expf(GC);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
+    tc::fence_before();
     __syncthreads();
-    for (int e = tid; e < kGC * 128; e += 256) {
-        const int i = e >> 7, col = e & 127;
-        Ks[i * kGP + col] *= expf(Gc[i]);
+    tc::fence_after();
+    constexpr uint32_t idesc = tc::idesc_bf16(128, 64);
+    const uint32_t akq = smem_u32(AKQ), tb = smem_u32(TB), av = smem_u32(AV), ag = smem_u32(AG);
+    if (tid == 0) {
+        // [K K^T; Q K^T]: B = the first 64 rows (the K rows) of the same tiles
+        for (int kc = 0; kc < 2; ++kc) {
+            const uint64_t ah = tc::desc128(akq + kc * kT128), al = tc::desc128(akq + (2 + kc) * kT128);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+                tc::mma_ss(tmem, ah + adv, ah + adv, idesc, (kc | ks) != 0 ? 1u : 0u);
+                tc::mma_ss(tmem, ah + adv, al + adv, idesc, 1u);
+                tc::mma_ss(tmem, al + adv, ah + adv, idesc, 1u);
+            }
+        }
+        tc::commit(mma1);
     }
-    __syncthreads();
-    // forward substitution: U (columns of V) on threads 0-127, W (columns of Gamma K) on 128-255
-    {
-        float* M = tid < 128 ? Vs : Ks;
-        const int col = tid & 127;
-        for (int i = 1; i < n; ++i) {
-            float acc = M[i * kGP + col];
-            for (int m = 0; m < i; ++m) acc -= Ls[i * kGLP + m] * M[m * kGP + col];
-            M[i * kGP + col] = acc;
-            __syncthreads();
+    bool ok = mbar_wait_bounded(mma1, 0u, err, DEV_TC_EPI_TIMEOUT);
+    ok = __all_sync(0xffffffffu, ok);
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    if (ok) {
+        tc::fence_after();
+        uint32_t r[4][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tc::ld16_nowait(trow + q * 16, r[q]);
+        tc::ld_wait();
+        const int i = tid & 63;
+        const float Gi = Gc[i];
+        if (tid < 64) {
+            // L[i][j] = exp(G_i - G_j) b_j (k_i . k_j) for j < i (rows past the chunk: 0)
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                const float f = (j < i && i < n) ? expf(Gi - Gc[j]) * Bs[j] : 0.f;
+                Lt[j * kLtP + i] = f * __uint_as_float(r[j >> 4][j & 15]);
+            }
+        } else {
+            // P[i][j] = exp(G_i - G_j) b_j (q_i . k_j) for j <= i, as bf16 pairs
+            uint16_t* Pg = p.P + (((size_t)vh * nch + c) * 2 * kGC + i) * kGC;
+#pragma unroll
+            for (int j0 = 0; j0 < 64; j0 += 8) {
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int j = j0 + 2 * u;
+                    const float f0 = (j <= i && i < n) ? expf(Gi - Gc[j]) * Bs[j] : 0.f;
+                    const float f1 = (j + 1 <= i && i < n) ? expf(Gi - Gc[j + 1]) * Bs[j + 1] : 0.f;
+                    tc::split2(f0 * __uint_as_float(r[j >> 4][j & 15]), f1 * __uint_as_float(r[(j + 1) >> 4][(j + 1) & 15]),
+                               hw[u], lw[u]);
+                }
+                *reinterpret_cast<uint4*>(Pg + j0) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(Pg + kGC * kGC + j0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
         }
     }
-    for (int e = tid; e < kGC * 32; e += 256) {
-        const int i = e >> 5, c4 = (e & 31) * 4;
-        if (i >= n) continue;
-        *reinterpret_cast<float4*>(p.U + hrow + (size_t)i * 128 + c4) = *reinterpret_cast<const float4*>(Vs + i * kGP + c4);
-        *reinterpret_cast<float4*>(p.W + hrow + (size_t)i * 128 + c4) = *reinterpret_cast<const float4*>(Ks + i * kGP + c4);
+    if (tid < 64) asm volatile("bar.sync 1, 64;" ::: "memory");  // threads 0-63: L^T complete
+    if (ok && tid < 64) {
+        // column j = tid of T = (I + L)^-1: t = e_j, then for m = 0..62: t_i -= L[i][m] t_m (i > m)
+        const int j = tid;
+        float t[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) t[i] = (i == j) ? 1.f : 0.f;
+#pragma unroll
+        for (int m = 0; m < 63; ++m) {
+            const float tm = t[m];
+            const float* lc = Lt + m * kLtP;
+#pragma unroll
+            for (int i = m + 1; i < 64; ++i) t[i] -= lc[i] * tm;
+        }
+        // T as the B operand of step 3: row i, column (K index) m = j
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            uint16_t hi, lo;
+            split_bf16(t[i], hi, lo);
+            const uint32_t o = sw_off(i, j);
+            *reinterpret_cast<uint16_t*>(TB + o) = hi;
+            *reinterpret_cast<uint16_t*>(TB + kT64 + o) = lo;
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (tid == 0) {
+        if (ok) {
+            const uint64_t bh = tc::desc128(tb), bl = tc::desc128(tb + kT64);
+            const uint64_t vhd = tc::desc128(av), vld = tc::desc128(av + kT128);
+            const uint64_t ghd = tc::desc128(ag), gld = tc::desc128(ag + kT128);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+                tc::mma_ss(tmem + 64, vhd + adv, bh + adv, idesc, ks != 0 ? 1u : 0u);
+                tc::mma_ss(tmem + 64, vhd + adv, bl + adv, idesc, 1u);
+                tc::mma_ss(tmem + 64, vld + adv, bh + adv, idesc, 1u);
+                tc::mma_ss(tmem + 128, ghd + adv, bh + adv, idesc, ks != 0 ? 1u : 0u);
+                tc::mma_ss(tmem + 128, ghd + adv, bl + adv, idesc, 1u);
+                tc::mma_ss(tmem + 128, gld + adv, bh + adv, idesc, 1u);
+            }
+        }
+        tc::commit(mma2);
+    }
+    ok = mbar_wait_bounded(mma2, 0u, err, DEV_TC_EPI_TIMEOUT) && ok;
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+        tc::fence_after();
+        // row tid of U^T / W^T = column tid of U / W
+#pragma unroll 1
+        for (int q = 0; q < 4; ++q) {
+            uint32_t ru[16], rw[16];
+            tc::ld16_nowait(trow + 64 + q * 16, ru);
+            tc::ld16_nowait(trow + 128 + q * 16, rw);
+            tc::ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int i = q * 16 + e;
+                if (i < n) {
+                    p.U[hrow + (size_t)i * 128 + tid] = __uint_as_float(ru[e]);
+                    p.W[hrow + (size_t)i * 128 + tid] = __uint_as_float(rw[e]);
+                }
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::tmem_dealloc(tmem, 256);
     }
 }
 
@@ -468,8 +588,6 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
 // arrive by TMA (no multicast), all K-major with 128-byte swizzle: S_c^T [128][128] and
 // E^T [128][64] as A, Gamma Q [64 tokens][128] and P [64][64] as B. Thread = value dim
 // (its TMEM lane) in the epilogue; a warp's 32 lanes store 32 consecutive outputs.
-constexpr uint32_t kT128 = 128 * 128;  // bytes of a 128-row x 64-column bf16 tile
-constexpr uint32_t kT64 = 64 * 128;    // bytes of a 64-row x 64-column bf16 tile
 constexpr uint32_t kGdnOutBytes = 4 * kT128 + 4 * kT64 + 2 * kT128 + 2 * kT64;
 constexpr size_t kGdnOutSmem = kGdnOutBytes + 1024 + 64;
 __global__ void __launch_bounds__(128, 1)
@@ -896,7 +1014,7 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
     PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.ST, a.ET, a.state, a.out,
                   a.T, a.KH, a.VH, a.VD};
     {
-        cudaError_t e = cudaFuncSetAttribute(k_pf_gdn_chunk_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnASmem);
+        cudaError_t e = cudaFuncSetAttribute(k_pf_gdn_chunk_a_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnATcSmem);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_pf_gdn_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnB1Smem);
         if (e == cudaSuccess)
@@ -909,7 +1027,7 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
     if (tc_make_map_box(&mST, a.ST, pl * 128, 128, 128, 128) || tc_make_map_box(&mQG, a.QG, 2L * a.VH * Tpad, 128, 128, 64) ||
         tc_make_map_box(&mET, a.ET, pl * 128, kGC, kGC, 128) || tc_make_map_box(&mP, a.P, pl * kGC, kGC, kGC, 64))
         return cudaErrorInvalidValue;
-    k_pf_gdn_chunk_a<<<dim3(nch, a.VH), 256, kGdnASmem, s>>>(ck);
+    k_pf_gdn_chunk_a_tc<<<dim3(nch, a.VH), 128, kGdnATcSmem, s>>>(ck, a.err);
     k_pf_gdn_state<<<a.VH * (128 / kGS1), 256, kGdnB1Smem, s>>>(ck);
     k_pf_gdn_out_tc<<<dim3(nch, a.VH), 128, kGdnOutSmem, s>>>(mST, mQG, mET, mP, ck, a.err);
     return cudaGetLastError();

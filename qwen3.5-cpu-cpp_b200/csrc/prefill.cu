@@ -215,8 +215,17 @@ constexpr uint32_t kA_KQ = 4 * kT128;               // [K; Q] tiles [hi|lo][dims
 constexpr uint32_t kA_T = 2 * kT64;                 // T tiles [hi|lo]
 constexpr uint32_t kA_V = 2 * kT128;                // V^T tiles [hi|lo]
 constexpr uint32_t kA_G = 2 * kT128;                // (Gamma K)^T tiles [hi|lo]
-constexpr int kLtP = kGC + 4;                       // row stride of L^T (floats)
-constexpr size_t kGdnATcSmem = kA_KQ + kA_T + kA_V + kA_G + (size_t)(kGC * kLtP + 2 * kGC) * 4 + 1024 + 64;
+constexpr int kLtP = kGC;                           // row stride of L^T (floats)
+// fp32 staging of the chunk's k and v rows [2][64][132], alive only while the operand tiles
+// are built; it shares its space with T and L^T, which are written later
+constexpr uint32_t kA_Stage = 2u * kGC * kGP * 4;
+constexpr uint32_t kA_Late = kA_T + (uint32_t)(kGC * kLtP * 4);
+constexpr uint32_t kA_Shared = kA_Stage > kA_Late ? kA_Stage : kA_Late;
+constexpr size_t kGdnATcSmem = kA_KQ + kA_V + kA_G + kA_Shared + (size_t)(2 * kGC) * 4 + 1024 + 64;
+__device__ __forceinline__ void cp16z(void* dst, const void* src, bool pred) {
+    const int nb = pred ? 16 : 0;  // 0: zero fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(nb) : "memory");
+}
 // byte offset of element (row, col) in a 128-byte-swizzled K-major tile
 __device__ __forceinline__ uint32_t sw_off(int row, int col) {
     return (uint32_t)row * 128u + (uint32_t)((((col >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1));
@@ -225,11 +234,13 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
     extern __shared__ uint8_t sa_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sa_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* AKQ = sm;
-    uint8_t* TB = AKQ + kA_KQ;
-    uint8_t* AV = TB + kA_T;
+    uint8_t* AV = AKQ + kA_KQ;
     uint8_t* AG = AV + kA_V;
-    float* Lt = reinterpret_cast<float*>(AG + kA_G);  // L^T: Lt[m][i] = L[i][m]
-    float* Gc = Lt + kGC * kLtP;
+    uint8_t* TB = AG + kA_G;
+    float* Lt = reinterpret_cast<float*>(TB + kA_T);  // L^T: Lt[m][i] = L[i][m]
+    float* Kst = reinterpret_cast<float*>(TB);        // staging k rows [64][132] (phase 0 only)
+    float* Vst = Kst + kGC * kGP;                     // staging v rows [64][132] (phase 0 only)
+    float* Gc = reinterpret_cast<float*>(TB + kA_Shared);
     float* Bs = Gc + kGC;
     uint64_t* bar = reinterpret_cast<uint64_t*>(Bs + kGC);
     uint64_t* mma1 = bar;
@@ -244,6 +255,14 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
         mbar_init(mma2, 1);
         fence_mbar_init();
     }
+    // k and v rows of the chunk -> shared memory (many copies in flight; rows past the chunk: 0)
+    for (int e = tid; e < kGC * 32; e += 128) {
+        const int i = e >> 5, c4 = (e & 31) * 4;
+        const size_t t = (size_t)(t0 + (i < n ? i : 0));
+        cp16z(Kst + i * kGP + c4, p.kn + t * KD + kh * 128 + c4, i < n);
+        cp16z(Vst + i * kGP + c4, p.vc + t * p.VD + vh * 128 + c4, i < n);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
     if (warp == 1) {
         // inclusive prefix sum of g over the chunk (two values per lane); beta
@@ -262,6 +281,7 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
         Bs[i0] = i0 < n ? p.beta[(size_t)(t0 + i0) * p.VH + vh] : 0.f;
         Bs[i0 + 1] = i0 + 1 < n ? p.beta[(size_t)(t0 + i0 + 1) * p.VH + vh] : 0.f;
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -272,12 +292,9 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
     const size_t qrow = (size_t)nch * kGC;
     for (int e = tid; e < kGC * 32; e += 128) {
         const int i = e >> 5, c4 = (e & 31) * 4;
-        float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = k4;
-        if (i < n) {
-            const size_t t = (size_t)(t0 + i);
-            k4 = *reinterpret_cast<const float4*>(p.kn + t * KD + kh * 128 + c4);
-            q4 = *reinterpret_cast<const float4*>(p.qn + t * KD + kh * 128 + c4);
-        }
+        const float4 k4 = *reinterpret_cast<const float4*>(Kst + i * kGP + c4);
+        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n) q4 = *reinterpret_cast<const float4*>(p.qn + (size_t)(t0 + i) * KD + kh * 128 + c4);
         uint32_t kh2[2], kl2[2], qh2[2], ql2[2];
         tc::split2(k4.x, k4.y, kh2[0], kl2[0]);
         tc::split2(k4.z, k4.w, kh2[1], kl2[1]);
@@ -306,9 +323,8 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int i = g * 8 + u;
-            const size_t t = (size_t)(t0 + (i < n ? i : 0));
-            v8[u] = i < n ? p.vc[t * p.VD + vh * 128 + tid] : 0.f;
-            k8[u] = i < n ? expf(Gc[i]) * p.kn[t * KD + kh * 128 + tid] : 0.f;
+            v8[u] = Vst[i * kGP + tid];
+            k8[u] = expf(Gc[i]) * Kst[i * kGP + tid];
         }
         uint32_t vh4[4], vl4[4], kh4[4], kl4[4];
 #pragma unroll
@@ -514,21 +530,21 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         const float* Ksm = Wsm + kGC * kGP;
         const float* Usm = Ksm + kGC * kGP;
         // the state entering chunk c, transposed (rows = value dims) as bf16 pairs, for the
-        // output kernel: thread -> value dim dv = tid / 16 of the slice, key dims 8 (tid % 16) ..
+        // output kernel: thread -> key dim k = tid % 128 and value dims 8 (tid / 128) .. +7 of the
+        // slice (row reads of S; a warp's stores cover 32 consecutive key dims)
         {
-            const int dv = tid >> 4, k0 = (tid & 15) * 8;
-            uint32_t hw[4], lw[4];
+            const int k = tid & 127, d0 = (tid >> 7) * 8;
+            const float4 a4 = *reinterpret_cast<const float4*>(Ssm + k * kGS1P + d0);
+            const float4 b4 = *reinterpret_cast<const float4*>(Ssm + k * kGS1P + d0 + 4);
+            const float v8[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+            uint16_t* st = p.ST + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + d0) * 128 + k;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                uint16_t h0, l0, h1, l1;
-                split_bf16(Ssm[(k0 + 2 * u) * kGS1P + dv], h0, l0);
-                split_bf16(Ssm[(k0 + 2 * u + 1) * kGS1P + dv], h1, l1);
-                hw[u] = h0 | ((uint32_t)h1 << 16);
-                lw[u] = l0 | ((uint32_t)l1 << 16);
+            for (int u = 0; u < 8; ++u) {
+                uint16_t hi, lo;
+                split_bf16(v8[u], hi, lo);
+                st[u * 128] = hi;
+                st[128 * 128 + u * 128] = lo;
             }
-            uint16_t* st = p.ST + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + dv) * 128 + k0;
-            *reinterpret_cast<uint4*>(st) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(st + 128 * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
         // E = U - W S
         {
@@ -544,16 +560,19 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         }
         __syncthreads();  // E complete; every read of S for E done
         // E^T of the slice as bf16 pairs (rows = value dims, 64 token columns; rows past the
-        // chunk's tokens are zero): thread -> dv = tid / 16, tokens 4 (tid % 16) ..
+        // chunk's tokens are zero): thread -> token j = tid % 64 and value dims 4 (tid / 64) .. +3
         {
-            const int dv = tid >> 4, j0 = (tid & 15) * 4;
-            uint16_t hh[4], ll[4];
+            const int j = tid & 63, d0 = (tid >> 6) * 4;
+            const float4 e4 = *reinterpret_cast<const float4*>(Esm + j * kGS1P + d0);
+            const float v4[4] = {e4.x, e4.y, e4.z, e4.w};
+            uint16_t* et = p.ET + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + d0) * kGC + j;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) split_bf16(Esm[(j0 + u) * kGS1P + dv], hh[u], ll[u]);
-            uint16_t* et = p.ET + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + dv) * kGC + j0;
-            *reinterpret_cast<uint2*>(et) = make_uint2(hh[0] | ((uint32_t)hh[1] << 16), hh[2] | ((uint32_t)hh[3] << 16));
-            *reinterpret_cast<uint2*>(et + 128 * kGC) =
-                make_uint2(ll[0] | ((uint32_t)ll[1] << 16), ll[2] | ((uint32_t)ll[3] << 16));
+            for (int u = 0; u < 4; ++u) {
+                uint16_t hi, lo;
+                split_bf16(v4[u], hi, lo);
+                et[u * kGC] = hi;
+                et[128 * kGC + u * kGC] = lo;
+            }
         }
         // S = gamma_C S + Kd^T E (each thread reads and writes only its own S entries here)
         {

@@ -12,16 +12,18 @@
 // (hi in columns [0, K), lo in [K, 2K)) and are written in that form by the kernels
 // that produce them.
 //
-// Kernel: one CTA per SM, persistent over 128 x 128 output tiles (feature tile outer,
-// token tile inner, so concurrent CTAs share a weight tile through L2).
-//   warp 0 (one lane)  TMA producer: 2-D tiled loads (128-byte swizzle) of the weight
-//                      tile (128 x 64) and the hi / lo activation tiles (128 x 64 each)
-//                      into a 4-stage ring; every CTA loads its own tiles.
-//   warp 1             allocates 256 TMEM columns (two fp32 accumulators of 128 x 128);
-//                      one lane issues tcgen05.mma (M=128, N=128, K=16, kind::f16, bf16
-//                      in, fp32 accumulate) from shared-memory descriptors and commits
-//                      each stage back to the producer and each finished tile to the
-//                      epilogue.
+// Kernel: one CTA per SM, persistent over 256 x 128 output tiles (256 features x 128
+// tokens; feature tile outer, token tile inner, so concurrent CTAs share a weight tile
+// through L2). Two 128-row weight tiles share every hi / lo activation tile, so a 64 KB
+// stage carries 8 MFLOP.
+//   warp 0 (one lane)  TMA producer: 2-D tiled loads (128-byte swizzle) of the two weight
+//                      tiles (128 x 64 each) and the hi / lo activation tiles (128 x 64
+//                      each) into a 3-stage ring; every CTA loads its own tiles.
+//   warp 1             allocates 512 TMEM columns (two tiles in flight, each two fp32
+//                      accumulators of 128 x 128); one lane issues tcgen05.mma (M=128,
+//                      N=128, K=16, kind::f16, bf16 in, fp32 accumulate) from shared-memory
+//                      descriptors and commits each stage back to the producer and each
+//                      finished tile to the epilogue.
 //   warps 2-5          epilogue: tcgen05.ld of their 32 TMEM lanes (= output features),
 //                      store / residual add / SwiGLU + hi-lo split, coalesced across the
 //                      warp (consecutive features of one token).
@@ -36,11 +38,13 @@
 
 namespace qwc {
 
-constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 4, kTThreads = 192;
+constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 3, kTThreads = 192;
+constexpr int kTileRows = 2 * kTM;               // features per output tile
 constexpr uint32_t kTileABytes = kTM * kTK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = kTN * kTK * 2;  // 16 KB
-constexpr uint32_t kStageBytes = kTileABytes + 2 * kTileBBytes;
-constexpr int kTmemCols = 2 * kTN;
+constexpr uint32_t kStageBytes = 2 * kTileABytes + 2 * kTileBBytes;
+constexpr int kAccCols = 2 * kTN;                // columns of one tile's two accumulators
+constexpr int kTmemCols = 2 * kAccCols;
 constexpr size_t kTcSmem = (size_t)kTStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntm = (p.M + kTM - 1) / kTM, ntn = (p.N + kTN - 1) / kTN, ntiles = ntm * ntn;
+    const int ntm = (p.M + kTileRows - 1) / kTileRows, ntn = (p.N + kTN - 1) / kTN, ntiles = ntm * ntn;
     const int nkb = p.K / kTK;
 
     if (threadIdx.x == 0) {
@@ -147,16 +151,18 @@ __global__ void __launch_bounds__(kTThreads, 1)
         // ------------------------------------------------ TMA producer
         long kc = 0;
         for (int tile = blockIdx.x; tile < ntiles && !aborted(); tile += gridDim.x) {
-            const int m0 = (tile / ntn) * kTM, n0 = (tile % ntn) * kTN;
+            const int m0 = (tile / ntn) * kTileRows, n0 = (tile % ntn) * kTN;
             for (int kb = 0; kb < nkb; ++kb, ++kc) {
                 const int s = (int)(kc % kTStages);
                 const uint32_t ph = (uint32_t)((kc / kTStages) & 1);
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, DEV_TC_PRODUCER_TIMEOUT)) { abort_with(DEV_TC_PRODUCER_TIMEOUT); break; }
                 uint8_t* st = smem + (size_t)s * kStageBytes;
                 mbar_arrive_expect_tx(&full[s], kStageBytes);
+                // rows past M (a partial or empty second weight tile) read as zero
                 tma_load_2d(st, &mapW, kb * kTK, m0, &full[s]);
-                tma_load_2d(st + kTileABytes, &mapX, kb * kTK, n0, &full[s]);
-                tma_load_2d(st + kTileABytes + kTileBBytes, &mapX, p.K + kb * kTK, n0, &full[s]);
+                tma_load_2d(st + kTileABytes, &mapW, kb * kTK, m0 + kTM, &full[s]);
+                tma_load_2d(st + 2 * kTileABytes, &mapX, kb * kTK, n0, &full[s]);
+                tma_load_2d(st + 2 * kTileABytes + kTileBBytes, &mapX, p.K + kb * kTK, n0, &full[s]);
             }
         }
         // every stage issued has been consumed (its MMAs completed) before the CTA exits
@@ -174,7 +180,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const uint32_t use = (uint32_t)(it >> 1);
             if (!mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, p.err, DEV_TC_MMA_TIMEOUT)) { abort_with(DEV_TC_MMA_TIMEOUT); break; }
             tc_fence_after();
-            const uint32_t d = tmem + (uint32_t)(buf * kTN);
+            const uint32_t d0 = tmem + (uint32_t)(buf * kAccCols), d1 = d0 + kTN;
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++kc) {
                 const int s = (int)(kc % kTStages);
@@ -182,13 +188,16 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 if (!mbar_wait_bounded(&full[s], ph, p.err, DEV_TC_MMA_TIMEOUT)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t a0 = sbase + (uint32_t)s * kStageBytes;
-                const uint64_t da = sw128_desc(a0), dh = sw128_desc(a0 + kTileABytes),
-                               dl = sw128_desc(a0 + kTileABytes + kTileBBytes);
+                const uint64_t da0 = sw128_desc(a0), da1 = sw128_desc(a0 + kTileABytes),
+                               dh = sw128_desc(a0 + 2 * kTileABytes), dl = sw128_desc(a0 + 2 * kTileABytes + kTileBBytes);
 #pragma unroll
                 for (int ks = 0; ks < kTK / 16; ++ks) {
                     const uint64_t adv = (uint64_t)((ks * 32) >> 4);  // +32 bytes along K
-                    umma_bf16(d, da + adv, dh + adv, (kb | ks) != 0 ? 1u : 0u);
-                    umma_bf16(d, da + adv, dl + adv, 1u);
+                    const uint32_t first = (kb | ks) != 0 ? 1u : 0u;
+                    umma_bf16(d0, da0 + adv, dh + adv, first);
+                    umma_bf16(d0, da0 + adv, dl + adv, 1u);
+                    umma_bf16(d1, da1 + adv, dh + adv, first);
+                    umma_bf16(d1, da1 + adv, dl + adv, 1u);
                 }
                 umma_commit(&empty[s]);  // stage free once these MMAs have read it
             }
@@ -208,10 +217,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
             ok = __all_sync(0xffffffffu, ok && !aborted());
             if (!ok) break;
             tc_fence_after();
-            const int m0 = (tile / ntn) * kTM, n0 = (tile % ntn) * kTN;
-            const int m = m0 + 32 * q + lane;
-            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTN);
-            for (int c = 0; c < kTN; c += 16) {
+            const int n0 = (tile % ntn) * kTN;
+            for (int c = 0; c < 2 * kTN; c += 16) {
+                // columns [0, 128): features m0 + lane row; [128, 256): the second weight tile
+                const int m = (tile / ntn) * kTileRows + (c >= kTN ? kTM : 0) + 32 * q + lane;
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kAccCols);
                 float v[16];
                 tmem_ld16(taddr + (uint32_t)c, v);
                 if (p.epi == TC_SWIGLU_SPLIT) {
@@ -219,7 +229,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const float u = __shfl_xor_sync(0xffffffffu, v[j], 1);
-                        const int n = n0 + c + j;
+                        const int n = n0 + (c & (kTN - 1)) + j;
                         if ((lane & 1) == 0 && m + 1 < p.M && n < p.N) {
                             const float a = silu_f(v[j]) * u;
                             const uint16_t hi = bf16_rne(a);
@@ -230,14 +240,21 @@ __global__ void __launch_bounds__(kTThreads, 1)
                         }
                     }
                 } else if (m < p.M) {
+                    const int nb = n0 + (c & (kTN - 1));
+                    float* dst = p.y + (size_t)nb * p.ldy + m;
+                    if (p.epi == TC_RESIDUAL) {
+                        // all 16 residual loads in flight before the adds (one dependent
+                        // round trip per 16 tokens instead of one per token)
+                        float r[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int n = n0 + c + j;
-                        if (n < p.N) {
-                            float* dst = p.y + (size_t)n * p.ldy + m;
-                            if (p.epi == TC_RESIDUAL) *dst += v[j];
-                            else *dst = v[j];
-                        }
+                        for (int j = 0; j < 16; ++j) r[j] = nb + j < p.N ? dst[(size_t)j * p.ldy] : 0.f;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (nb + j < p.N) dst[(size_t)j * p.ldy] = r[j] + v[j];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (nb + j < p.N) dst[(size_t)j * p.ldy] = v[j];
                     }
                 }
             }
@@ -301,7 +318,7 @@ cudaError_t launch_tc_gemm(const CUtensorMap& mapW, const CUtensorMap& mapX, con
         if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
-    const long ntiles = (long)((p.M + kTM - 1) / kTM) * ((p.N + kTN - 1) / kTN);
+    const long ntiles = (long)((p.M + kTileRows - 1) / kTileRows) * ((p.N + kTN - 1) / kTN);
     const int grid = (int)std::min<long>(ntiles, num_sms());
     k_tc_gemm<<<grid, kTThreads, kTcSmem, s>>>(mapW, mapX, p);
     return cudaGetLastError();

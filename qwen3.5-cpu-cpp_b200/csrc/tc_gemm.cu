@@ -225,18 +225,30 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 float v[16];
                 tmem_ld16(taddr + (uint32_t)c, v);
                 if (p.epi == TC_SWIGLU_SPLIT) {
-                    // rows alternate gate_i (even) / up_i (odd): pair lanes l, l^1
+                    // rows alternate gate_i (even lane) / up_i (odd lane): the pair swaps
+                    // halves so that the even lane forms tokens 0-7 and the odd lane 8-15
+                    const bool odd = (lane & 1) != 0;
+                    float g8[8], u8[8];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float u = __shfl_xor_sync(0xffffffffu, v[j], 1);
-                        const int n = n0 + (c & (kTN - 1)) + j;
-                        if ((lane & 1) == 0 && m + 1 < p.M && n < p.N) {
-                            const float a = silu_f(v[j]) * u;
-                            const uint16_t hi = bf16_rne(a);
-                            const uint16_t lo = bf16_rne(a - __uint_as_float((uint32_t)hi << 16));
-                            uint16_t* row = p.ys + (size_t)n * p.ldys;
-                            row[m >> 1] = hi;
-                            row[p.split_k + (m >> 1)] = lo;
+                    for (int e = 0; e < 8; ++e) {
+                        const float send = odd ? v[e] : v[8 + e];
+                        const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        g8[e] = odd ? recv : v[e];
+                        u8[e] = odd ? v[8 + e] : recv;
+                    }
+                    const int nb = n0 + (c & (kTN - 1)) + (odd ? 8 : 0);
+                    if ((m | 1) < p.M) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            if (nb + e < p.N) {
+                                const float g = g8[e];
+                                const float a = g * __frcp_rn(1.0f + __expf(-g)) * u8[e];
+                                const uint16_t hi = bf16_rne(a);
+                                const uint16_t lo = bf16_rne(a - __uint_as_float((uint32_t)hi << 16));
+                                uint16_t* row = p.ys + (size_t)(nb + e) * p.ldys;
+                                row[m >> 1] = hi;
+                                row[p.split_k + (m >> 1)] = lo;
+                            }
                         }
                     }
                 } else if (m < p.M) {

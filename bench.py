@@ -224,11 +224,11 @@ def prefill_flops(c, T):
 def prefill_launches(c, T, world, chunk=4096):
     """Kernels the library launches for one qwc_prefill: per chunk the embedding, per
     layer two norms and four GEMMs, the mixer (attention: prep, V transpose, tensor-core
-    attention; GDN: prep, conv ring, the two chunked-recurrence kernels, gated norm), with
+    attention; GDN: prep, conv ring, chunk factors, state pass, outputs, gated norm), with
     tensor parallelism one residual add per all-reduce; then final norm + lm_head."""
     L = c.n_layers_total
     n_attn = L // c.attn_interval
-    per_chunk = 1 + n_attn * (6 + 3) + (L - n_attn) * (6 + 5) + (2 * L if world > 1 else 0)
+    per_chunk = 1 + n_attn * (6 + 3) + (L - n_attn) * (6 + 6) + (2 * L if world > 1 else 0)
     return ((T + chunk - 1) // chunk) * per_chunk + 2
 
 

@@ -24,9 +24,10 @@
 //                      N=128, K=16, kind::f16, bf16 in, fp32 accumulate) from shared-memory
 //                      descriptors and commits each stage back to the producer and each
 //                      finished tile to the epilogue.
-//   warps 2-5          epilogue: tcgen05.ld of their 32 TMEM lanes (= output features),
-//                      store / residual add / SwiGLU + hi-lo split, coalesced across the
-//                      warp (consecutive features of one token).
+//   warps 2-9          epilogue: tcgen05.ld of their 32 TMEM lanes (= output features) of
+//                      one of the tile's two accumulators (warps 2-5 the first, 6-9 the
+//                      second), store / residual add / SwiGLU + hi-lo split, coalesced
+//                      across the warp (consecutive features of one token).
 // Every wait is bounded: on a timeout the kernel posts an error code and all roles stop.
 #include "common.cuh"
 #include "kernels.h"
@@ -38,7 +39,7 @@
 
 namespace qwc {
 
-constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 3, kTThreads = 192;
+constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 3, kTEpiWarps = 8, kTThreads = 64 + 32 * kTEpiWarps;
 constexpr int kTileRows = 2 * kTM;               // features per output tile
 constexpr uint32_t kTileABytes = kTM * kTK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = kTN * kTK * 2;  // 16 KB
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&acc_empty[b], kTEpiWarps);
         }
         mbar_init(mma_done, 1);
         *s_abort = 0;
@@ -208,7 +209,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
         mbar_wait_bounded(mma_done, 0u, p.err, DEV_TC_DRAIN_TIMEOUT);
     } else if (warp >= 2) {
         // ------------------------------------------------ epilogue
-        const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
+        const int q = warp & 3;           // TMEM lanes 32q..32q+31 belong to this warp
+        const int half = (warp - 2) >> 2;  // accumulator (weight tile) of this warp
         int it = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
             const int buf = it & 1;
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const int n0 = (tile % ntn) * kTN;
-            for (int c = 0; c < 2 * kTN; c += 16) {
+            for (int c = half * kTN; c < (half + 1) * kTN; c += 16) {
                 // columns [0, 128): features m0 + lane row; [128, 256): the second weight tile
                 const int m = (tile / ntn) * kTileRows + (c >= kTN ? kTM : 0) + 32 * q + lane;
                 const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kAccCols);

@@ -10,8 +10,8 @@
 // query heads of kv head `kv`. The number of active splits follows the live context
 // length (read from the device position, so one captured graph serves every step).
 // Inside a CTA each warp owns every 8th position and keeps its own online softmax
-// (running max, sum and a 256-wide accumulator per head, 8 dims per lane); K and V rows
-// of two positions are loaded together per iteration. Warps are merged through shared
+// (running max, sum and a 256-wide accumulator per head, 8 dims per lane); the K and V
+// rows of the next positions are in flight while the current ones are consumed. Warps are merged through shared
 // memory, CTAs by the last CTA of each kv head (atomic ticket), which also applies the
 // sigmoid gate.
 //
@@ -102,8 +102,12 @@ __device__ __forceinline__ void warp_norm_rope(float* x, const float* w1, float 
 }
 
 // One (kv head, split) item on 256 threads (one CTA). The split count follows the live
-// context length, so an item whose split is beyond it returns at once (uniformly).
-template <int GRP>
+// context length, so an item whose split is beyond it returns at once (uniformly). Each
+// warp works on groups of DEPTH positions with two register buffers: the next group's
+// K/V rows are loaded while the current group is consumed (DEPTH 1 in the decode step,
+// where contexts are short and registers are shared with the GEMV phases; 2 for the
+// standalone kernel).
+template <int GRP, int DEPTH = 1>
 __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int kv, int sp,
                                                  long long* marks = nullptr) {
     auto mark = [&](int k) {
@@ -146,8 +150,8 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     const size_t cache_head = (size_t)kv * p.max_ctx * kHD;
     const bool owner = decode && pos >= j0 && pos < j1;
 
-    // ---- round trip 2: this warp's first two K/V rows (the new row comes from smem)
-    float kA[8], vA[8], kB[8], vB[8];
+    // ---- round trip 2: this warp's first DEPTH K/V rows (the new row comes from smem)
+    float kr[DEPTH][8], vr[DEPTH][8], kr2[DEPTH][8], vr2[DEPTH][8];
     auto fetch = [&](int j, float* kk, float* vv) {
         if (j < j1 && !(decode && j == pos)) {
             load8(p.k_cache, p.kv_bf16, cache_head + (size_t)j * kHD + lane * 8, kk);
@@ -155,8 +159,8 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
         }
     };
     int j = j0 + warp;
-    fetch(j, kA, vA);
-    fetch(j + kWarpsA, kB, vB);
+#pragma unroll
+    for (int d = 0; d < DEPTH; ++d) fetch(j + d * kWarpsA, kr[d], vr[d]);
 
     // ---- prologue roles: q heads (norm + rope), and in the owner CTA k (norm + rope) / v
     const float* cs_row = decode ? p.rope_cs + (size_t)pos * p.rot : nullptr;
@@ -232,14 +236,21 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
             m[g] = mn;
         }
     };
-    // two positions per iteration: both rows' loads are in flight together
+    // groups of DEPTH positions: the next group's loads are issued before the current
+    // group is consumed (two static register buffers, alternating)
+    constexpr int G = DEPTH * kWarpsA;
     while (j < j1) {
-        consume(j, kA, vA);
-        consume(j + kWarpsA, kB, vB);
-        j += 2 * kWarpsA;
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d) fetch(j + G + d * kWarpsA, kr2[d], vr2[d]);
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d) consume(j + d * kWarpsA, kr[d], vr[d]);
+        j += G;
         if (j >= j1) break;
-        fetch(j, kA, vA);
-        fetch(j + kWarpsA, kB, vB);
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d) fetch(j + G + d * kWarpsA, kr[d], vr[d]);
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d) consume(j + d * kWarpsA, kr2[d], vr2[d]);
+        j += G;
     }
     mark(1);
     // ---- merge the warps: per head, M = max m_w, L = sum l_w e^(m_w-M), o = sum acc_w e^(m_w-M)

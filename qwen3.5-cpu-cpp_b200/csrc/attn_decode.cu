@@ -7,7 +7,7 @@ template <int GRP>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeParams p) {
     pdl_wait();
     pdl_launch_dependents();
-    attn_decode_item<GRP>(p, blockIdx.x, blockIdx.y);
+    attn_decode_item<GRP, 2>(p, blockIdx.x, blockIdx.y);
 }
 
 int attn_nsplit_for(int max_ctx, int nkv) {

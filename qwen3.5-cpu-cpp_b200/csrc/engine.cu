@@ -1793,7 +1793,10 @@ extern "C" int qwc_attention_decode(const float* q, const float* gate, const voi
     p.n_ctx_val = n_ctx;
     p.NQ = NQ;
     p.NKV = NKV;
-    p.nsplit = attn_nsplit_for(n_ctx, NKV);
+    // long caches: the block-per-warp kernel (lane = position for the scores) and a separate
+    // combine; short ones: the per-position kernel shared with the decode step
+    const bool long_ctx = n_ctx >= kAttnLongMin;
+    p.nsplit = long_ctx ? attn_long_nsplit(n_ctx, NKV) : attn_nsplit_for(n_ctx, NKV);
     p.out = out;
     const int grp = NQ / NKV;
     const size_t need_o = (size_t)NKV * p.nsplit * grp * 256;
@@ -1815,7 +1818,7 @@ extern "C" int qwc_attention_decode(const float* q, const float* gate, const voi
     p.part_o = s.part_o;
     p.part_ml = s.part_ml;
     p.counters = s.counters;
-    cudaError_t e = launch_attn_decode(p, (cudaStream_t)stream, false);
+    cudaError_t e = long_ctx ? launch_attn_long(p, (cudaStream_t)stream) : launch_attn_decode(p, (cudaStream_t)stream, false);
     if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_attention_decode: ") + cudaGetErrorString(e));
     return QWC_OK;
 }

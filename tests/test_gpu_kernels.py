@@ -71,9 +71,13 @@ def test_gdn_decode_step_matches_oracle(pkg, oracle, KH, VH):
 
 
 @pytest.mark.parametrize("kv_dtype", [0, 1])
-@pytest.mark.parametrize("n_ctx", [1, 63, 64, 65, 1000, 4099])
-def test_attention_decode_matches_oracle(pkg, oracle, kv_dtype, n_ctx):
-    NQ, NKV, HD = 8, 2, 256
+@pytest.mark.parametrize("n_ctx,NQ,NKV", [(1, 8, 2), (63, 8, 2), (64, 8, 2), (65, 8, 2), (1000, 8, 2),
+                                          (2047, 8, 2), (2048, 8, 2), (4099, 8, 2), (32768, 8, 2),
+                                          (5000, 8, 8), (5000, 8, 4), (5000, 8, 1)])
+def test_attention_decode_matches_oracle(pkg, oracle, kv_dtype, n_ctx, NQ, NKV):
+    """Contexts below 2048 run the per-position kernel shared with the decode step, longer
+    ones the block-per-warp kernel with its separate split combine; GQA groups 1-8."""
+    HD = 256
     max_ctx = n_ctx + 5
     rng = np.random.default_rng(n_ctx)
     q = rng.standard_normal((NQ, HD), dtype=np.float32) * 0.1

@@ -36,8 +36,9 @@ __device__ __forceinline__ void load8nc(const void* base, int kv_bf16, size_t of
     }
 }
 
+// two CTAs per SM (16 warps to hide load latency) where the accumulators allow it
 template <int GRP>
-__global__ void __launch_bounds__(kLThreads, 1) k_attn_long(const AttnDecodeParams p) {
+__global__ void __launch_bounds__(kLThreads, GRP <= 4 ? 2 : 1) k_attn_long(const AttnDecodeParams p) {
     __shared__ __align__(16) float qs[GRP][kLHD];
     __shared__ __align__(16) float wacc[kLWarps][kLHD];
     __shared__ float wm[kLWarps][GRP], wl[kLWarps][GRP];
@@ -193,9 +194,9 @@ __global__ void __launch_bounds__(256) k_attn_long_combine(const AttnDecodeParam
 
 }  // namespace
 
-int attn_long_nsplit(int n_ctx, int nkv) {
+int attn_long_nsplit(int n_ctx, int nkv, int grp) {
     int want = (n_ctx + kLWarps * kLBlock - 1) / (kLWarps * kLBlock);
-    int cap = num_sms() / (nkv > 0 ? nkv : 1);
+    int cap = (grp <= 4 ? 2 : 1) * num_sms() / (nkv > 0 ? nkv : 1);
     if (cap > 1024) cap = 1024;
     return want < 1 ? 1 : (want > cap ? cap : want);
 }

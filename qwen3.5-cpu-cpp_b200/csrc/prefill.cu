@@ -89,62 +89,77 @@ struct PfGdnPrep {
     float* beta;          // [T][VH]
     int p0, KH, VH, C, VD;
 };
-__global__ void __launch_bounds__(kPT) k_pf_gdn_prep(const PfGdnPrep p) {
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KD = p.KH * 128;
-    const int nvec = 2 * p.KH + p.VH;
-    for (int v = warp; v < nvec; v += kPT / 32) {
-        const int kind = v < p.KH ? 0 : (v < 2 * p.KH ? 1 : 2);
-        const int head = kind == 0 ? v : (kind == 1 ? v - p.KH : v - 2 * p.KH);
-        const int c0 = kind == 0 ? head * 128 : (kind == 1 ? KD + head * 128 : 2 * KD + head * 128);
-        float val[4];
-        double ss = 0.0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = c0 + lane + 32 * j;
-            // inputs at positions pos-3 .. pos (pos = p0 + t)
-            float xin[4];
-#pragma unroll
-            for (int d = 0; d < 4; ++d) {
-                const int tt = t - 3 + d;
-                if (tt >= 0) {
-                    xin[d] = p.proj[(size_t)tt * p.ldp + c];
-                } else {
-                    const int pos = p.p0 + tt;
-                    xin[d] = pos >= 0 ? p.ring[(size_t)c * 4 + (pos & 3)] : 0.f;
-                }
-            }
-            const float4 w = reinterpret_cast<const float4*>(p.conv_w)[c];
-            float acc = 0.f;
-            acc += w.x * xin[0];
-            acc += w.y * xin[1];
-            acc += w.z * xin[2];
-            acc += w.w * xin[3];
-            val[j] = silu_f(acc);
-            ss += (double)val[j] * val[j];
+// CTA = (16 tokens, one q / k / v head vector), thread = channel. The thread reads its channel's inputs for the 3 positions before the tile and
+// the tile's 16 tokens once (sliding conv window in registers, every row read once instead
+// of four times); the l2norm sums of squares are reduced per token across the 128 channels
+// (double, like the per-token kernel). Blocks with y = 2 KH + VH form the gates.
+constexpr int kPrepT = 16;
+__global__ void __launch_bounds__(128) k_pf_gdn_prep_tiled(const PfGdnPrep p, int T) {
+    __shared__ double red[4][kPrepT];
+    const int tb = blockIdx.x * kPrepT, v = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int KD = p.KH * 128, nvec = 2 * p.KH + p.VH;
+    if (v == nvec) {
+        for (int i = tid; i < kPrepT * p.VH; i += 128) {
+            const int t = tb + i / p.VH, h = i % p.VH;
+            if (t >= T) continue;
+            const float bv = p.b_in[(size_t)t * p.ldab + h], av = p.a_in[(size_t)t * p.ldab + h];
+            p.glog[(size_t)t * p.VH + h] = p.neg_exp_A[h] * softplus_f(av + p.dt_bias[h]);
+            p.beta[(size_t)t * p.VH + h] = sigmoid_f(bv);
         }
-        if (kind < 2) {
+        return;
+    }
+    const int kind = v < p.KH ? 0 : (v < 2 * p.KH ? 1 : 2);
+    const int head = kind == 0 ? v : (kind == 1 ? v - p.KH : v - 2 * p.KH);
+    const int c = (kind == 0 ? head * 128 : (kind == 1 ? KD + head * 128 : 2 * KD + head * 128)) + tid;
+    float x[kPrepT + 3];  // inputs at tb-3 .. tb+15
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float inv = 1.0f / sqrtf((float)ss + 1e-6f);
-            float* dst = (kind == 0 ? p.qn : p.kn) + (size_t)t * KD + head * 128;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float x = val[j] * inv;
-                if (kind == 0) x = x * (1.0f / sqrtf(128.0f));
-                dst[lane + 32 * j] = x;
-            }
+    for (int d = 0; d < kPrepT + 3; ++d) {
+        const int tt = tb - 3 + d;
+        if (tt >= 0) {
+            x[d] = tt < T ? p.proj[(size_t)tt * p.ldp + c] : 0.f;
         } else {
-            float* dst = p.vc + (size_t)t * p.VD + head * 128;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = val[j];
+            const int pos = p.p0 + tt;
+            x[d] = pos >= 0 ? p.ring[(size_t)c * 4 + (pos & 3)] : 0.f;
         }
     }
-    for (int h = threadIdx.x; h < p.VH; h += kPT) {
-        const float bv = p.b_in[(size_t)t * p.ldab + h], av = p.a_in[(size_t)t * p.ldab + h];
-        const float g = p.neg_exp_A[h] * softplus_f(av + p.dt_bias[h]);
-        p.glog[(size_t)t * p.VH + h] = g;  // log of the decay exp(g)
-        p.beta[(size_t)t * p.VH + h] = sigmoid_f(bv);
+    const float4 w = reinterpret_cast<const float4*>(p.conv_w)[c];
+    float val[kPrepT];
+#pragma unroll
+    for (int i = 0; i < kPrepT; ++i) {
+        float acc = 0.f;
+        acc += w.x * x[i];
+        acc += w.y * x[i + 1];
+        acc += w.z * x[i + 2];
+        acc += w.w * x[i + 3];
+        val[i] = silu_f(acc);
+    }
+    if (kind < 2) {
+#pragma unroll
+        for (int i = 0; i < kPrepT; ++i) {
+            double ss = (double)val[i] * val[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red[warp][i] = ss;
+        }
+        __syncthreads();
+        float* dst = (kind == 0 ? p.qn : p.kn) + head * 128 + tid;
+#pragma unroll
+        for (int i = 0; i < kPrepT; ++i) {
+            const int t = tb + i;
+            if (t >= T) break;
+            const double ss = red[0][i] + red[1][i] + red[2][i] + red[3][i];
+            float xo = val[i] * (1.0f / sqrtf((float)ss + 1e-6f));
+            if (kind == 0) xo = xo * (1.0f / sqrtf(128.0f));
+            dst[(size_t)t * KD] = xo;
+        }
+    } else {
+        float* dst = p.vc + head * 128 + tid;
+#pragma unroll
+        for (int i = 0; i < kPrepT; ++i) {
+            const int t = tb + i;
+            if (t >= T) break;
+            dst[(size_t)t * p.VD] = val[i];
+        }
     }
 }
 
@@ -1027,7 +1042,7 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
     if (a.VH % a.KH) return cudaErrorInvalidValue;
     PfGdnPrep pp{a.proj, a.ldp, a.a_in, a.b_in, a.ldab, a.conv_w, a.ring, a.neg_exp_A, a.dt_bias, a.qn, a.kn, a.vc,
                  a.glog, a.beta, a.p0, a.KH, a.VH, a.C, a.VD};
-    k_pf_gdn_prep<<<a.T, kPT, 0, s>>>(pp);
+    k_pf_gdn_prep_tiled<<<dim3((a.T + kPrepT - 1) / kPrepT, 2 * a.KH + a.VH + 1), 128, 0, s>>>(pp, a.T);
     k_pf_conv_ring<<<(a.C + 255) / 256, 256, 0, s>>>(a.proj, a.ldp, a.T, a.p0, a.C, a.ring);
     if (!a.ST || !a.ET || !a.QG || !a.P) return cudaErrorInvalidValue;
     PfGdnChunk ck{a.qn, a.kn, a.vc, a.glog, a.beta, a.U, a.W, a.QG, a.KD, a.P, a.gC, a.ST, a.ET, a.state, a.out,

@@ -71,7 +71,6 @@ __global__ void __launch_bounds__(kPT) k_pf_rmsnorm_split(const float* x, long l
 // Per token: causal depthwise conv (K=4) over the qkv channels, continuing from the conv
 // ring for positions before the chunk, SiLU; l2norm of q and k per head (q also scaled by
 // 1/sqrt(DK)); the gates g = -exp(A_log) softplus(a + dt_bias) (decay exp(g)), beta = sigmoid(b).
-// One warp per 128-channel head vector (q heads, k heads, v heads), 4 channels per lane.
 struct PfGdnPrep {
     const float* proj;    // [T][ldp]: the C conv inputs (q | k | v) first
     long ldp;

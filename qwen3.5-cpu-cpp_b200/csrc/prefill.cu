@@ -532,7 +532,6 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
     const int ei = tid >> 2, ec = (tid & 3) * 4;
     const int sr = tid >> 1, sc = (tid & 1) * 8;
     for (int c = 0; c < nch; ++c) {
-        const int n = min(kGC, p.T - c * kGC);
         if (c + 1 < nch) {
             fetch(c + 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
@@ -562,14 +561,20 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         }
         // E = U - W S
         {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int r = 0; r < 128; ++r) {
-                const float w = Wsm[ei * kGP + r];
-                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + ec);
-                acc[0] += w * s4.x; acc[1] += w * s4.y; acc[2] += w * s4.z; acc[3] += w * s4.w;
+            // even and odd key dims in separate accumulators (two independent FMA chains),
+            // unrolled so that the shared-memory loads run ahead of the FMAs
+            float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+            for (int r = 0; r < 128; r += 2) {
+                const float2 w2 = *reinterpret_cast<const float2*>(Wsm + ei * kGP + r);
+                const float4 s0 = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + ec);
+                const float4 s1 = *reinterpret_cast<const float4*>(Ssm + (r + 1) * kGS1P + ec);
+                a[0] += w2.x * s0.x; a[1] += w2.x * s0.y; a[2] += w2.x * s0.z; a[3] += w2.x * s0.w;
+                b[0] += w2.y * s1.x; b[1] += w2.y * s1.y; b[2] += w2.y * s1.z; b[3] += w2.y * s1.w;
             }
             const float4 u4 = *reinterpret_cast<const float4*>(Usm + ei * kGS1P + ec);
-            const float4 e4 = make_float4(u4.x - acc[0], u4.y - acc[1], u4.z - acc[2], u4.w - acc[3]);
+            const float4 e4 = make_float4(u4.x - (a[0] + b[0]), u4.y - (a[1] + b[1]), u4.z - (a[2] + b[2]),
+                                          u4.w - (a[3] + b[3]));
             *reinterpret_cast<float4*>(Esm + ei * kGS1P + ec) = e4;
         }
         __syncthreads();  // E complete; every read of S for E done
@@ -596,13 +601,23 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             const float4 s1 = *reinterpret_cast<const float4*>(Ssm + sr * kGS1P + sc + 4);
             acc[0] = gC * s0.x; acc[1] = gC * s0.y; acc[2] = gC * s0.z; acc[3] = gC * s0.w;
             acc[4] = gC * s1.x; acc[5] = gC * s1.y; acc[6] = gC * s1.z; acc[7] = gC * s1.w;
-            for (int i = 0; i < n; ++i) {
-                const float kd = Ksm[i * kGP + sr];
+            // even and odd tokens in separate accumulators; rows past the chunk's tokens are
+            // zero in Kd and E, so the loop runs over all 64
+            float odd[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+            for (int i = 0; i < kGC; i += 2) {
+                const float kd0 = Ksm[i * kGP + sr], kd1 = Ksm[(i + 1) * kGP + sr];
                 const float4 e0 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc);
                 const float4 e1 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc + 4);
-                acc[0] += kd * e0.x; acc[1] += kd * e0.y; acc[2] += kd * e0.z; acc[3] += kd * e0.w;
-                acc[4] += kd * e1.x; acc[5] += kd * e1.y; acc[6] += kd * e1.z; acc[7] += kd * e1.w;
+                const float4 f0 = *reinterpret_cast<const float4*>(Esm + (i + 1) * kGS1P + sc);
+                const float4 f1 = *reinterpret_cast<const float4*>(Esm + (i + 1) * kGS1P + sc + 4);
+                acc[0] += kd0 * e0.x; acc[1] += kd0 * e0.y; acc[2] += kd0 * e0.z; acc[3] += kd0 * e0.w;
+                acc[4] += kd0 * e1.x; acc[5] += kd0 * e1.y; acc[6] += kd0 * e1.z; acc[7] += kd0 * e1.w;
+                odd[0] += kd1 * f0.x; odd[1] += kd1 * f0.y; odd[2] += kd1 * f0.z; odd[3] += kd1 * f0.w;
+                odd[4] += kd1 * f1.x; odd[5] += kd1 * f1.y; odd[6] += kd1 * f1.z; odd[7] += kd1 * f1.w;
             }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] += odd[e];
             *reinterpret_cast<float4*>(Ssm + sr * kGS1P + sc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
             *reinterpret_cast<float4*>(Ssm + sr * kGS1P + sc + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
         }

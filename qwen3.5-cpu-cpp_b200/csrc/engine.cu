@@ -1193,7 +1193,7 @@ static int pf_workspace(qwc_handle* h, int cap) {
                  o_o = carve(c * h->VD * 4), o_qn = carve(c * h->KD * 4), o_kn = carve(c * h->KD * 4),
                  o_vc = carve(c * h->VD * 4), o_dec = carve(c * h->VH * 4), o_beta = carve(c * h->VH * 4),
                  o_qbuf = carve(c * h->NQ * h->HD * 4), o_log = carve((size_t)kPfLogitRows * h->V * 4),
-                 o_u = carve(c * h->VD * 4), o_w = carve(c * h->VD * 4), o_qg = carve((c + 63) / 64 * 64 * h->VD * 4),
+                 o_u = carve(c * h->VD * 4), o_w = carve((c + 63) / 64 * 64 * h->VD * 4), o_qg = carve((c + 63) / 64 * 64 * h->VD * 4),
                  o_kd = carve(c * h->VD * 4), o_p = carve((size_t)h->VH * ((c + 63) / 64) * 2 * 64 * 64 * 2),
                  o_gc = carve((size_t)h->VH * ((c + 63) / 64) * 4), o_part = carve(c * h->H * 4),
                  o_xa = carve(c * h->pf_lda * 2), o_xb = carve(c * h->pf_ldb * 2),

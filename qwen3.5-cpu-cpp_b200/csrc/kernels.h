@@ -195,7 +195,7 @@ struct PfGdnArgs {
     float* glog = nullptr;        // scratch [T][VH] log decay
     float* beta = nullptr;        // scratch [T][VH]
     float* U = nullptr;           // scratch [VH][T][128]  (chunked WY form)
-    float* W = nullptr;           // scratch [VH][T][128]
+    float* W = nullptr;           // scratch [VH][ceil(T/64)][128][64]  W^T per chunk
     uint16_t* QG = nullptr;       // scratch [VH][2][ceil(T/64)*64][128] bf16 pairs
     float* KD = nullptr;          // scratch [VH][T][128]
     uint16_t* P = nullptr;        // scratch [VH][ceil(T/64)][2][64][64] bf16 pairs

@@ -199,7 +199,7 @@ struct PfGdnChunk {
     const float* glog;   // [T][VH] g = log of the decay
     const float* beta;   // [T][VH]
     float* U;            // [VH][T][128]
-    float* W;            // [VH][T][128]
+    float* W;            // [VH][nch][128 key dims][64 tokens]  W^T per chunk
     uint16_t* QG;        // [VH][hi|lo][Tpad][128]  gamma_i q_i as bf16 pairs
     float* KD;           // [VH][T][128]  b_i exp(G_C - G_i) k_i
     uint16_t* P;         // [VH][nch][hi|lo][64][64] bf16 pairs
@@ -461,6 +461,9 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
     if (ok) {
         tc::fence_after();
         // row tid of U^T / W^T = column tid of U / W
+        // W is kept transposed per chunk (row = key dim, 64 tokens; rows past the chunk's
+        // tokens are zero), so this thread's row is 256 contiguous bytes
+        float* wt = p.W + (((size_t)vh * nch + c) * 128 + tid) * kGC;
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
             uint32_t ru[16], rw[16];
@@ -470,11 +473,11 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const int i = q * 16 + e;
-                if (i < n) {
-                    p.U[hrow + (size_t)i * 128 + tid] = __uint_as_float(ru[e]);
-                    p.W[hrow + (size_t)i * 128 + tid] = __uint_as_float(rw[e]);
-                }
+                if (i < n) p.U[hrow + (size_t)i * 128 + tid] = __uint_as_float(ru[e]);
             }
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+                *reinterpret_cast<uint4*>(wt + q * 16 + e) = make_uint4(rw[e], rw[e + 1], rw[e + 2], rw[e + 3]);
         }
     }
     tc::fence_before();
@@ -493,7 +496,8 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
 // the final state.
 constexpr int kGS1 = 16;             // columns of S per CTA
 constexpr int kGS1P = kGS1 + 4;      // padded stride of [.][16] tiles
-constexpr int kB1Buf = 2 * kGC * kGP + kGC * kGS1P;  // floats per chunk buffer: W, Kd, U slice
+constexpr int kWtP = kGC + 4;         // padded stride of the W^T rows
+constexpr int kB1Buf = 128 * kWtP + kGC * kGP + kGC * kGS1P;  // floats per chunk buffer: W^T, Kd, U slice
 constexpr size_t kGdnB1Smem = (size_t)(2 * kB1Buf + 128 * kGS1P + kGC * kGS1P) * 4;
 __device__ __forceinline__ void cp16(float* dst, const float* src, bool pred) {
     const uint32_t d = smem_u32(dst);
@@ -515,22 +519,29 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         float* B = sb + (c & 1) * kB1Buf;
         const int t0 = c * kGC, n = min(kGC, p.T - t0);
         const size_t hrow = ((size_t)vh * p.T + t0) * 128;
+        const float* wt = p.W + ((size_t)vh * nch + c) * 128 * kGC;
+        for (int e = tid; e < 128 * (kGC / 4); e += 256) {  // W^T rows: all 64 tokens (zeros past n)
+            const int r = e >> 4, c4 = (e & 15) * 4;
+            cp16(B + r * kWtP + c4, wt + (size_t)r * kGC + c4, true);
+        }
+        float* Bk = B + 128 * kWtP;
         for (int e = tid; e < kGC * 32; e += 256) {
             const int i = e >> 5, c4 = (e & 31) * 4;
             const size_t off = hrow + (size_t)(i < n ? i : 0) * 128 + c4;
-            cp16(B + i * kGP + c4, p.W + off, i < n);
-            cp16(B + kGC * kGP + i * kGP + c4, p.KD + off, i < n);
+            cp16(Bk + i * kGP + c4, p.KD + off, i < n);
         }
         for (int e = tid; e < kGC * (kGS1 / 4); e += 256) {
             const int i = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
-            cp16(B + 2 * kGC * kGP + i * kGS1P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * kGS1 + c4, i < n);
+            cp16(Bk + kGC * kGP + i * kGS1P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * kGS1 + c4, i < n);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     fetch(0);
-    // E tile: row tid >> 2, columns 4 (tid & 3) .. +3; state tile: row tid >> 1, columns 8 (tid & 1) .. +7
-    const int ei = tid >> 2, ec = (tid & 3) * 4;
-    const int sr = tid >> 1, sc = (tid & 1) * 8;
+    // E: 4 x 4 tile (rows ei.., columns ec..) over every 4th key dim (kq = lane % 4), the four
+    // partial tiles summed across lanes; state update: 4 x 4 tile (key dims sr.., columns
+    // sc..) over every 2nd token (kh = lane % 2), summed across the lane pair
+    const int kq = tid & 3, et = tid >> 2, ei = (et >> 2) * 4, ec = (et & 3) * 4;
+    const int kh = tid & 1, stl = tid >> 1, sr = (stl >> 2) * 4, sc = (stl & 3) * 4;
     for (int c = 0; c < nch; ++c) {
         if (c + 1 < nch) {
             fetch(c + 1);
@@ -539,9 +550,9 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();  // chunk c's operands and the state are visible to every thread
-        const float* Wsm = sb + (c & 1) * kB1Buf;
-        const float* Ksm = Wsm + kGC * kGP;
-        const float* Usm = Ksm + kGC * kGP;
+        const float* Wts = sb + (c & 1) * kB1Buf;  // W^T [128][68]
+        const float* Ksm = Wts + 128 * kWtP;         // Kd [64][132]
+        const float* Usm = Ksm + kGC * kGP;          // U slice [64][20]
         // the state entering chunk c, transposed (rows = value dims) as bf16 pairs, for the
         // output kernel: thread -> key dim k = tid % 128 and value dims 8 (tid / 128) .. +7 of the
         // slice (row reads of S; a warp's stores cover 32 consecutive key dims)
@@ -561,21 +572,37 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         }
         // E = U - W S
         {
-            // even and odd key dims in separate accumulators (two independent FMA chains),
-            // unrolled so that the shared-memory loads run ahead of the FMAs
-            float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-            for (int r = 0; r < 128; r += 2) {
-                const float2 w2 = *reinterpret_cast<const float2*>(Wsm + ei * kGP + r);
-                const float4 s0 = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + ec);
-                const float4 s1 = *reinterpret_cast<const float4*>(Ssm + (r + 1) * kGS1P + ec);
-                a[0] += w2.x * s0.x; a[1] += w2.x * s0.y; a[2] += w2.x * s0.z; a[3] += w2.x * s0.w;
-                b[0] += w2.y * s1.x; b[1] += w2.y * s1.y; b[2] += w2.y * s1.z; b[3] += w2.y * s1.w;
+            float acc[4][4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+#pragma unroll 4
+            for (int it = 0; it < 32; ++it) {
+                const int r = it * 4 + kq;
+                const float4 w4 = *reinterpret_cast<const float4*>(Wts + r * kWtP + ei);
+                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + ec);
+                const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int x = 0; x < 4; ++x)
+#pragma unroll
+                    for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(wv[x], sv[y], acc[x][y]);
             }
-            const float4 u4 = *reinterpret_cast<const float4*>(Usm + ei * kGS1P + ec);
-            const float4 e4 = make_float4(u4.x - (a[0] + b[0]), u4.y - (a[1] + b[1]), u4.z - (a[2] + b[2]),
-                                          u4.w - (a[3] + b[3]));
-            *reinterpret_cast<float4*>(Esm + ei * kGS1P + ec) = e4;
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) {
+                    acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], 1);
+                    acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], 2);
+                }
+            // lane kq of the quad stores row ei + kq of the tile
+            const float4 u4 = *reinterpret_cast<const float4*>(Usm + (ei + kq) * kGS1P + ec);
+            float rowv[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+                rowv[y] = kq == 0 ? acc[0][y] : (kq == 1 ? acc[1][y] : (kq == 2 ? acc[2][y] : acc[3][y]));
+            *reinterpret_cast<float4*>(Esm + (ei + kq) * kGS1P + ec) =
+                make_float4(u4.x - rowv[0], u4.y - rowv[1], u4.z - rowv[2], u4.w - rowv[3]);
         }
         __syncthreads();  // E complete; every read of S for E done
         // E^T of the slice as bf16 pairs (rows = value dims, 64 token columns; rows past the
@@ -593,33 +620,40 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
                 et[128 * kGC + u * kGC] = lo;
             }
         }
-        // S = gamma_C S + Kd^T E (each thread reads and writes only its own S entries here)
+        // S = gamma_C S + Kd^T E (each lane pair reads and writes only its own S tile here)
         {
             const float gC = p.gC[(size_t)vh * nch + c];
-            float acc[8];
-            const float4 s0 = *reinterpret_cast<const float4*>(Ssm + sr * kGS1P + sc);
-            const float4 s1 = *reinterpret_cast<const float4*>(Ssm + sr * kGS1P + sc + 4);
-            acc[0] = gC * s0.x; acc[1] = gC * s0.y; acc[2] = gC * s0.z; acc[3] = gC * s0.w;
-            acc[4] = gC * s1.x; acc[5] = gC * s1.y; acc[6] = gC * s1.z; acc[7] = gC * s1.w;
-            // even and odd tokens in separate accumulators; rows past the chunk's tokens are
-            // zero in Kd and E, so the loop runs over all 64
-            float odd[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-            for (int i = 0; i < kGC; i += 2) {
-                const float kd0 = Ksm[i * kGP + sr], kd1 = Ksm[(i + 1) * kGP + sr];
-                const float4 e0 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc);
-                const float4 e1 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc + 4);
-                const float4 f0 = *reinterpret_cast<const float4*>(Esm + (i + 1) * kGS1P + sc);
-                const float4 f1 = *reinterpret_cast<const float4*>(Esm + (i + 1) * kGS1P + sc + 4);
-                acc[0] += kd0 * e0.x; acc[1] += kd0 * e0.y; acc[2] += kd0 * e0.z; acc[3] += kd0 * e0.w;
-                acc[4] += kd0 * e1.x; acc[5] += kd0 * e1.y; acc[6] += kd0 * e1.z; acc[7] += kd0 * e1.w;
-                odd[0] += kd1 * f0.x; odd[1] += kd1 * f0.y; odd[2] += kd1 * f0.z; odd[3] += kd1 * f0.w;
-                odd[4] += kd1 * f1.x; odd[5] += kd1 * f1.y; odd[6] += kd1 * f1.z; odd[7] += kd1 * f1.w;
+            float acc[4][4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+#pragma unroll 4
+            for (int it = 0; it < kGC / 2; ++it) {  // rows past the chunk's tokens are zero
+                const int i = it * 2 + kh;
+                const float4 k4 = *reinterpret_cast<const float4*>(Ksm + i * kGP + sr);
+                const float4 e4 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc);
+                const float kv4[4] = {k4.x, k4.y, k4.z, k4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+                for (int x = 0; x < 4; ++x)
+#pragma unroll
+                    for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(kv4[x], ev[y], acc[x][y]);
             }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] += odd[e];
-            *reinterpret_cast<float4*>(Ssm + sr * kGS1P + sc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            *reinterpret_cast<float4*>(Ssm + sr * kGS1P + sc + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], 1);
+            // lane kh of the pair updates rows sr + 2 kh and sr + 2 kh + 1 of the tile
+#pragma unroll
+            for (int x2 = 0; x2 < 2; ++x2) {
+                const int x = 2 * kh + x2;
+                float* srow = Ssm + (sr + x) * kGS1P + sc;
+                const float4 s4 = *reinterpret_cast<const float4*>(srow);
+                const float a0 = kh ? acc[2 + x2][0] : acc[x2][0], a1 = kh ? acc[2 + x2][1] : acc[x2][1];
+                const float a2 = kh ? acc[2 + x2][2] : acc[x2][2], a3 = kh ? acc[2 + x2][3] : acc[x2][3];
+                *reinterpret_cast<float4*>(srow) =
+                    make_float4(gC * s4.x + a0, gC * s4.y + a1, gC * s4.z + a2, gC * s4.w + a3);
+            }
         }
         __syncthreads();  // new S visible; chunk c's buffer free for the fetch of chunk c + 2
     }
@@ -1085,7 +1119,7 @@ static void gdn_pieces(int KH, int VH, int T, size_t (&b)[13]) {
     const size_t t = (size_t)T, nch = (t + kGC - 1) / kGC, KD = (size_t)KH * 128, VD = (size_t)VH * 128;
     const size_t vh = (size_t)VH;
     const size_t v[13] = {t * KD * 4, t * KD * 4, t * VD * 4,            // qn, kn, vc
-                          t * VD * 4, t * VD * 4,                        // U, W
+                          t * VD * 4, nch * kGC * VD * 4,                // U, W^T per chunk
                           vh * 2 * nch * kGC * 128 * 2,                  // Gamma Q pairs
                           t * VD * 4,                                    // Kd
                           t * vh * 4, t * vh * 4,                        // glog, beta

@@ -170,6 +170,12 @@ int qwc_generate_greedy(qwc_handle* h, const int* prompt, int n_prompt, int n_ne
  * h is not touched. */
 int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only);
 
+/* The same stateless pass, returning the residual stream instead of logits (no reference
+ * counterpart; a parity hook for the per-layer hidden states that QwenForward::prefill
+ * keeps internally, src/qwen_forward.cpp:154-206): hidden_out [n_layers + 1][T][hidden],
+ * slot 0 the embedding rows, slot l + 1 the stream after layer l (before the final norm). */
+int qwc_forward_hidden(qwc_handle* h, const int* ids, int T, float* hidden_out);
+
 /* Prefill that also seeds the decode state (the reference equivalent is stepping the
  * prompt through QwenModel::step, src/qwen_model.cpp:245): resets h, runs ids[T] and
  * leaves position() == T with KV / GDN / conv state filled. logits_out: the last

@@ -25,7 +25,7 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_solve_max_context",
            "qwc_create", "qwc_create_from_dir", "qwc_destroy", "qwc_last_error", "qwc_get_budget",
            "qwc_get_config", "qwc_reset", "qwc_position", "qwc_step", "qwc_generate_greedy",
-           "qwc_forward_logits", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
+           "qwc_forward_logits", "qwc_forward_hidden", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
            "qwc_gemv_bf16", "qwc_gemm_bf16",
            "qwc_tp_shard_of", "qwc_tp_unique_id", "qwc_create_tp", "qwc_create_from_dir_tp",
@@ -111,6 +111,7 @@ def lib():
     L.qwc_step.argtypes = [vp, C.c_int, fp, ip]
     L.qwc_generate_greedy.argtypes = [vp, ip, C.c_int, C.c_int, ip]
     L.qwc_forward_logits.argtypes = [vp, ip, C.c_int, fp, C.c_int]
+    L.qwc_forward_hidden.argtypes = [vp, ip, C.c_int, fp]
     L.qwc_prefill.argtypes = [vp, ip, C.c_int, fp]
     L.qwc_stream.argtypes = [vp]
     L.qwc_stream.restype = C.c_void_p
@@ -230,6 +231,15 @@ class Model:
         check(lib().qwc_forward_logits(self._h, _iptr(ids), T, lg.ctypes.data,
                                        1 if last_only else 0), self._h)
         return lg
+
+    def forward_hidden(self, ids) -> np.ndarray:
+        """The stateless pass's residual stream: [n_layers + 1, T, hidden] (slot 0 the
+        embedding rows, slot l + 1 after layer l), the oracle's per-layer hidden states."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        T = len(ids)
+        hs = np.empty((self.cfg.n_layers_total + 1, T, self.cfg.hidden_size), np.float32)
+        check(lib().qwc_forward_hidden(self._h, _iptr(ids), T, hs.ctypes.data), self._h)
+        return hs
 
     # ---- measurement hooks (no reference counterpart)
     def stream(self) -> int:

@@ -1268,7 +1268,8 @@ static int pf_residual_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t
 // Forward pass of ids[0..T) at positions p0.. on state sv. Logits: every position's
 // rows into logits_host[T][V] (all), only the last position's into logits_host[V]
 // (!all), or none (logits_host == nullptr).
-static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int p0, float* logits_host, bool all) {
+static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int p0, float* logits_host, bool all,
+                  float* hidden_host = nullptr) {
     if (h->H % 64 || h->I % 64 || h->VD % 64 || (h->NQ * h->HD) % 64)
         return fail(h, QWC_E_SHAPE, "batched prefill needs hidden, intermediate, GDN value and attention widths that are multiples of 64");
     int rc = pf_build_maps(h);
@@ -1298,6 +1299,14 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
         const int Tc = std::min(chunk, T - c0), pc = p0 + c0;
         CU(cudaMemcpyAsync(h->pf_ids, ids + c0, (size_t)Tc * 4, cudaMemcpyHostToDevice, h->stream));
         CU(pf_embed(h->pf_ids, Tc, h->embed, H, h->V, h->pf_hid, h->dev_err, h->stream));
+        // residual stream [L+1][T][H]: after the embedding and after every layer
+        auto save_hidden = [&](int slot) -> int {
+            if (hidden_host)
+                CU(cudaMemcpyAsync(hidden_host + ((size_t)slot * T + c0) * H, h->pf_hid, (size_t)Tc * H * 4,
+                                   cudaMemcpyDeviceToHost, h->stream));
+            return QWC_OK;
+        };
+        if ((rc = save_hidden(0))) return rc;
         for (int l = 0; l < h->L; ++l) {
             const Layer& lw = h->layers[l];
             CU(pf_rmsnorm_split(h->pf_hid, H, Tc, lw.in_ln1, H, h->eps, h->pf_xa, h->pf_lda, h->stream));
@@ -1382,6 +1391,7 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
             gu.split_k = h->I;
             if ((rc = pf_gemm(h, h->pf_map_gu[l], h->pf_xa, h->pf_lda, 2 * h->I, Tc, H, gu))) return rc;
             if ((rc = pf_residual_gemm(h, h->pf_map_down[l], h->pf_xb, h->pf_ldb, Tc, h->I))) return rc;
+            if ((rc = save_hidden(l + 1))) return rc;
         }
         // final norm + lm_head for the rows whose logits are wanted
         if (!logits_host) continue;
@@ -1523,12 +1533,11 @@ extern "C" int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full) {
 
 // QwenForward::prefill semantics: stateless. A temporary state of T positions is
 // allocated for the call; the handle's decode state and position are untouched.
-extern "C" int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only) {
-    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_forward_logits: null handle");
-    if (T <= 0 || !ids || !logits_out) return fail(h, QWC_E_INVALID, "qwc_forward_logits: invalid argument");
+static int forward_stateless(qwc_handle* h, const char* who, const int* ids, int T, float* logits_out, bool all,
+                             float* hidden_out) {
     for (int i = 0; i < T; ++i)
-        if (ids[i] < 0 || ids[i] >= h->V) return fail(h, QWC_E_INVALID, "qwc_forward_logits: token id out of range");
-    if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_forward_logits: T exceeds max_context");
+        if (ids[i] < 0 || ids[i] >= h->V) return fail(h, QWC_E_INVALID, std::string(who) + ": token id out of range");
+    if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, std::string(who) + ": T exceeds max_context");
     CU(cudaSetDevice(h->device));
     StateView tv;
     tv.max_ctx = T;
@@ -1541,12 +1550,24 @@ extern "C" int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* l
     if ((gb && cudaMemsetAsync(tv.gdn_state, 0, gb, h->stream) != cudaSuccess) ||
         (cb && cudaMemsetAsync(tv.conv_ring, 0, cb, h->stream) != cudaSuccess))
         rc = fail(h, QWC_E_CUDA, "forward state clear failed");
-    if (rc == QWC_OK) rc = pf_run(h, tv, ids, T, 0, logits_out, !last_only);
+    if (rc == QWC_OK) rc = pf_run(h, tv, ids, T, 0, logits_out, all, hidden_out);
     cudaStreamSynchronize(h->stream);
     cudaFree(tv.gdn_state);
     cudaFree(tv.conv_ring);
     cudaFree(tv.kv);
     return rc;
+}
+
+extern "C" int qwc_forward_logits(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_forward_logits: null handle");
+    if (T <= 0 || !ids || !logits_out) return fail(h, QWC_E_INVALID, "qwc_forward_logits: invalid argument");
+    return forward_stateless(h, "qwc_forward_logits", ids, T, logits_out, !last_only, nullptr);
+}
+
+extern "C" int qwc_forward_hidden(qwc_handle* h, const int* ids, int T, float* hidden_out) {
+    if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_forward_hidden: null handle");
+    if (T <= 0 || !ids || !hidden_out) return fail(h, QWC_E_INVALID, "qwc_forward_hidden: invalid argument");
+    return forward_stateless(h, "qwc_forward_hidden", ids, T, nullptr, false, hidden_out);
 }
 
 // ------------------------------------------------------------------ measurement API

@@ -125,3 +125,21 @@ def test_tensor_core_attention_matches_simt_and_oracle(pkg, oracle, chunk, attn_
         assert rel_l2(got[i], want[i]) < LOGIT_TOL, i
         assert rel_l2(got[i], simt[i]) < LOGIT_TOL, i
     assert (got.argmax(1) == simt.argmax(1)).mean() > 0.99
+
+
+@pytest.mark.parametrize("chunk", [96, 4096], indirect=True)
+@pytest.mark.parametrize("shape,T", [("tiny", 200), ("small-0.8b-widths", 150)])
+def test_per_layer_hidden_states_match_oracle(pkg, oracle, chunk, shape, T):
+    """The north star's bar on every layer: the residual stream after the embedding and
+    after each layer of the batched pass (tcgen05 GEMMs, GDN, attention), across chunk
+    boundaries, against the oracle's QwenForward::prefill, rel_l2 <= 2e-3 per layer."""
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=41)
+    m = pkg.abi.Model(d, max_context=T + 8)
+    got = m.forward_hidden(ids)
+    m.close()
+    _, want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=True, hidden=True)
+    assert got.shape == want.shape == (s.num_hidden_layers + 1, T, s.hidden_size)
+    errs = [rel_l2(got[l], want[l]) for l in range(got.shape[0])]
+    assert max(errs) < LOGIT_TOL, errs

@@ -497,7 +497,7 @@ def run_attn_op(args):
                     {"workload": "configs[2]: gated attention decode, 8q/2kv, HD 256, bf16 KV 32768, 512 steps",
                      "kv_cache": "bf16", "context": CTX, "l2": "KV 64 MiB per step (inputs larger than L2 in total)"},
                     {"ms_per_step": round(us / 1000, 5),
-                     "roofline": {"bound": "hbm", "kernel": "k_attn_decode (split-K flash decode)",
+                     "roofline": {"bound": "hbm", "kernel": "k_attn_long_st + k_attn_long_combine (split-K flash decode, cp.async-staged K/V)",
                                   "achieved": round(bytes_step / (us * 1e3), 1), "peak": peak, "unit": "GB/s",
                                   "frac": round(bytes_step / (us * 1e3) / peak, 4), "peak_source": src,
                                   "traffic": None, "bytes_per_step": bytes_step},

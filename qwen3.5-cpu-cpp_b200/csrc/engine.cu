@@ -1817,7 +1817,7 @@ extern "C" int qwc_attention_decode(const float* q, const float* gate, const voi
     // long caches: the block-per-warp kernel (lane = position for the scores) and a separate
     // combine; short ones: the per-position kernel shared with the decode step
     const bool long_ctx = n_ctx >= kAttnLongMin;
-    p.nsplit = long_ctx ? attn_long_nsplit(n_ctx, NKV, NQ / NKV) : attn_nsplit_for(n_ctx, NKV);
+    p.nsplit = long_ctx ? attn_long_nsplit(n_ctx, NKV, NQ / NKV, kv_dtype == QWC_DTYPE_BF16) : attn_nsplit_for(n_ctx, NKV);
     p.out = out;
     const int grp = NQ / NKV;
     const size_t need_o = (size_t)NKV * p.nsplit * grp * 256;

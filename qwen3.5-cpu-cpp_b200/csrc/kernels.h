@@ -117,7 +117,7 @@ int attn_nsplit_for(int max_ctx, int nkv);
 // Op mode over long caches (attn_long.cu): splits of whole 256-position rounds, then a
 // separate combine kernel; q_in / gate_in, part_o / part_ml sized for attn_long_nsplit.
 constexpr int kAttnLongMin = 2048;
-int attn_long_nsplit(int n_ctx, int nkv, int grp);
+int attn_long_nsplit(int n_ctx, int nkv, int grp, int kv_bf16);
 cudaError_t launch_attn_long(const AttnDecodeParams& p, cudaStream_t s);
 
 // ------------------------------------------------------------------ persistent step

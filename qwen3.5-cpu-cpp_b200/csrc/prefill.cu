@@ -254,6 +254,7 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
     float* Lt = reinterpret_cast<float*>(TB + kA_T);  // L^T: Lt[m][i] = L[i][m]
     float* Kst = reinterpret_cast<float*>(TB);        // staging k rows [64][132] (phase 0 only)
     float* Vst = Kst + kGC * kGP;                     // staging v rows [64][132] (phase 0 only)
+    float* Qst = reinterpret_cast<float*>(AV);        // staging q rows [64][128] until V^T is built
     float* Gc = reinterpret_cast<float*>(TB + kA_Shared);
     float* Bs = Gc + kGC;
     uint64_t* bar = reinterpret_cast<uint64_t*>(Bs + kGC);
@@ -269,12 +270,13 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
         mbar_init(mma2, 1);
         fence_mbar_init();
     }
-    // k and v rows of the chunk -> shared memory (many copies in flight; rows past the chunk: 0)
+    // q, k and v rows of the chunk -> shared memory (many copies in flight; rows past the chunk: 0)
     for (int e = tid; e < kGC * 32; e += 128) {
         const int i = e >> 5, c4 = (e & 31) * 4;
         const size_t t = (size_t)(t0 + (i < n ? i : 0));
         cp16z(Kst + i * kGP + c4, p.kn + t * KD + kh * 128 + c4, i < n);
         cp16z(Vst + i * kGP + c4, p.vc + t * p.VD + vh * 128 + c4, i < n);
+        cp16z(Qst + i * 128 + c4, p.qn + t * KD + kh * 128 + c4, i < n);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
@@ -307,8 +309,7 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
     for (int e = tid; e < kGC * 32; e += 128) {
         const int i = e >> 5, c4 = (e & 31) * 4;
         const float4 k4 = *reinterpret_cast<const float4*>(Kst + i * kGP + c4);
-        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n) q4 = *reinterpret_cast<const float4*>(p.qn + (size_t)(t0 + i) * KD + kh * 128 + c4);
+        const float4 q4 = *reinterpret_cast<const float4*>(Qst + i * 128 + c4);
         uint32_t kh2[2], kl2[2], qh2[2], ql2[2];
         tc::split2(k4.x, k4.y, kh2[0], kl2[0]);
         tc::split2(k4.z, k4.w, kh2[1], kl2[1]);
@@ -331,6 +332,7 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
             *reinterpret_cast<uint2*>(qg + qrow * 128) = make_uint2(gl[0], gl[1]);
         }
     }
+    __syncthreads();  // every read of the staged q is done before V^T overwrites it
     // ---- V^T and (Gamma K)^T: thread = value / key dim, 8 tokens per 16-byte segment
     for (int g = 0; g < 8; ++g) {
         float v8[8], k8[8];

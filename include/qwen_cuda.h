@@ -306,7 +306,9 @@ int qwc_gdn_prefill(const float* mixed, const float* a, const float* b, const fl
 /* Attention of one query over a KV cache on device memory (the loop of attn_step,
  * src/qwen_model.cpp:134-150): q [NQ][HD] (normed and roped), gate [NQ][HD],
  * K/V cache [NKV][max_ctx][HD] of kv_dtype, positions 0..n_ctx-1; out [NQ][HD] =
- * softmax(q K^T / sqrt(HD)) V * sigmoid(gate). HD = 256 is supported. */
+ * softmax(q K^T / sqrt(HD)) V * sigmoid(gate). HD = 256 is supported. From 2048 cached
+ * positions on, a block-per-warp split kernel (bf16 caches: K/V staged through shared
+ * memory) and a second, combining kernel run on `stream`. */
 int qwc_attention_decode(const float* q, const float* gate, const void* k_cache,
                          const void* v_cache, int kv_dtype, int NQ, int NKV, int max_ctx,
                          int n_ctx, float* out, void* stream);

@@ -19,15 +19,21 @@ reference processes its prompt one token at a time).
   cpu_baseline  the reference engine itself (oracle/_ref: its own sources, built here)
              on this host's cores, one full generation.
 
---impl reference times the reference's CPU generate_greedy on the same workload.
+--impl reference times the reference's CPU path on the same workload: generate_greedy for
+decode, QwenForward::prefill of a bounded prefix of the prompt for prefill.
 Multi-GPU: single-sequence decode does not shard; N ranks run N independent replicas
 (weak scaling), value = total tokens/s over all ranks.
 
---workload prefill measures the batched forward pass instead (configs[3] / [4]: the
-2B-shaped model, --seq-len tokens, default 8192): one step = one qwc_prefill of the whole
-prompt (state seeded for decoding, last logits returned). Under torchrun the N ranks run it
-tensor parallel (heads sharded, NCCL all-reduce inside the library; strong scaling), value =
-prompt tokens / device time (max over ranks). Roofline: tensor, the algorithmic FLOPs of
+--workload prefill measures the batched forward pass instead (configs[4]: the 2B-shaped
+model, --seq-len tokens, default 131072; --seq-len 8192 is configs[3]'s prompt): one step =
+one qwc_prefill of the whole prompt (state seeded for decoding, last logits returned). Under
+torchrun the N ranks run it tensor parallel (heads sharded, NCCL all-reduce inside the
+library; strong scaling), value = prompt tokens / device time (max over ranks).
+
+Defaults: N=1 runs the decode workload (the headline metric) and adds a `prefill_tp1`
+object, the prefill workload timed on one GPU; N>1 (torchrun) runs the prefill workload
+tensor parallel, so the scaling lines all measure the same prefill at tp1 (from the N=1
+line's `prefill_tp1`), tp2, tp4 and tp8. Roofline: tensor, the algorithmic FLOPs of
 the forward pass (2 x projection parameters per token, causal attention
 4 NQ HD (t+1) per token per attention layer, GDN 7 DK DV per head per token per GDN layer,
 the lm_head for the last token) against the measured bf16 peak.
@@ -241,6 +247,86 @@ def measured_tflops():
     return 1590.0, "fallback"
 
 
+PREFILL_MODEL = "qwen3.5-2b-shaped"
+PREFILL_T = 131072
+
+
+def prefill_config(name, T, world, params=None):
+    c = {"workload": f"prefill of {T} random ids, {name} (configs[4] shape and length)"
+         if T == PREFILL_T else f"prefill of {T} random ids, {name} (configs[3]/[4] shape)",
+         "model": name, "global_batch": 1, "seq_len": T, "parallelism": f"tp{world}", "kv_cache": "fp32",
+         "l2": "inputs larger than L2 (weights and activations of every layer streamed)"}
+    if params is not None:
+        c["projection_params"] = params
+    return c
+
+
+def prefill_model(pkg, name, dist=None):
+    shape = pkg.synth.SHAPES[name]
+    base = os.environ.get("QWC_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "qwc_models"))
+    mdir = os.path.join(base, f"{name}-s0")
+    if RANK == 0:
+        pkg.synth.write_model(shape, mdir, seed=0)
+    if dist:
+        dist.barrier()
+    return shape, pkg.synth.write_model(shape, mdir, seed=0)
+
+
+def gpu_index_of(local_rank):
+    """nvidia-smi index of this rank's GPU (CUDA_VISIBLE_DEVICES may remap it)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids_v = [v for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids_v) and ids_v[local_rank].strip().isdigit():
+            return int(ids_v[local_rank])
+    return local_rank
+
+
+def time_prefill(m, ids, steps, warmup, dist=None):
+    """Device time (max over ranks) and wall time of `steps` qwc_prefill calls."""
+    import torch
+    stream = torch.cuda.ExternalStream(m.stream())
+    for _ in range(warmup):
+        m.prefill(ids)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_index_of(LOCAL_RANK)) as clocks:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        w0 = time.perf_counter()
+        for _ in range(steps):
+            lg = m.prefill(ids)
+        e1.record(stream)
+        stream.synchronize()
+        wall = time.perf_counter() - w0
+        if dist:
+            dist.barrier()
+    dev_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, wall = float(t[0]), float(t[1])
+    return dev_ms, wall, lg, clocks.summary()
+
+
+def prefill_fields(cfg, T, steps, dev_ms, wall, world, vocab):
+    """value / roofline / e2e of a timed prefill (tensor roofline of the algorithmic FLOPs)."""
+    flops, params = prefill_flops(cfg, T)
+    tf, tf_src = measured_tflops()
+    achieved = flops * steps / (dev_ms / 1000.0) / 1e12
+    return params, {
+        "value": round(T * steps / (dev_ms / 1000.0), 1), "unit": "tok/s",
+        "ms_per_step": round(dev_ms / steps, 3),
+        "roofline": {"bound": "tensor", "kernel": "whole forward pass (tcgen05 GEMMs + GDN + attention)",
+                     "achieved": round(achieved, 1), "peak": tf, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf, 4), "peak_source": tf_src, "traffic": None,
+                     "flops_per_step": flops},
+        "e2e": {"value": round(T * steps / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * T,
+                "d2h_bytes_per_step": 4 * vocab},
+        "gpu_launches": steps * prefill_launches(cfg, T, world)}
+
+
 def run_prefill(args):
     import numpy as np
     import torch
@@ -254,83 +340,24 @@ def run_prefill(args):
         # forward pass run on the library's own NCCL communicator
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     pkg = __graft_entry__.load_package()
-    name = args.model or "qwen3.5-2b-shaped"
-    shape = pkg.synth.SHAPES[name]
-    base = os.environ.get("QWC_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "qwc_models"))
-    mdir = os.path.join(base, f"{name}-s0")
-    if RANK == 0:
-        pkg.synth.write_model(shape, mdir, seed=0)
-    if dist:
-        dist.barrier()
-    d = pkg.synth.write_model(shape, mdir, seed=0)
+    name = args.model or PREFILL_MODEL
+    shape, d = prefill_model(pkg, name, dist)
     T = args.seq_len
     box = [pkg.abi.tp_unique_id() if RANK == 0 and WORLD > 1 else None]
     if dist:
         dist.broadcast_object_list(box, src=0)
     m = pkg.abi.Model(d, max_context=T + 16, device=LOCAL_RANK, rank=RANK, world=WORLD, unique_id=box[0])
     ids = pkg.synth.random_prompt(shape.vocab_size, T, seed=1234)
-    stream = torch.cuda.ExternalStream(m.stream())
-    for _ in range(args.warmup):
-        m.prefill(ids)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    gpu_index = LOCAL_RANK
-    if vis:
-        ids_v = [v for v in vis.split(",") if v.strip()]
-        if LOCAL_RANK < len(ids_v) and ids_v[LOCAL_RANK].strip().isdigit():
-            gpu_index = int(ids_v[LOCAL_RANK])
-    with ClockSampler(gpu_index) as clocks:
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        w0 = time.perf_counter()
-        for _ in range(args.steps):
-            lg = m.prefill(ids)
-        e1.record(stream)
-        stream.synchronize()
-        wall = time.perf_counter() - w0
-        if dist:
-            dist.barrier()
-    dev_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([dev_ms, wall], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_ms, wall = float(t[0]), float(t[1])
-    cfg = m.cfg
-    flops, params = prefill_flops(cfg, T)
-    tf, tf_src = measured_tflops()
-    achieved = flops * args.steps / (dev_ms / 1000.0) / 1e12
-    value = T * args.steps / (dev_ms / 1000.0)
-    line = {"metric": "prefill tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": WORLD,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
+    dev_ms, wall, lg, clk = time_prefill(m, ids, args.steps, args.warmup, dist)
+    params, f = prefill_fields(m.cfg, T, args.steps, dev_ms, wall, WORLD, shape.vocab_size)
+    line = {"metric": "prefill tok/s", "value": f["value"], "unit": "tok/s", "n_gpus": WORLD,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": f["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": f"prefill of {T} random ids, {name} (configs[3]/[4] shape)", "model": name,
-                       "global_batch": 1, "seq_len": T, "parallelism": f"tp{WORLD}",
-                       "kv_cache": "fp32", "projection_params": params,
-                       "l2": "inputs larger than L2 (weights and activations of every layer streamed)"},
-            "roofline": {"bound": "tensor", "kernel": "whole forward pass (tcgen05 GEMMs + GDN + attention)",
-                         "achieved": round(achieved, 1), "peak": tf, "unit": "TFLOP/s",
-                         "frac": round(achieved / tf, 4), "peak_source": tf_src, "traffic": None,
-                         "flops_per_step": flops},
-            "e2e": {"value": round(T * args.steps / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * T,
-                    "d2h_bytes_per_step": 4 * shape.vocab_size},
-            "gpu_launches": args.steps * prefill_launches(cfg, T, WORLD), "clocks": clocks.summary(),
+            "data": "synthetic", "config": prefill_config(name, T, WORLD, params),
+            "roofline": f["roofline"], "e2e": f["e2e"], "gpu_launches": f["gpu_launches"], "clocks": clk,
             "last_argmax": int(np.argmax(lg))}
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
-        from oracle import bindings
-        n = min(T, 64)
-        if bindings.ref_available():
-            ref, kind = bindings.RefModel(d, n + 2), "reference"
-        else:
-            ref, kind = bindings.OracleModel(d, n + 2), "port"
-        t0 = time.perf_counter()
-        ref.prefill(ids[:n])
-        secs = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": round(n / secs, 3), "unit": "tok/s",
-                                "cores": int(os.environ.get("OMP_NUM_THREADS", HOST_CORES)), "kind": kind,
-                                "sample": f"QwenForward::prefill of the first {n} ids ({secs:.1f} s)"}
+        line["cpu_baseline"] = ref_prefill_sample(d, ids)
     m.close()
     if RANK == 0:
         emit(line)
@@ -338,6 +365,37 @@ def run_prefill(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def ref_prefill_sample(d, ids, n=32):
+    """The reference's QwenForward::prefill (oracle/_ref) on the first n ids of the prompt."""
+    from oracle import bindings
+    n = min(len(ids), n)
+    if bindings.ref_available():
+        ref, kind = bindings.RefModel(d, n + 2), "reference"
+    else:
+        ref, kind = bindings.OracleModel(d, n + 2), "port"
+    t0 = time.perf_counter()
+    ref.prefill(ids[:n])
+    secs = time.perf_counter() - t0
+    return {"value": round(n / secs, 3), "unit": "tok/s", "cores": int(os.environ.get("OMP_NUM_THREADS", HOST_CORES)),
+            "kind": kind, "sample": f"QwenForward::prefill of the first {n} ids ({secs:.1f} s)"}
+
+
+def prefill_point(pkg, steps=3, warmup=1):
+    """The prefill workload of the scaling lines timed on this one GPU (tp1)."""
+    import torch
+    shape, d = prefill_model(pkg, PREFILL_MODEL)
+    m = pkg.abi.Model(d, max_context=PREFILL_T + 16, device=LOCAL_RANK)
+    ids = pkg.synth.random_prompt(shape.vocab_size, PREFILL_T, seed=1234)
+    dev_ms, wall, _, clk = time_prefill(m, ids, steps, warmup)
+    params, f = prefill_fields(m.cfg, PREFILL_T, steps, dev_ms, wall, 1, shape.vocab_size)
+    m.close()
+    torch.cuda.empty_cache()
+    out = {"metric": "prefill tok/s", "steps": steps, "warmup": warmup,
+           "config": prefill_config(PREFILL_MODEL, PREFILL_T, 1, params), "clocks": clk}
+    out.update(f)
+    return out
 
 
 def _op_line(args, metric, value, unit, config, extra):
@@ -417,12 +475,17 @@ def run_gdn_op(args):
     peak, src = measured_peaks()
     dec_bytes = 2 * VH * DK * DV * 4 + C * 4 + 2 * VH * 4 + VH * DV * 4 + 2 * C * 4 * 4
     from oracle import bindings
-    n = 256
+    # the oracle's C restatement over the whole workload (4096-token prefill + 256 steps,
+    # ~3 s on one core): the CPU baseline sample and the parity of every output row
+    n = T + ND
     st, cs, want = np.zeros((VH, DK, DV), np.float32), np.zeros((C, 3), np.float32), np.empty((n, VH, DV), np.float32)
     t0 = time.perf_counter()
     bindings.orc_lib().orc_gdn_core(n, KH, VH, DK, DV, 4, np.ascontiguousarray(mixed[:n]), conv_w,
                                     np.ascontiguousarray(a[:n]), np.ascontiguousarray(b[:n]), A_log, dt, st, cs, want)
     cpu = n / (time.perf_counter() - t0)
+    got = d_out.cpu().numpy().reshape(n, VH, DV).astype(np.float64)
+    rel = float(np.linalg.norm(got - want) / np.linalg.norm(want.astype(np.float64)))
+    rel_pf = float(np.linalg.norm(got[:T] - want[:T]) / np.linalg.norm(want[:T].astype(np.float64)))
     line = _op_line(args, "GDN op prefill tok/s", T / (pf_ms / 1000), "tok/s",
                     {"workload": "configs[1]: GDN mixer op, T=4096 prefill then 256 decode steps", "heads": VH,
                      "dk": DK, "dv": DV, "conv": 4, "l2": "state 1 MiB per head set, inputs 100+ MB"},
@@ -435,8 +498,9 @@ def run_gdn_op(args):
                                   "frac": round(dec_bytes / (us_step * 1e3) / peak, 4), "peak_source": src,
                                   "traffic": None},
                      "e2e": None, "gpu_launches": args.steps * (4 + ND),
+                     "rel_l2_vs_oracle": rel, "rel_l2_vs_oracle_prefill": rel_pf,
                      "cpu_baseline": {"value": round(cpu, 1), "unit": "tok/s", "cores": 1, "kind": "port",
-                                      "sample": f"orc_gdn_core over {n} tokens (the oracle's C restatement)"}})
+                                      "sample": f"orc_gdn_core over all {n} tokens (the oracle's C restatement)"}})
     emit(line)
     return 0
 
@@ -536,11 +600,13 @@ def cpu_baseline(d, prompt, n_new):
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU generate_greedy, rank 0 only."""
+    """--impl reference: the reference's CPU path on this arm's workload, rank 0 only."""
     if RANK != 0:
         return 0
     import __graft_entry__
     pkg = __graft_entry__.load_package()
+    if args.workload == "prefill":
+        return run_reference_prefill(args, pkg)
     from oracle import bindings
     d = ensure_model(pkg)
     prompt = pkg.synth.random_prompt(pkg.synth.SHAPES[SHAPE].vocab_size, N_PROMPT, seed=1234)
@@ -548,9 +614,9 @@ def run_reference(args):
         ref, kind = bindings.RefModel(d, N_PROMPT + N_NEW + 2), "reference"
     else:
         ref, kind = bindings.OracleModel(d, N_PROMPT + N_NEW + 2), "port"
-    # each step: one generation, shortened when many steps are asked for so the whole
-    # run stays within a few minutes
-    n_new = N_NEW if args.steps + args.warmup <= 12 else max(8, N_NEW * 12 // (args.steps + args.warmup))
+    # each step: one whole generation (32 prompt + 128 new tokens, ~4 s on 16 cores); only
+    # a run of more than 30 steps is shortened, and the line's config then says so
+    n_new = N_NEW if args.steps + args.warmup <= 30 else max(8, N_NEW * 30 // (args.steps + args.warmup))
 
     def one():
         t0 = time.perf_counter()
@@ -563,15 +629,56 @@ def run_reference(args):
     toks = args.steps * (N_PROMPT + n_new)
     val = toks / secs
     cores = int(os.environ.get("OMP_NUM_THREADS", HOST_CORES))
+    config = workload_config(args)
+    config["new_tokens"] = n_new
+    config["tokens_per_step"] = N_PROMPT + n_new
+    config["seq_len"] = N_PROMPT + n_new
     line = {"metric": METRIC, "value": round(val, 3), "unit": UNIT, "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000 * secs / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(args),
+            "config": config,
             "cpu_baseline": {"value": round(val, 3), "unit": UNIT, "cores": cores, "kind": kind,
                              "sample": f"{args.steps} x generate_greedy({N_PROMPT} prompt + {n_new} new)"},
             "e2e": {"value": round(val, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    emit(line)
+    return 0
+
+
+def run_reference_prefill(args, pkg):
+    """The reference's QwenForward::prefill on the prefill workload's prompt: each step a
+    32-id prefix (the reference's attention is O(T^2) scalar code and it materialises
+    [T][vocab] fp32 logits, so the full 131072-id prompt does not run on the CPU)."""
+    from oracle import bindings
+    name = args.model or PREFILL_MODEL
+    shape, d = prefill_model(pkg, name)
+    T = args.seq_len
+    n = min(T, 32)
+    ids = pkg.synth.random_prompt(shape.vocab_size, T, seed=1234)
+    if bindings.ref_available():
+        ref, kind = bindings.RefModel(d, n + 2), "reference"
+    else:
+        ref, kind = bindings.OracleModel(d, n + 2), "port"
+
+    def one():
+        t0 = time.perf_counter()
+        ref.prefill(ids[:n])
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        one()
+    secs = sum(one() for _ in range(args.steps))
+    val = args.steps * n / secs
+    cores = int(os.environ.get("OMP_NUM_THREADS", HOST_CORES))
+    line = {"metric": "prefill tok/s", "value": round(val, 3), "unit": "tok/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000 * secs / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": prefill_config(name, T, WORLD),
+            "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": cores, "kind": kind,
+                             "sample": f"{args.steps} x QwenForward::prefill of the first {n} of the {T} ids"},
+            "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
     return 0
 
@@ -711,6 +818,9 @@ def run_ours(args):
         cb["tokens_match"] = bool(np.array_equal(np.asarray(toks[:N_NEW]), ref_tokens))
         line["cpu_baseline"] = cb
     m.close()
+    if WORLD == 1 and not args.no_prefill_point:
+        # the scaling lines' prefill workload on this one GPU (their tp1 point)
+        line["prefill_tp1"] = prefill_point(pkg)
     if RANK == 0:
         emit(line)
     if dist:
@@ -730,10 +840,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("decode", "prefill", "gdn-op", "attn-op"), default="decode")
-    ap.add_argument("--seq-len", type=int, default=8192, help="prefill workload: prompt length")
+    ap.add_argument("--workload", choices=("decode", "prefill", "gdn-op", "attn-op"), default=None,
+                    help="default: decode on one GPU, prefill (tensor parallel) under torchrun")
+    ap.add_argument("--seq-len", type=int, default=PREFILL_T, help="prefill workload: prompt length")
     ap.add_argument("--model", default=None, help="prefill workload: synthetic shape name")
+    ap.add_argument("--no-prefill-point", action="store_true",
+                    help="decode workload: skip the one-GPU prefill point (prefill_tp1)")
     args = ap.parse_args()
+    if args.workload is None:
+        args.workload = "prefill" if WORLD > 1 else "decode"
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)

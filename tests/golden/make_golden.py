@@ -6,8 +6,10 @@ reference's src/*.cpp compiled from the reference tree (oracle/Makefile) behind 
 driver (oracle/ref_harness.cpp). Inputs are the seeded synthetic checkpoints of
 synth.py and seeded prompts, so the fixtures stay small: outputs only.
 
-Run from the repository root:  python tests/golden/make_golden.py [--full]
---full adds the 24-layer 0.8B-shaped model (about a minute).
+Run from the repository root:  python tests/golden/make_golden.py [--full] [--2b] [--only NAME ...]
+--full adds the 24-layer 0.8B-shaped model (about a minute); --2b adds the 24-layer
+2B-shaped model with a 512-id prompt (a few minutes on 8 cores); --only regenerates the
+named cases alone (config, tiny, tiny-rep, tiny-untied, small-0.8b, small-2b, 0.8b, 2b).
 """
 import argparse
 import json
@@ -96,20 +98,32 @@ def config_budget_case():
     print("config/budget cases", list(cases))
 
 
+CASES = {
+    "config": config_budget_case,
+    "tiny": lambda: small_case("tiny", 8, 16, prefill=True),
+    "tiny-rep": lambda: small_case("tiny-rep", 8, 16, prefill=False),
+    "tiny-untied": lambda: small_case("tiny-untied", 8, 24, prefill=False),
+    "small-0.8b": lambda: large_case("small-0.8b-widths", 32, 32, "small_0_8b_widths.npz"),
+    "small-2b": lambda: large_case("small-2b-widths", 32, 32, "small_2b_widths.npz"),
+    "0.8b": lambda: large_case("qwen3.5-0.8b-shaped", 32, 64, "qwen35_0_8b.npz"),
+    # configs[3]'s model: a longer prompt so that the attention layers see a real context
+    "2b": lambda: large_case("qwen3.5-2b-shaped", 512, 64, "qwen35_2b.npz"),
+}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--full", action="store_true")
+    ap.add_argument("--2b", dest="two_b", action="store_true")
+    ap.add_argument("--only", nargs="*", choices=sorted(CASES))
     a = ap.parse_args()
     B.build()
     if not B.ref_available():
         sys.exit("oracle/_ref/libqwen_ref.so is missing: the reference tree is needed to make fixtures")
-    config_budget_case()
-    small_case("tiny", 8, 16, prefill=True)
-    small_case("tiny-rep", 8, 16, prefill=False)
-    small_case("tiny-untied", 8, 24, prefill=False)
-    large_case("small-0.8b-widths", 32, 32, "small_0_8b_widths.npz")
-    if a.full:
-        large_case("qwen3.5-0.8b-shaped", 32, 64, "qwen35_0_8b.npz")
+    names = a.only or (["config", "tiny", "tiny-rep", "tiny-untied", "small-0.8b", "small-2b"] +
+                       (["0.8b"] if a.full else []) + (["2b"] if a.two_b else []))
+    for n in names:
+        CASES[n]()
 
 
 if __name__ == "__main__":

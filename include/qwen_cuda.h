@@ -179,8 +179,9 @@ int qwc_forward_hidden(qwc_handle* h, const int* ids, int T, float* hidden_out);
 /* Prefill that also seeds the decode state (the reference equivalent is stepping the
  * prompt through QwenModel::step, src/qwen_model.cpp:245): resets h, runs ids[T] and
  * leaves position() == T with KV / GDN / conv state filled. logits_out: the last
- * position's [vocab] logits, or NULL. */
-int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out);
+ * position's [vocab] logits when last_only != 0, else every position's [T][vocab]
+ * (the lm_head then runs over all T rows), or NULL. */
+int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only);
 
 /* ---------------------------------------------------------------- measurement */
 /* No reference counterpart: hooks for timing the decode path without host round trips. */

@@ -112,7 +112,7 @@ def lib():
     L.qwc_generate_greedy.argtypes = [vp, ip, C.c_int, C.c_int, ip]
     L.qwc_forward_logits.argtypes = [vp, ip, C.c_int, fp, C.c_int]
     L.qwc_forward_hidden.argtypes = [vp, ip, C.c_int, fp]
-    L.qwc_prefill.argtypes = [vp, ip, C.c_int, fp]
+    L.qwc_prefill.argtypes = [vp, ip, C.c_int, fp, C.c_int]
     L.qwc_stream.argtypes = [vp]
     L.qwc_stream.restype = C.c_void_p
     L.qwc_set_prompt.argtypes = [vp, ip, C.c_int]
@@ -294,12 +294,14 @@ class Model:
         fn.argtypes = [C.c_void_p, C.c_void_p]
         check(fn(self._h, full._h if full is not None else None), self._h)
 
-    def prefill(self, ids, logits: bool = True):
-        """Prefill that seeds the decode state; returns the last position's logits."""
+    def prefill(self, ids, logits: bool = True, last_only: bool = True):
+        """Prefill that seeds the decode state; returns the last position's logits [vocab]
+        (last_only) or every position's [T, vocab]."""
         ids = np.ascontiguousarray(ids, dtype=np.int32)
-        lg = np.empty(self.vocab, np.float32) if logits else None
+        shape = (self.vocab,) if last_only else (len(ids), self.vocab)
+        lg = np.empty(shape, np.float32) if logits else None
         check(lib().qwc_prefill(self._h, _iptr(ids), len(ids),
-                                lg.ctypes.data if logits else None), self._h)
+                                lg.ctypes.data if logits else None, 1 if last_only else 0), self._h)
         return lg
 
 

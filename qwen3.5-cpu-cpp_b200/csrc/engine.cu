@@ -1415,7 +1415,7 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
     return check_device_error(h);
 }
 
-extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out) {
+extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only) {
     if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_prefill: null handle");
     if (T <= 0 || !ids) return fail(h, QWC_E_INVALID, "qwc_prefill: empty prompt");
     if (T > h->max_ctx) return fail(h, QWC_E_CONTEXT, "qwc_prefill: T exceeds max_context");
@@ -1426,7 +1426,7 @@ extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_o
     // the batched pass fills the KV cache, GDN state and conv ring for positions 0..T-1;
     // decoding continues at position T
     CU(cudaMemcpyAsync(h->tokens, ids, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
-    rc = pf_run(h, h->st, ids, T, 0, logits_out, false);
+    rc = pf_run(h, h->st, ids, T, 0, logits_out, last_only == 0);
     if (rc) return rc;
     h->h_pin[4] = T;
     CU(cudaMemcpyAsync(h->pos, &h->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, h->stream));

@@ -16,6 +16,9 @@ struct qwc_handle;
 class QwenModel {
 public:
     QwenModel(SafeTensors& weights, const ModelConfig& cfg, int max_context);
+    // Not in the reference: the GPU to run on and the KV cache type (QWC_DTYPE_F32, the
+    // reference's fp32 cache and the default above, or QWC_DTYPE_BF16).
+    QwenModel(SafeTensors& weights, const ModelConfig& cfg, int max_context, int device, int kv_dtype);
     ~QwenModel();
     QwenModel(const QwenModel&) = delete;
     QwenModel& operator=(const QwenModel&) = delete;

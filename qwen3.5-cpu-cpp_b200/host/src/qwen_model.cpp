@@ -10,13 +10,16 @@
 
 // ---------------------------------------------------------------- QwenModel
 QwenModel::QwenModel(SafeTensors& weights, const ModelConfig& cfg, int max_context)
+    : QwenModel(weights, cfg, max_context, 0, QWC_DTYPE_F32) {}
+
+QwenModel::QwenModel(SafeTensors& weights, const ModelConfig& cfg, int max_context, int device, int kv_dtype)
     : cfg_(cfg), max_context_(max_context) {
     qwc_config c;
     qwh::to_c(cfg_, c);
     std::vector<std::string> names;
     std::vector<qwc_tensor> tensors;
     qwh::tensor_table(weights, names, tensors);
-    int rc = qwc_create(&c, tensors.data(), (int)tensors.size(), max_context, QWC_DTYPE_F32, 0, &h_);
+    int rc = qwc_create(&c, tensors.data(), (int)tensors.size(), max_context, kv_dtype, device, &h_);
     if (rc != QWC_OK) {
         err_ = qwc_last_error(nullptr);
         std::cerr << (rc == QWC_E_MISSING ? "" : "[qwen] ") << err_ << "\n";

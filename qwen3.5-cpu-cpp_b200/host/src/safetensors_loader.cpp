@@ -134,54 +134,69 @@ const SafeTensors::Entry* SafeTensors::find(const std::string& name) const {
     return it == entries_.end() ? nullptr : &it->second;
 }
 
+// ---------------------------------------------------------------- element access
+// Tensor data stays in the file mapping. Every fp32 read goes through one routine that
+// widens a run of elements (fp32 copied, bf16 exact), shared by the cached whole-tensor
+// copy and the single-row read.
+namespace {
+enum class Elem { F32, BF16, Unsupported };
+
+Elem elem_kind(const std::string& dtype) {
+    if (dtype == "F32") return Elem::F32;
+    if (dtype == "BF16") return Elem::BF16;
+    return Elem::Unsupported;
+}
+
+// dst[0, count) <- elements [first, first + count) of the tensor whose data starts at base
+bool widen_run(const uint8_t* base, Elem kind, int64_t first, int64_t count, float* dst) {
+    if (kind == Elem::F32) {
+        std::memcpy(dst, base + first * 4, (size_t)count * 4);
+        return true;
+    }
+    if (kind == Elem::BF16) {
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(base) + first;
+        std::transform(h, h + count, dst, bf16_to_f32);
+        return true;
+    }
+    return false;
+}
+}  // namespace
+
 WeightView SafeTensors::view(const std::string& name) const {
-    WeightView v;
+    WeightView out;
     const Entry* e = find(name);
-    if (!e) return v;
-    v.numel = e->numel();
-    if (e->dtype == "BF16") v.bf16 = reinterpret_cast<const uint16_t*>(data_of(*e));
-    else if (e->dtype == "F32") v.f32 = reinterpret_cast<const float*>(data_of(*e));
-    return v;
+    if (e == nullptr) return out;  // empty view: no such tensor
+    out.numel = e->numel();
+    const uint8_t* data = data_of(*e);
+    switch (elem_kind(e->dtype)) {
+        case Elem::BF16: out.bf16 = reinterpret_cast<const uint16_t*>(data); break;
+        case Elem::F32: out.f32 = reinterpret_cast<const float*>(data); break;
+        case Elem::Unsupported: break;  // element count only
+    }
+    return out;
 }
 
 const float* SafeTensors::get_f32(const std::string& name, int64_t* out_numel) {
-    auto cit = f32_cache_.find(name);
-    if (cit != f32_cache_.end()) {
-        if (out_numel) *out_numel = (int64_t)cit->second.size();
-        return cit->second.data();
+    // One fp32 copy per tensor, made on the first request and kept for the object's lifetime.
+    auto hit = f32_cache_.find(name);
+    if (hit == f32_cache_.end()) {
+        const Entry* e = find(name);
+        if (e == nullptr) return nullptr;
+        std::vector<float> widened((size_t)e->numel());
+        if (!widen_run(data_of(*e), elem_kind(e->dtype), 0, e->numel(), widened.data())) {
+            std::cerr << "[safetensors] '" << name << "': no fp32 reading of dtype " << e->dtype << "\n";
+            return nullptr;
+        }
+        hit = f32_cache_.emplace(name, std::move(widened)).first;
     }
-    const Entry* e = find(name);
-    if (!e) return nullptr;
-    const int64_t n = e->numel();
-    std::vector<float> buf((size_t)n);
-    const uint8_t* src = data_of(*e);
-    if (e->dtype == "F32") {
-        std::memcpy(buf.data(), src, (size_t)n * 4);
-    } else if (e->dtype == "BF16") {
-        const uint16_t* s = reinterpret_cast<const uint16_t*>(src);
-        for (int64_t i = 0; i < n; ++i) buf[(size_t)i] = bf16_to_f32(s[i]);
-    } else {
-        std::cerr << "[safetensors] unsupported dtype " << e->dtype << " for '" << name << "'\n";
-        return nullptr;
-    }
-    auto res = f32_cache_.emplace(name, std::move(buf));
-    if (out_numel) *out_numel = (int64_t)res.first->second.size();
-    return res.first->second.data();
+    if (out_numel) *out_numel = (int64_t)hit->second.size();
+    return hit->second.data();
 }
 
 bool SafeTensors::get_row_f32(const std::string& name, int64_t row, float* dst) const {
+    // Row `row` of a 2-D tensor, widened in place from the mapping (no cache).
     const Entry* e = find(name);
-    if (!e || e->shape.size() != 2) return false;
-    const int64_t rows = e->shape[0], cols = e->shape[1];
-    if (row < 0 || row >= rows) return false;
-    const uint8_t* base = data_of(*e);
-    if (e->dtype == "F32") {
-        std::memcpy(dst, reinterpret_cast<const float*>(base) + row * cols, (size_t)cols * 4);
-    } else if (e->dtype == "BF16") {
-        const uint16_t* s = reinterpret_cast<const uint16_t*>(base) + row * cols;
-        for (int64_t i = 0; i < cols; ++i) dst[i] = bf16_to_f32(s[i]);
-    } else {
-        return false;
-    }
-    return true;
+    if (e == nullptr || e->shape.size() != 2 || row < 0 || row >= e->shape[0]) return false;
+    const int64_t width = e->shape[1];
+    return widen_run(data_of(*e), elem_kind(e->dtype), row * width, width, dst);
 }

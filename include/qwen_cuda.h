@@ -254,6 +254,14 @@ int qwc_create_tp(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensor
 int qwc_create_from_dir_tp(const char* model_dir, int max_context, int kv_dtype, int device, int rank,
                            int world, const void* unique_id, qwc_handle** out);
 
+/* Bound, in milliseconds, on every wait of a tensor-parallel handle for its group (default
+ * 300000, or QWC_TP_TIMEOUT_MS at creation). The communicator is non-blocking; when a wait
+ * runs out -- a rank died or never joined the collective -- the handle aborts it, so that
+ * its kernels stop waiting, and the call returns QWC_E_DEVICE; the handle then refuses
+ * further batched passes (destroy it and build the group again). No reference
+ * counterpart (the reference runs on one CPU). */
+int qwc_tp_set_timeout(qwc_handle* h, int ms);
+
 /* After qwc_prefill on a tensor-parallel group: gathers every rank's shard of the decode
  * state (GDN state and conv ring of its heads, KV of its kv heads for the T prefilled
  * positions) into `full`, a single-GPU handle of the same model on rank 0's device, over

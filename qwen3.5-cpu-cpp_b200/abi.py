@@ -29,7 +29,7 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
            "qwc_gemv_bf16", "qwc_gemm_bf16",
            "qwc_tp_shard_of", "qwc_tp_unique_id", "qwc_create_tp", "qwc_create_from_dir_tp",
-           "qwc_tp_gather_state",
+           "qwc_tp_gather_state", "qwc_tp_set_timeout",
            "qwc_gdn_decode_step", "qwc_gdn_prefill", "qwc_gdn_prefill_workspace",
            "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
@@ -286,6 +286,12 @@ class Model:
         G, P = int(buf[0]), int(buf[1])
         kinds = [KERNEL_KINDS[int(k)] for k in buf[2:2 + P]]
         return kinds, buf[2 + P:].reshape(G, P, 8)
+
+    def tp_set_timeout(self, ms: int):
+        """qwc_tp_set_timeout: bound on every wait of this rank for its group."""
+        fn = lib().qwc_tp_set_timeout
+        fn.argtypes = [C.c_void_p, C.c_int]
+        check(fn(self._h, int(ms)), self._h)
 
     def tp_gather_state(self, full: "Model | None"):
         """qwc_tp_gather_state: collective over the tensor-parallel group; rank 0 passes

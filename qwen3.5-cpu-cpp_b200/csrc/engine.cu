@@ -13,6 +13,8 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
+#include <thread>
 
 #include <cmath>
 #include <cstdio>
@@ -89,6 +91,7 @@ struct qwc_handle {
     float *hidden = nullptr, *proj = nullptr, *mix = nullptr, *ffn_h = nullptr, *logits = nullptr;
     float *am_val = nullptr, *part_o = nullptr, *part_ml = nullptr;
     int *am_idx = nullptr, *tokens = nullptr, *pos = nullptr, *n_prompt = nullptr, *argmax = nullptr;
+    int* tp_vote = nullptr;  // tensor parallelism: the status vote of qwc_tp_gather_state
     int* dev_err = nullptr;
     unsigned *am_counter = nullptr, *attn_counters = nullptr;
 
@@ -129,7 +132,14 @@ struct qwc_handle {
     int tp_rank = 0, tp_world = 1;
     qwc_tp_shard shard{};
     int gKH = 0, gVH = 0, gKD = 0, gVD = 0, gC = 0, gNQ = 0, gNKV = 0, gI = 0;
-    ncclComm_t nccl = nullptr;
+    ncclComm_t nccl = nullptr;       // non-blocking communicator (calls are settled, waits bounded)
+    int tp_timeout_ms = 300000;      // bound on every wait for the group (env QWC_TP_TIMEOUT_MS)
+    bool nccl_aborted = false;       // the communicator was aborted: the handle refuses work
+    // QWC_PF_TIMING=1: per batched pass, the device time of the whole pass and of the
+    // all-reduces (event pairs around each, from a pool reused across passes) on stderr
+    bool pf_timing = false;
+    std::vector<cudaEvent_t> pf_ev;
+    size_t pf_ev_used = 0;
     float* pf_part = nullptr;  // prefill: [chunk][H] partial sums to all-reduce
 
     cudaGraphExec_t graph = nullptr;
@@ -140,6 +150,7 @@ struct qwc_handle {
 };
 
 // ------------------------------------------------------------------ error helpers
+static int nccl_settle(qwc_handle* h, ncclResult_t r, const char* what);  // group failures, below
 static int fail(qwc_handle* h, int code, const std::string& msg) {
     if (h) h->err = msg;
     g_last_error = msg;
@@ -815,9 +826,16 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     cudaFree(h->st.kv);
     cudaFree(h->scratch);
     cudaFree(h->step_phases);
+    for (cudaEvent_t e : h->pf_ev) cudaEventDestroy(e);
     cudaFree(h->pf_ws);
     cudaFree(h->pf_kvs);
-    if (h->nccl) ncclCommDestroy(h->nccl);
+    if (h->nccl) {
+        // a communicator whose group is incomplete would block ncclCommDestroy: abort it
+        ncclResult_t st = ncclSuccess;
+        ncclCommGetAsyncError(h->nccl, &st);
+        if (st == ncclSuccess) ncclCommDestroy(h->nccl);
+        else ncclCommAbort(h->nccl);
+    }
     if (h->h_pin) cudaFreeHost(h->h_pin);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
@@ -891,6 +909,8 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
     }
     const char* ng = std::getenv("QWC_NO_GRAPH");
     h->use_graph = !(ng && ng[0] == '1');
+    const char* pt = std::getenv("QWC_PF_TIMING");
+    h->pf_timing = pt && pt[0] == '1';
     const char* np = std::getenv("QWC_NO_PDL");
     h->use_pdl = !(np && np[0] == '1');
     h->max_ctx = max_context;
@@ -1021,13 +1041,17 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
     rc = qwc_reset(h);
     if (rc) return bail(rc);
     if (world > 1) {
+        if (const char* e = std::getenv("QWC_TP_TIMEOUT_MS")) h->tp_timeout_ms = std::max(1, std::atoi(e));
         ncclUniqueId id;
         std::memcpy(&id, unique_id, sizeof(id));
-        const ncclResult_t r = ncclCommInitRank(&h->nccl, world, id, rank);
-        if (r != ncclSuccess) {
+        ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+        ncfg.blocking = 0;  // every wait for the group is bounded (nccl_settle, stream_wait)
+        const ncclResult_t r = ncclCommInitRankConfig(&h->nccl, world, id, rank, &ncfg);
+        if (r != ncclSuccess && r != ncclInProgress) {
             h->nccl = nullptr;
-            return bail(fail(h, QWC_E_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(r)));
+            return bail(fail(h, QWC_E_CUDA, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r)));
         }
+        if ((rc = nccl_settle(h, r, "ncclCommInitRankConfig"))) return bail(rc);
         *out = h;  // decode state machinery is single-GPU only
         return QWC_OK;
     }
@@ -1232,6 +1256,85 @@ static int pf_workspace(qwc_handle* h, int cap) {
     return QWC_OK;
 }
 
+// ------------------------------------------------------------------ group failures
+// The communicator is non-blocking: an NCCL call may return ncclInProgress, and the
+// group's state is polled with ncclCommGetAsyncError. Every wait for the group is bounded
+// by tp_timeout_ms; when it runs out (a rank died, or never posted its part of a
+// collective) the communicator is aborted -- its kernels stop waiting -- and the call
+// returns QWC_E_DEVICE. An aborted handle refuses further work.
+static double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+static int tp_abort(qwc_handle* h, const std::string& why) {
+    if (h->nccl && !h->nccl_aborted) {
+        ncclCommAbort(h->nccl);
+        h->nccl = nullptr;
+        h->nccl_aborted = true;
+        // the aborted collectives return; let the rest of the stream drain (bounded)
+        const double t0 = now_ms();
+        while (cudaStreamQuery(h->stream) == cudaErrorNotReady && now_ms() - t0 < 10000.0)
+            std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    return fail(h, QWC_E_DEVICE, why);
+}
+// An NCCL call's return code: settles ncclInProgress (bounded), aborts on group errors.
+static int nccl_settle(qwc_handle* h, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return QWC_OK;
+    if (r != ncclInProgress) return tp_abort(h, std::string(what) + ": " + ncclGetErrorString(r));
+    const double t0 = now_ms();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclCommGetAsyncError(h->nccl, &st);
+        if (st == ncclSuccess) return QWC_OK;
+        if (st != ncclInProgress) return tp_abort(h, std::string(what) + ": " + ncclGetErrorString(st));
+        if (now_ms() - t0 > h->tp_timeout_ms) return tp_abort(h, std::string(what) + ": timed out");
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+// Waits for the handle's stream: plain for a single-GPU handle; for a tensor-parallel one
+// polled together with the group's error state, bounded by tp_timeout_ms.
+static int stream_wait(qwc_handle* h, const char* who) {
+    if (h->tp_world == 1) {
+        CU(cudaStreamSynchronize(h->stream));
+        return QWC_OK;
+    }
+    const double t0 = now_ms();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(h->stream);
+        if (q == cudaSuccess) return QWC_OK;
+        if (q != cudaErrorNotReady) return fail(h, QWC_E_CUDA, std::string(who) + ": " + cudaGetErrorString(q));
+        ncclResult_t st = ncclSuccess;
+        if (h->nccl) ncclCommGetAsyncError(h->nccl, &st);
+        if (st != ncclSuccess && st != ncclInProgress)
+            return tp_abort(h, std::string(who) + ": tensor-parallel group error: " + ncclGetErrorString(st));
+        if (now_ms() - t0 > h->tp_timeout_ms)
+            return tp_abort(h, std::string(who) + ": the tensor-parallel group did not complete in time (a rank is gone?)");
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+}
+
+// next event of the timing pool (QWC_PF_TIMING)
+static cudaEvent_t pf_event(qwc_handle* h) {
+    if (h->pf_ev_used == h->pf_ev.size()) {
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        h->pf_ev.push_back(e);
+    }
+    return h->pf_ev[h->pf_ev_used++];
+}
+// events 0 / 1: the pass; then pairs around each all-reduce (+ the residual add)
+static void pf_timing_report(qwc_handle* h, int T) {
+    if (!h->pf_timing || h->pf_ev_used < 2) return;
+    float total = 0.f, ar = 0.f, t = 0.f;
+    cudaEventElapsedTime(&total, h->pf_ev[0], h->pf_ev[h->pf_ev_used - 1]);
+    for (size_t i = 1; i + 2 < h->pf_ev_used; i += 2) {
+        cudaEventElapsedTime(&t, h->pf_ev[i], h->pf_ev[i + 1]);
+        ar += t;
+    }
+    std::fprintf(stderr, "[qwc] prefill T=%d rank %d/%d: %.3f ms device, all-reduce + add %.3f ms (%zu calls)\n", T,
+                 h->tp_rank, h->tp_world, total, ar, (h->pf_ev_used - 2) / 2);
+}
+
 static int pf_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t* xs, long ldxs, int M, int N, int K,
                    TcGemmParams p) {
     CUtensorMap mx;
@@ -1259,9 +1362,12 @@ static int pf_residual_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t
     g.y = h->pf_part;
     int rc = pf_gemm(h, mw, xs, ldxs, h->H, Tc, K, g);
     if (rc) return rc;
-    const ncclResult_t r = ncclAllReduce(h->pf_part, h->pf_part, (size_t)Tc * h->H, ncclFloat32, ncclSum, h->nccl, h->stream);
-    if (r != ncclSuccess) return fail(h, QWC_E_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
+    rc = nccl_settle(h, ncclAllReduce(h->pf_part, h->pf_part, (size_t)Tc * h->H, ncclFloat32, ncclSum, h->nccl, h->stream),
+                     "ncclAllReduce");
+    if (rc) return rc;
     CU(pf_add(h->pf_hid, h->pf_part, (size_t)Tc * h->H, h->stream));
+    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
     return QWC_OK;
 }
 
@@ -1270,6 +1376,8 @@ static int pf_residual_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t
 // (!all), or none (logits_host == nullptr).
 static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int p0, float* logits_host, bool all,
                   float* hidden_host = nullptr) {
+    if (h->tp_world > 1 && !h->nccl)
+        return fail(h, QWC_E_DEVICE, "the tensor-parallel communicator was aborted after a group failure");
     if (h->H % 64 || h->I % 64 || h->VD % 64 || (h->NQ * h->HD) % 64)
         return fail(h, QWC_E_SHAPE, "batched prefill needs hidden, intermediate, GDN value and attention widths that are multiples of 64");
     int rc = pf_build_maps(h);
@@ -1278,6 +1386,8 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
     rc = pf_workspace(h, std::min(T, chunk));
     if (rc) return rc;
     const int H = h->H;
+    h->pf_ev_used = 0;
+    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
     const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
     // tensor-core attention operands for positions [0, p0 + T): K and V^T pairs per layer
     const bool attn_tc = pf_attn_tc() && h->HD == 256 && h->n_attn > 0;
@@ -1411,7 +1521,9 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
             CU(cudaMemcpyAsync(dst, h->pf_logits, (size_t)gn * h->V * 4, cudaMemcpyDeviceToHost, h->stream));
         }
     }
-    CU(cudaStreamSynchronize(h->stream));
+    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
+    if ((rc = stream_wait(h, "prefill"))) return rc;
+    pf_timing_report(h, T);
     return check_device_error(h);
 }
 
@@ -1441,23 +1553,50 @@ extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_o
 // decodes from position T. Collective: every rank of the group calls it, rank 0 with its
 // single-GPU handle, the others with null. All ranks walk the pieces in the same order,
 // so the NCCL sends and receives pair up.
+extern "C" int qwc_tp_set_timeout(qwc_handle* h, int ms) {
+    if (!h || h->tp_world < 2 || ms <= 0) return fail(h, QWC_E_INVALID, "qwc_tp_set_timeout: needs a tensor-parallel handle and ms > 0");
+    h->tp_timeout_ms = ms;
+    return QWC_OK;
+}
+
 extern "C" int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full) {
     if (!tp || tp->tp_world < 2 || !tp->nccl)
         return fail(tp, QWC_E_INVALID, "qwc_tp_gather_state: needs a tensor-parallel handle");
     qwc_handle* h = tp;  // errors are reported on the tensor-parallel handle
     const bool root = tp->tp_rank == 0;
     const int T = tp->pos_host, W = tp->tp_world;
+    // Each rank checks what it can see, then all ranks vote (minimum of the status codes)
+    // before any send or receive is posted, so that either every rank transfers or none
+    // does: a rank that returned early would leave its peers' transfers waiting forever.
+    int bad = QWC_OK;
+    std::string why;
     if (root) {
-        if (!full || full->tp_world != 1 || full->device != tp->device)
-            return fail(tp, QWC_E_INVALID, "qwc_tp_gather_state: rank 0 needs a single-GPU handle on its device");
-        if (full->H != tp->H || full->L != tp->L || full->KH != tp->gKH || full->VH != tp->gVH ||
-            full->NKV != tp->gNKV || full->NQ != tp->gNQ || full->kv_dtype != tp->kv_dtype)
-            return fail(tp, QWC_E_SHAPE, "qwc_tp_gather_state: the handles hold different models");
-        if (T > full->max_ctx) return fail(tp, QWC_E_CONTEXT, "qwc_tp_gather_state: prefix longer than max_context");
+        if (!full || full->tp_world != 1 || full->device != tp->device) {
+            bad = QWC_E_INVALID;
+            why = "qwc_tp_gather_state: rank 0 needs a single-GPU handle on its device";
+        } else if (full->H != tp->H || full->L != tp->L || full->KH != tp->gKH || full->VH != tp->gVH ||
+                   full->NKV != tp->gNKV || full->NQ != tp->gNQ || full->kv_dtype != tp->kv_dtype) {
+            bad = QWC_E_SHAPE;
+            why = "qwc_tp_gather_state: the handles hold different models";
+        } else if (T > full->max_ctx) {
+            bad = QWC_E_CONTEXT;
+            why = "qwc_tp_gather_state: prefix longer than max_context";
+        }
     } else if (full) {
-        return fail(tp, QWC_E_INVALID, "qwc_tp_gather_state: only rank 0 passes a destination handle");
+        bad = QWC_E_INVALID;
+        why = "qwc_tp_gather_state: only rank 0 passes a destination handle";
     }
     CU(cudaSetDevice(tp->device));
+    tp->h_pin[5] = bad;
+    CU(cudaMemcpyAsync(tp->tp_vote, &tp->h_pin[5], sizeof(int), cudaMemcpyHostToDevice, tp->stream));
+    int vrc = nccl_settle(tp, ncclAllReduce(tp->tp_vote, tp->tp_vote, 1, ncclInt32, ncclMin, tp->nccl, tp->stream),
+                          "qwc_tp_gather_state: vote");
+    if (vrc) return vrc;
+    CU(cudaMemcpyAsync(&tp->h_pin[5], tp->tp_vote, sizeof(int), cudaMemcpyDeviceToHost, tp->stream));
+    if ((vrc = stream_wait(tp, "qwc_tp_gather_state"))) return vrc;
+    if (bad != QWC_OK) return fail(tp, bad, why);
+    if (tp->h_pin[5] != QWC_OK)
+        return fail(tp, tp->h_pin[5], "qwc_tp_gather_state: another rank of the group rejected the call");
     std::vector<qwc_tp_shard> sh(W);
     for (int r = 0; r < W; ++r) {
         int rc = qwc_tp_shard_of(&tp->cfg, r, W, &sh[r]);
@@ -1520,8 +1659,8 @@ extern "C" int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full) {
     }
     const ncclResult_t ge = ncclGroupEnd();
     if (rc) return rc;
-    if (ge != ncclSuccess) return fail(tp, QWC_E_CUDA, std::string("qwc_tp_gather_state: ") + ncclGetErrorString(ge));
-    CU(cudaStreamSynchronize(tp->stream));
+    if ((rc = nccl_settle(tp, ge, "qwc_tp_gather_state"))) return rc;
+    if ((rc = stream_wait(tp, "qwc_tp_gather_state"))) return rc;
     if (root) {
         full->h_pin[4] = T;
         CU(cudaMemcpyAsync(full->pos, &full->h_pin[4], sizeof(int), cudaMemcpyHostToDevice, full->stream));

@@ -137,3 +137,92 @@ def test_tp_prefill_then_decode_on_rank0(pkg, oracle, tmp_path, shape, world):
         assert rel_l2(lgs[i], ref) < 2e-3, i
         tok = int(np.argmax(ref))
         assert tok == toks[i]
+
+
+def _gather_reject_main(rank, world, port, d, ids, out_dir):
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    abi = __graft_entry__.load_package().abi
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        box = [abi.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        m = abi.Model(d, max_context=len(ids) + 8, device=rank, rank=rank, world=world, unique_id=box[0])
+        m.prefill(ids)
+        # rank 0 passes no destination handle: every rank must return an error (nobody
+        # left waiting in a transfer), and the group must still work afterwards
+        code = 0
+        try:
+            m.tp_gather_state(None)
+        except abi.QwcError as e:
+            code = e.code
+        last = m.prefill(ids)
+        np.save(os.path.join(out_dir, f"code{rank}.npy"), np.array([code]))
+        if rank == 0:
+            np.save(os.path.join(out_dir, "last.npy"), last)
+        dist.barrier()
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_gather_state_rejected_on_one_rank_fails_on_all(pkg, tmp_path):
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    d = model_dir(pkg, "tiny")
+    ids = pkg.synth.random_prompt(pkg.synth.SHAPES["tiny"].vocab_size, 40, seed=5)
+    mp.start_processes(_gather_reject_main, args=(world, _free_port(), d, ids, str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    codes = [int(np.load(tmp_path / f"code{r}.npy")[0]) for r in range(world)]
+    assert codes[0] == -1 and all(c < 0 for c in codes)
+    one = pkg.abi.Model(d, max_context=48)
+    assert rel_l2(np.load(tmp_path / "last.npy"), one.prefill(ids)) < 1e-4
+    one.close()
+
+
+def _dead_peer_main(rank, world, port, d, ids, out_dir):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"  # plain peer transfers: no multicast object outlives a rank
+    sys.path.insert(0, ROOT)
+    import time
+    import __graft_entry__
+    abi = __graft_entry__.load_package().abi
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    box = [abi.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    m = abi.Model(d, max_context=len(ids) + 8, device=rank, rank=rank, world=world, unique_id=box[0])
+    dist.barrier()  # both handles exist; nothing is in flight
+    if rank != 0:
+        os._exit(0)  # this rank leaves between steps, before the next collective
+    m.tp_set_timeout(3000)
+    codes = []
+    t0 = time.time()
+    for _ in range(2):
+        try:
+            m.prefill(ids)
+            codes.append(0)
+        except abi.QwcError as e:
+            codes.append(e.code)
+    np.save(os.path.join(out_dir, "dead.npy"), np.array(codes + [time.time() - t0]))
+    m.close()
+    os._exit(0)
+
+
+def test_tp_prefill_returns_device_error_when_a_rank_is_gone(pkg, tmp_path):
+    """A rank that exits before a collective: the survivor's bounded wait runs out, its
+    communicator is aborted (the waiting NCCL kernels return) and qwc_prefill returns
+    QWC_E_DEVICE instead of hanging; the handle then refuses further passes."""
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    d = model_dir(pkg, "tiny")
+    ids = pkg.synth.random_prompt(pkg.synth.SHAPES["tiny"].vocab_size, 40, seed=6)
+    mp.start_processes(_dead_peer_main, args=(world, _free_port(), d, ids, str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    r = np.load(tmp_path / "dead.npy")
+    assert int(r[0]) == -7 and int(r[1]) == -7
+    assert r[2] < 60.0

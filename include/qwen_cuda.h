@@ -127,7 +127,12 @@ int64_t qwc_solve_max_context(const qwc_config* cfg, uint64_t ram_budget_bytes,
  * uploads them to `device` in the decode layout, and allocates all device arenas once
  * (sized by the memory equation). kv_dtype: QWC_DTYPE_F32 (the reference's cache
  * type) or QWC_DTYPE_BF16. Missing tensors -> QWC_E_MISSING with the name in the
- * error message. */
+ * error message. Weights are copied through pinned staging buffers (the caller's host
+ * buffers, e.g. a file mapping, are read once; no full host copy is made).
+ * max_context <= 0 plans the context from the device's free memory: solve_max_context
+ * (src/memory_budget.cpp:56-81) over the free bytes with the weights and state as fixed
+ * costs (qwc_max_context reports the chosen size); QWC_E_OOM when the model itself
+ * does not fit. */
 int qwc_create(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors,
                int max_context, int kv_dtype, int device, qwc_handle** out);
 
@@ -151,6 +156,18 @@ int qwc_reset(qwc_handle* h);
 
 /* QwenModel::position (include/qwen_model.h:27). */
 int qwc_position(const qwc_handle* h);
+
+/* Test of the decode step's bounded waits (no reference counterpart): runs one step in
+ * which one CTA never arrives at the first grid barrier, with every wait of the step
+ * limited to wait_ms (1..2000). The other CTAs' waits run out, the kernel posts an error
+ * code and returns, and the call returns QWC_E_DEVICE -- the path a real stall would
+ * take, exercised without a fault. Nothing hangs; the decode state is then undefined:
+ * call qwc_reset before the next step. */
+int qwc_check_step_timeout(qwc_handle* h, int wait_ms);
+
+/* The handle's context capacity (positions): the max_context it was created with, or the
+ * planned one. Not in the reference (its callers pass the value they chose). */
+int qwc_max_context(const qwc_handle* h);
 
 /* QwenModel::step (src/qwen_model.cpp:211-239): one token through all layers (one CUDA
  * graph replay). logits_host: [vocab] floats or NULL; argmax_out: the greedy id
@@ -277,6 +294,20 @@ int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full);
 int qwc_gemv_bf16(const uint16_t* W, const float* x, float* y, int out_dim, int in_dim,
                   void* stream);
 
+/* Int8 weights for the decode GEMV (no reference implementation: the reference names
+ * 8/4-bit weights as its next step for decode speed, README.md:80-81). A GEMV at batch 1
+ * streams its weights once per token, so 1-byte codes halve the bytes of the bf16 path.
+ * Format: codes Wq[out_dim][in_dim] int8 and one fp32 scale per row and 128-column group,
+ * scales[out_dim][in_dim / 128], w ~= q * scale.
+ * qwc_quantize_q8: from bf16 W on the device: scale = max |w| / 127 over the group,
+ *   q = round-to-nearest-even(w / scale) in [-127, 127] (0 codes for an all-zero group);
+ *   in_dim a multiple of 128.
+ * qwc_gemv_q8: y = dequant(W) . x in fp32 (per lane: the group's scale times the fp32 sum
+ *   of its codes times x); in_dim a multiple of 512, at most 8192. */
+int qwc_quantize_q8(const uint16_t* W, int8_t* Wq, float* scales, int out_dim, int in_dim, void* stream);
+int qwc_gemv_q8(const int8_t* Wq, const float* scales, const float* x, float* y, int out_dim, int in_dim,
+                void* stream);
+
 /* The projections of QwenForward::prefill (src/qwen_forward.cpp:154-206, each row a
  * matmul of src/forward_pass.cpp:65-75) for N tokens at once on the tensor cores:
  * Y[N][M] (=, or += when accumulate) sum_k X[n][k] W[m][k], W bf16 [M][K] row-major,
@@ -335,7 +366,13 @@ int qwc_attention_decode(const float* q, const float* gate, const void* k_cache,
  *    larger requests
  *    return QWC_E_INVALID with the sizes in qwc_last_error(NULL). NKV <= 64.
  *  - The first call on each device looks up the array's device address (with that
- *    device current); make that first call before any stream capture.
+ *    device current). With lazy module loading (the CUDA default) that first call may
+ *    also load the library's device code and so reserve the array: a caller that must
+ *    not allocate at all makes its first call during its own set-up, before any stream
+ *    capture.
+ *  - It always runs the per-position split kernel that qwc_attention_decode uses below
+ *    2048 cached positions; on longer caches it is slower than qwc_attention_decode,
+ *    which switches to its block-per-warp kernel there (results agree to rounding).
  *  - Every call on a device shares the one array: calls that overlap on the GPU (on
  *    different streams, or from different host threads) race and give wrong results.
  *    The split counters are cleared on `stream` at the start of each call. */

@@ -254,3 +254,30 @@ class RefModel:
         out = np.zeros(6, np.uint64)
         ref_lib().ref_budget(self._h, out)
         return out
+
+
+# ---------------------------------------------------------------- int8 weight format
+# No reference counterpart (the reference streams bf16 weights and names 8/4-bit weights as
+# its next step, README.md:80-81): the format's definition restated in numpy, as the checker
+# of qwc_quantize_q8 / qwc_gemv_q8. Groups of 128 columns per row.
+Q8_GROUP = 128
+
+
+def q8_quantize(w_bf16_bits: np.ndarray):
+    """bf16 bits [rows][cols] -> (int8 codes, fp32 scales [rows][cols / 128]):
+    scale = max |w| / 127 in fp32, q = round-half-even(w / scale) clamped to +-127."""
+    w = (w_bf16_bits.astype(np.uint32) << 16).view(np.float32)
+    rows, cols = w.shape
+    g = w.reshape(rows, cols // Q8_GROUP, Q8_GROUP)
+    scale = (np.abs(g).max(axis=2) / np.float32(127.0)).astype(np.float32)
+    safe = np.where(scale > 0, scale, np.float32(1.0)).astype(np.float32)
+    q = np.rint((g / safe[:, :, None]).astype(np.float32))
+    q = np.where(scale[:, :, None] > 0, np.clip(q, -127, 127), 0).astype(np.int8)
+    return q.reshape(rows, cols), scale
+
+
+def q8_gemv(q: np.ndarray, scale: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """y = dequant(q, scale) . x in float64 (the exact value the fp32 kernel approximates)."""
+    rows, cols = q.shape
+    w = q.astype(np.float64).reshape(rows, cols // Q8_GROUP, Q8_GROUP) * scale.astype(np.float64)[:, :, None]
+    return w.reshape(rows, cols) @ x.astype(np.float64)

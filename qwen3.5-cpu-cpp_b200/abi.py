@@ -27,9 +27,9 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_get_config", "qwc_reset", "qwc_position", "qwc_step", "qwc_generate_greedy",
            "qwc_forward_logits", "qwc_forward_hidden", "qwc_prefill", "qwc_stream", "qwc_set_prompt",
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
-           "qwc_gemv_bf16", "qwc_gemm_bf16",
+           "qwc_gemv_bf16", "qwc_gemm_bf16", "qwc_quantize_q8", "qwc_gemv_q8",
            "qwc_tp_shard_of", "qwc_tp_unique_id", "qwc_create_tp", "qwc_create_from_dir_tp",
-           "qwc_tp_gather_state", "qwc_tp_set_timeout",
+           "qwc_tp_gather_state", "qwc_max_context", "qwc_check_step_timeout", "qwc_tp_set_timeout",
            "qwc_gdn_decode_step", "qwc_gdn_prefill", "qwc_gdn_prefill_workspace",
            "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
@@ -108,6 +108,7 @@ def lib():
     L.qwc_get_config.argtypes = [vp, C.POINTER(qwc_config)]
     L.qwc_reset.argtypes = [vp]
     L.qwc_position.argtypes = [vp]
+    L.qwc_max_context.argtypes = [vp]
     L.qwc_step.argtypes = [vp, C.c_int, fp, ip]
     L.qwc_generate_greedy.argtypes = [vp, ip, C.c_int, C.c_int, ip]
     L.qwc_forward_logits.argtypes = [vp, ip, C.c_int, fp, C.c_int]
@@ -185,7 +186,7 @@ class Model:
         check(lib().qwc_get_config(self._h, C.byref(cfg)), self._h)
         self.cfg = cfg
         self.vocab = cfg.vocab_size
-        self.max_context = max_context
+        self.max_context = lib().qwc_max_context(self._h)  # the planned size for max_context <= 0
 
     def close(self):
         if getattr(self, "_h", None):
@@ -287,6 +288,13 @@ class Model:
         kinds = [KERNEL_KINDS[int(k)] for k in buf[2:2 + P]]
         return kinds, buf[2 + P:].reshape(G, P, 8)
 
+    def check_step_timeout(self, wait_ms: int):
+        """qwc_check_step_timeout: one step whose grid barrier cannot complete; returns the
+        status code (QWC_E_DEVICE expected) instead of raising."""
+        fn = lib().qwc_check_step_timeout
+        fn.argtypes = [C.c_void_p, C.c_int]
+        return int(fn(self._h, int(wait_ms)))
+
     def tp_set_timeout(self, ms: int):
         """qwc_tp_set_timeout: bound on every wait of this rank for its group."""
         fn = lib().qwc_tp_set_timeout
@@ -313,6 +321,20 @@ class Model:
 
 def gemv_bf16(W_ptr, x_ptr, y_ptr, out_dim, in_dim, stream=0):
     check(lib().qwc_gemv_bf16(W_ptr, x_ptr, y_ptr, out_dim, in_dim, stream))
+
+
+def quantize_q8(W_ptr, Wq_ptr, scales_ptr, out_dim, in_dim, stream=0):
+    """qwc_quantize_q8: int8 codes + per-(row, 128-group) fp32 scales from bf16 W."""
+    fn = lib().qwc_quantize_q8
+    fn.argtypes = [C.c_void_p] * 3 + [C.c_int, C.c_int, C.c_void_p]
+    check(fn(W_ptr, Wq_ptr, scales_ptr, out_dim, in_dim, stream))
+
+
+def gemv_q8(Wq_ptr, scales_ptr, x_ptr, y_ptr, out_dim, in_dim, stream=0):
+    """qwc_gemv_q8: y = dequant(Wq, scales) . x."""
+    fn = lib().qwc_gemv_q8
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_int, C.c_void_p]
+    check(fn(Wq_ptr, scales_ptr, x_ptr, y_ptr, out_dim, in_dim, stream))
 
 
 def gemm_bf16(W_ptr, Xs_ptr, Y_ptr, M, N, K, accumulate=False, stream=0):

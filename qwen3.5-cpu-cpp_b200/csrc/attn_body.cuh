@@ -141,7 +141,7 @@ __device__ __forceinline__ void attn_decode_item(const AttnDecodeParams& p, int 
     const int pos = decode ? *p.pos_ptr : p.n_ctx_val - 1;
 
     const int n_ctx = pos + 1;
-    int n_act = (n_ctx + kMinChunk - 1) / kMinChunk;
+    int n_act = (n_ctx + p.min_chunk - 1) / p.min_chunk;
     if (n_act > p.nsplit) n_act = p.nsplit;
     if (sp >= n_act) return;
     const int chunk = (n_ctx + n_act - 1) / n_act;

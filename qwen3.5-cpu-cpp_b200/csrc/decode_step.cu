@@ -115,6 +115,10 @@ __device__ __forceinline__ float dot8s(uint4 w, const float* x, float acc) {
     return acc;
 }
 
+__device__ __forceinline__ unsigned long long step_wait_ns(const StepParams& sp) {
+    return sp.wait_ns ? sp.wait_ns : kWaitLimitNs;
+}
+
 __device__ __forceinline__ bool step_aborted(const StepParams& sp) {
     return *reinterpret_cast<const volatile int*>(sp.dev_err) != 0;
 }
@@ -143,7 +147,7 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
     for (unsigned it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0 && step_aborted(sp)) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > step_wait_ns(sp)) {
             post_error(sp.dev_err, err);
             return false;
         }
@@ -195,7 +199,7 @@ __device__ __noinline__ void grid_wait(StepShared& S, const StepParams sp, int p
             const unsigned long long t0 = globaltimer_ns();
             while (ld_acquire_u64(sp.bar) < target) {
                 if (step_aborted(sp)) break;
-                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                if (globaltimer_ns() - t0 > step_wait_ns(sp)) {
                     post_error(sp.dev_err, DEV_STEP_BARRIER_TIMEOUT);
                     break;
                 }
@@ -416,7 +420,7 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
         const GemvParams& g = ph.g;
         const int grp = g.nq / g.nkv;
         const int n_ctx = *g.pos + 1;
-        int n_act = (n_ctx + kMinChunk - 1) / kMinChunk;
+        int n_act = (n_ctx + g.min_chunk - 1) / g.min_chunk;
         if (n_act > g.nsplit) n_act = g.nsplit;
         for (int h = warp; h < g.nq; h += kSW) {
             const int kv = h / grp, gg = h % grp;
@@ -448,28 +452,42 @@ __device__ __noinline__ void gemv_phase(StepShared& S, const StepParams sp, int 
         const float* x0 = ph.g.x;
         const float* z0 = ph.g.z;
         const float* nw = ph.g.norm_w;
-        for (int h = warp; h < nh; h += kSW) {
-            const float* o = x0 + (size_t)h * D;
-            const float* zz = z0 + (size_t)h * D;
-            float ov[4], zv[4], wv4[4];
+        // heads warp, warp + 8, ... (up to kGnHeads per warp): every load of all of them is
+        // issued before the first reduction, one memory round trip for the prologue
+        constexpr int kGnHeads = 4;
+        for (int h0 = warp; h0 < nh; h0 += kSW * kGnHeads) {
+            float ov[kGnHeads][4], zv[kGnHeads][4], wv4[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int i = lane + 32 * k;
-                const bool in_r = i < D;
-                ov[k] = in_r ? o[i] : 0.f;
-                zv[k] = in_r ? zz[i] : 0.f;
-                wv4[k] = in_r ? nw[i] : 0.f;
+                wv4[k] = i < D ? nw[i] : 0.f;
             }
-            double ss = 0.0;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) ss += (double)ov[k] * ov[k];
+            for (int j = 0; j < kGnHeads; ++j) {
+                const int h = h0 + j * kSW;
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-            const float inv = 1.0f / sqrtf((float)(ss / D) + eps);
+                for (int k = 0; k < 4; ++k) {
+                    const int i = lane + 32 * k;
+                    const bool in_r = h < nh && i < D;
+                    ov[j][k] = in_r ? x0[(size_t)h * D + i] : 0.f;
+                    zv[j][k] = in_r ? z0[(size_t)h * D + i] : 0.f;
+                }
+            }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = lane + 32 * k;
-                if (i < D) xs[(size_t)h * D + i] = wv4[k] * (ov[k] * inv) * silu_f(zv[k]);
+            for (int j = 0; j < kGnHeads; ++j) {
+                const int h = h0 + j * kSW;
+                if (h >= nh) break;
+                double ss = 0.0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) ss += (double)ov[j][k] * ov[j][k];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+                const float inv = 1.0f / sqrtf((float)(ss / D) + eps);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int i = lane + 32 * k;
+                    if (i < D) xs[(size_t)h * D + i] = wv4[k] * (ov[j][k] * inv) * silu_f(zv[j][k]);
+                }
             }
         }
         cta_sync();
@@ -734,7 +752,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) k_decode_step(const StepPara
             }
             cta_sync();  // every warp is done (also ends every read of the staged descriptor)
             trace_mark(sp, c, p, 3);
-            if (p + 1 < sp.nphases && tid == 0) red_release_add_u64(sp.bar, 1ull);  // orders this CTA's writes before it
+            // (a test may have one CTA withhold its first arrival: every other CTA's bounded
+            // wait then runs out and the step ends with an error, see qwc_check_step_timeout)
+            if (p + 1 < sp.nphases && tid == 0 && !(p == 0 && c == sp.stall_cta))
+                red_release_add_u64(sp.bar, 1ull);  // orders this CTA's writes before it
         }
     }
     __syncthreads();

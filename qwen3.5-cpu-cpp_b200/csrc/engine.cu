@@ -70,7 +70,7 @@ struct qwc_handle {
     int max_ctx = 0, kv_dtype = QWC_DTYPE_F32, kv_bytes = 4;
     int H = 0, I = 0, V = 0, L = 0, NQ = 0, NKV = 0, HD = 0, ROT = 0;
     int KH = 0, VH = 0, DK = 0, DV = 0, KD = 0, VD = 0, C = 0, KER = 0;
-    int n_gdn = 0, n_attn = 0, nsplit = 1;
+    int n_gdn = 0, n_attn = 0, nsplit = 1, step_min_chunk = 8;
     float eps = 1e-6f;
 
     // arenas
@@ -96,6 +96,7 @@ struct qwc_handle {
     unsigned *am_counter = nullptr, *attn_counters = nullptr;
 
     int* h_pin = nullptr;  // pinned host ints for small transfers
+    struct Stager* stager = nullptr;  // weight upload staging (creation only)
 
     // persistent decode-step kernel (step_grid == 0: per-kernel path)
     StepParams step;
@@ -303,9 +304,72 @@ struct Arena {
 
 }  // namespace
 
-static int upload_f32(qwc_handle* h, float* dst, const std::vector<float>& v) {
-    CU(cudaMemcpy(dst, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+// Weight upload through pinned staging: the checkpoint stays in the caller's (memory-
+// mapped) host buffers; each piece is packed into one of two pinned buffers and copied to
+// the device asynchronously, so the host packs piece k+1 while the DMA engine moves piece
+// k. No full-file host copy is made, and no pageable copy is synchronous.
+struct Stager {
+    static constexpr size_t kCap = 32u << 20;  // bytes per pinned buffer
+    cudaStream_t s = nullptr;
+    uint8_t* pin[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    int cur = 0;
+    bool ok = false;
+    explicit Stager(cudaStream_t stream) : s(stream) {
+        ok = cudaHostAlloc(&pin[0], kCap, cudaHostAllocDefault) == cudaSuccess &&
+             cudaHostAlloc(&pin[1], kCap, cudaHostAllocDefault) == cudaSuccess &&
+             cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming) == cudaSuccess;
+    }
+    ~Stager() {
+        if (s) cudaStreamSynchronize(s);
+        for (int i = 0; i < 2; ++i) {
+            if (pin[i]) cudaFreeHost(pin[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
+    }
+    // rows x width bytes from src (row pitch spitch) to dst (row pitch dpitch), in batches
+    // of whole rows that fit one buffer (a row wider than a buffer is split into columns)
+    cudaError_t copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows) {
+        if (width > kCap) {
+            for (size_t c0 = 0; c0 < width; c0 += kCap) {
+                const size_t w = std::min(kCap, width - c0);
+                cudaError_t e = copy2d(static_cast<uint8_t*>(dst) + c0, dpitch, static_cast<const uint8_t*>(src) + c0,
+                                       spitch, w, rows);
+                if (e != cudaSuccess) return e;
+            }
+            return cudaSuccess;
+        }
+        const size_t per = kCap / width;
+        for (size_t r0 = 0; r0 < rows; r0 += per) {
+            const size_t n = std::min(per, rows - r0);
+            cudaError_t e = cudaEventSynchronize(done[cur]);  // this buffer's previous DMA is over
+            if (e != cudaSuccess) return e;
+            const uint8_t* sp = static_cast<const uint8_t*>(src) + r0 * spitch;
+            if (spitch == width) {
+                std::memcpy(pin[cur], sp, n * width);
+            } else {
+                for (size_t r = 0; r < n; ++r) std::memcpy(pin[cur] + r * width, sp + r * spitch, width);
+            }
+            e = cudaMemcpy2DAsync(static_cast<uint8_t*>(dst) + r0 * dpitch, dpitch, pin[cur], width, width, n,
+                                  cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return e;
+            if ((e = cudaEventRecord(done[cur], s)) != cudaSuccess) return e;
+            cur ^= 1;
+        }
+        return cudaSuccess;
+    }
+};
+
+static int h2d(qwc_handle* h, void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows) {
+    cudaError_t e = h->stager ? h->stager->copy2d(dst, dpitch, src, spitch, width, rows)
+                              : cudaMemcpy2D(dst, dpitch, src, spitch, width, rows, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail(h, QWC_E_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
     return QWC_OK;
+}
+
+static int upload_f32(qwc_handle* h, float* dst, const std::vector<float>& v) {
+    return h2d(h, dst, v.size() * sizeof(float), v.data(), v.size() * sizeof(float), v.size() * sizeof(float), 1);
 }
 
 // Copies a BF16 matrix [rows][cols] into dst with destination row pitch `dpitch` elements.
@@ -315,8 +379,7 @@ static int upload_mat(qwc_handle* h, uint16_t* dst, size_t dpitch, const qwc_ten
         return fail(h, QWC_E_SHAPE, std::string("matrix ") + t->name + " must be BF16");
     if (numel_of(t) != rows * cols)
         return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected shape");
-    CU(cudaMemcpy2D(dst, dpitch * 2, t->data, cols * 2, cols * 2, rows, cudaMemcpyHostToDevice));
-    return QWC_OK;
+    return h2d(h, dst, dpitch * 2, t->data, cols * 2, cols * 2, rows);
 }
 
 // Rows [row0, row0+nrows) of a BF16 matrix [total_rows][cols] into dst (row pitch dpitch).
@@ -327,8 +390,7 @@ static int upload_rows(qwc_handle* h, uint16_t* dst, size_t dpitch, const qwc_te
     if (numel_of(t) != total_rows * cols)
         return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected shape");
     const uint16_t* src = static_cast<const uint16_t*>(t->data) + row0 * cols;
-    CU(cudaMemcpy2D(dst, dpitch * 2, src, cols * 2, cols * 2, nrows, cudaMemcpyHostToDevice));
-    return QWC_OK;
+    return h2d(h, dst, dpitch * 2, src, cols * 2, cols * 2, nrows);
 }
 
 // Columns [col0, col0+ncols) of a BF16 matrix [rows][total_cols] into a dense [rows][ncols].
@@ -339,8 +401,7 @@ static int upload_cols(qwc_handle* h, uint16_t* dst, const qwc_tensor* t, int64_
     if (numel_of(t) != rows * total_cols)
         return fail(h, QWC_E_SHAPE, std::string("tensor ") + t->name + " has an unexpected shape");
     const uint16_t* src = static_cast<const uint16_t*>(t->data) + col0;
-    CU(cudaMemcpy2D(dst, ncols * 2, src, total_cols * 2, ncols * 2, rows, cudaMemcpyHostToDevice));
-    return QWC_OK;
+    return h2d(h, dst, ncols * 2, src, total_cols * 2, ncols * 2, rows);
 }
 
 static int vec_f32(qwc_handle* h, const qwc_tensor* t, int64_t n, std::vector<float>& out, float add = 0.f) {
@@ -485,12 +546,16 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
         if ((rc = upload_mat(h, const_cast<uint16_t*>(h->embed), H, emb, h->V, H) )) {
             // the embedding may hold more rows than vocab_size: upload only vocab_size rows
             if (emb->dtype != QWC_DTYPE_BF16) return rc;
-            CU(cudaMemcpy(const_cast<uint16_t*>(h->embed), emb->data, (size_t)h->V * H * 2, cudaMemcpyHostToDevice));
+            if ((rc = h2d(h, const_cast<uint16_t*>(h->embed), (size_t)H * 2, emb->data, (size_t)H * 2, (size_t)H * 2,
+                          (size_t)h->V)))
+                return rc;
         }
         if (lmh) {
             if (lmh->dtype != QWC_DTYPE_BF16 || lmh->ndim != 2 || lmh->shape[1] != H || lmh->shape[0] < h->V)
                 return fail(h, QWC_E_SHAPE, "lm_head.weight must be BF16 [>=vocab, hidden]");
-            CU(cudaMemcpy(const_cast<uint16_t*>(h->head), lmh->data, (size_t)h->V * H * 2, cudaMemcpyHostToDevice));
+            if ((rc = h2d(h, const_cast<uint16_t*>(h->head), (size_t)H * 2, lmh->data, (size_t)H * 2, (size_t)H * 2,
+                          (size_t)h->V)))
+                return rc;
         }
         if ((rc = vec_f32(h, fn, H, tmp, 1.0f)) || (rc = upload_f32(h, const_cast<float*>(h->final_ln1), tmp))) return rc;
         // RoPE table, exactly as apply_rope evaluates it (src/forward_pass.cpp:102-112):
@@ -506,7 +571,8 @@ static int place_weights(qwc_handle* h, Builder& b, Arena& a) {
                     tab[((size_t)pp * half + i) * 2] = (float)std::cos(ang);
                     tab[((size_t)pp * half + i) * 2 + 1] = (float)std::sin(ang);
                 }
-            CU(cudaMemcpy(const_cast<float*>(h->rope_cs), tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+            if ((rc = h2d(h, const_cast<float*>(h->rope_cs), tab.size() * 4, tab.data(), tab.size() * 4, tab.size() * 4, 1)))
+                return rc;
         }
     }
     if (!b.missing.empty()) return fail(h, QWC_E_MISSING, "[qwen] missing weight: " + b.missing);
@@ -532,7 +598,7 @@ struct StepProfile {
 // The decode step as a list of phases (one per kernel of the per-kernel path, one per
 // grid-barrier phase of the persistent kernel), with the profiling kind of each.
 static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std::vector<StepPhase>& out,
-                        std::vector<int>& kinds, bool defer_attn = false) {
+                        std::vector<int>& kinds, bool defer_attn = false, int min_chunk = 32) {
     const int H = h->H;
     out.clear();
     kinds.clear();
@@ -589,6 +655,7 @@ static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std
             a.NKV = h->NKV;
             a.rot = h->ROT;
             a.nsplit = attn_nsplit;
+            a.min_chunk = min_chunk;
             a.eps = h->eps;
             a.defer_combine = defer_attn ? 1 : 0;
             out.push_back(ph);
@@ -608,6 +675,7 @@ static void make_phases(qwc_handle* h, const StateView& sv, int attn_nsplit, std
                 o.part_ml = h->part_ml;
                 o.pos = h->pos;
                 o.nsplit = attn_nsplit;
+                o.min_chunk = min_chunk;
                 o.nq = h->NQ;
                 o.nkv = h->NKV;
             }
@@ -768,11 +836,12 @@ static int setup_persistent(qwc_handle* h) {
     if (h->H % 256 || h->I % 256 || h->VD % 256 || (h->NQ * h->HD) % 256 || h->H > 4096) return QWC_OK;
     const int xs_max = std::max({h->H, h->I, h->VD, h->NQ * h->HD});
     const int grid0 = num_sms();
-    // attention items are spread one per CTA: at most grid / NKV splits
-    const int nsplit = std::max(1, std::min(h->nsplit, grid0 / h->NKV));
+    // attention items are spread one per CTA: at most grid / NKV splits of >= step_min_chunk
+    const int nsplit = std::max(1, std::min({h->nsplit, grid0 / h->NKV,
+                                             (h->max_ctx + h->step_min_chunk - 1) / h->step_min_chunk}));
     std::vector<StepPhase> phases;
     // the o_proj phase combines the split attention partials when a warp per q head fits
-    make_phases(h, h->st, nsplit, phases, h->step_kinds, /*defer_attn=*/h->NQ <= 8);
+    make_phases(h, h->st, nsplit, phases, h->step_kinds, /*defer_attn=*/h->NQ <= 8, h->step_min_chunk);
     const int np = (int)phases.size();
     // Ring depth: three 4 KB slots per consumer warp (96 KB per SM) measured fastest with
     // the producer warp; deeper rings queue latency-critical loads behind weights.
@@ -891,9 +960,36 @@ extern "C" int qwc_create_tp(const qwc_config* cfg, const qwc_tensor* tensors, i
     return create_impl(cfg, tensors, n_tensors, max_context, kv_dtype, device, rank, world, unique_id, out);
 }
 
+// The longest context that fits the current device's free memory (max_context <= 0 at
+// creation): solve_max_context over the free bytes with the weight arena (as measured
+// with a one-position RoPE table), the GDN state and conv ring as fixed costs, a reserve
+// for the scratch, the step kernel and the batched pass's workspace, and an effective
+// per-element KV size that also carries the per-position RoPE table, token slot and
+// batched-pass attention operands.
+static int64_t plan_max_context(qwc_handle* h) {
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return -1;
+    qwc_config local = h->cfg;
+    local.gdn_k_heads = h->KH;
+    local.gdn_v_heads = h->VH;
+    local.attn_q_heads = h->NQ;
+    local.attn_kv_heads = h->NKV;
+    local.ffn_intermediate = h->I;
+    qwc_budget b{};
+    qwc_compute_budget(&local, 2, 1, h->kv_bytes, 4, 1024, &b);
+    const uint64_t state = b.gdn_state_bytes + (uint64_t)h->n_gdn * h->C * 4 * sizeof(float);
+    const uint64_t per_elem_tokens = (uint64_t)h->n_attn * 2 * h->NKV * h->HD;  // KV elements per position
+    if (per_elem_tokens == 0) return h->cfg.native_max_context;
+    const uint64_t extra = (uint64_t)h->ROT * 4 + 8 + (uint64_t)8 * h->NKV * h->HD * h->n_attn;
+    const int kvb_eff = (int)((per_elem_tokens * h->kv_bytes + extra + per_elem_tokens - 1) / per_elem_tokens);
+    const uint64_t reserve = 3ull << 30;  // scratch, step, batched-pass workspace (4096-token chunks)
+    const uint64_t margin = 512ull << 20;
+    return qwc_solve_max_context(&local, free_b, h->w_bytes, state, reserve, 0, margin, kvb_eff);
+}
+
 static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_tensors, int max_context,
                        int kv_dtype, int device, int rank, int world, const void* unique_id, qwc_handle** out) {
-    if (!cfg || !out || (!tensors && n_tensors > 0) || max_context <= 0 || world < 1 || rank < 0 || rank >= world)
+    if (!cfg || !out || (!tensors && n_tensors > 0) || world < 1 || rank < 0 || rank >= world)
         return fail(nullptr, QWC_E_INVALID, "qwc_create: invalid argument");
     if (kv_dtype != QWC_DTYPE_F32 && kv_dtype != QWC_DTYPE_BF16)
         return fail(nullptr, QWC_E_INVALID, "qwc_create: kv_dtype must be F32 or BF16");
@@ -913,7 +1009,7 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
     h->pf_timing = pt && pt[0] == '1';
     const char* np = std::getenv("QWC_NO_PDL");
     h->use_pdl = !(np && np[0] == '1');
-    h->max_ctx = max_context;
+    h->max_ctx = max_context > 0 ? max_context : 0;  // 0: planned once the weights are measured
     h->kv_dtype = kv_dtype;
     h->kv_bytes = kv_dtype == QWC_DTYPE_BF16 ? 2 : 4;
     h->H = cfg->hidden_size;
@@ -964,6 +1060,23 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
     rc = place_weights(h, b, meas);
     if (rc) { g_last_error = h->err; delete h; return rc; }
     h->w_bytes = meas.off;
+    if (h->max_ctx <= 0) {
+        // max_context <= 0: the longest context that fits the device's free memory, planned
+        // with the memory equation (solve_max_context, src/memory_budget.cpp:56-81)
+        int64_t ctx = plan_max_context(h);
+        if (ctx < 1) {
+            fail(h, QWC_E_OOM, "qwc_create: the model does not fit the free device memory");
+            g_last_error = h->err;
+            delete h;
+            return QWC_E_OOM;
+        }
+        h->max_ctx = (int)std::min<int64_t>(ctx, 1 << 30);
+        max_context = h->max_ctx;
+        Arena again;  // the RoPE table grows with the context
+        rc = place_weights(h, b, again);
+        if (rc) { g_last_error = h->err; delete h; return rc; }
+        h->w_bytes = again.off;
+    }
 
     auto bail = [&](int code) { g_last_error = h->err; qwc_destroy(h); return code; };
     if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -972,7 +1085,12 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
         return bail(fail(h, QWC_E_OOM, "weight arena allocation failed"));
     Arena real;
     real.base = h->w_arena;
-    rc = place_weights(h, b, real);
+    {
+        Stager st(h->stream);
+        if (st.ok) h->stager = &st;  // else plain synchronous copies
+        rc = place_weights(h, b, real);
+        h->stager = nullptr;
+    }  // every staged copy has completed here
     if (rc) return bail(rc);
 
     // state arenas, sized by the memory equation (compute_budget with bpw 2) for this shard
@@ -997,6 +1115,11 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
 
     // scratch arena
     h->nsplit = attn_nsplit_for(max_context, h->NKV);
+    // the persistent step splits attention into items of >= step_min_chunk positions (one
+    // per warp at 8), one (kv head, split) item per CTA: the partials are sized for both
+    if (const char* e = std::getenv("QWC_STEP_MIN_CHUNK")) h->step_min_chunk = std::max(1, std::atoi(e));
+    h->nsplit = std::max(h->nsplit, std::min((max_context + h->step_min_chunk - 1) / h->step_min_chunk,
+                                             std::max(1, num_sms() / h->NKV)));
     const int grp = h->NQ / h->NKV;
     Arena s;
     auto carve = [&](size_t bytes) { return s.take(bytes); };
@@ -1087,6 +1210,8 @@ extern "C" int qwc_reset(qwc_handle* h) {
 }
 
 extern "C" int qwc_position(const qwc_handle* h) { return h ? h->pos_host : -1; }
+
+extern "C" int qwc_max_context(const qwc_handle* h) { return h ? h->max_ctx : -1; }
 
 extern "C" int qwc_step(qwc_handle* h, int token, float* logits_host, int* argmax_out) {
     if (!h) return fail(nullptr, QWC_E_INVALID, "qwc_step: null handle");
@@ -1824,6 +1949,19 @@ extern "C" int qwc_trace_step(qwc_handle* h, int cap, int64_t* out) {
     return need;
 }
 
+extern "C" int qwc_check_step_timeout(qwc_handle* h, int wait_ms) {
+    if (!h || wait_ms <= 0 || wait_ms > 2000) return fail(h, QWC_E_INVALID, "qwc_check_step_timeout: invalid argument");
+    if (h->step_grid <= 0) return fail(h, QWC_E_INVALID, "qwc_check_step_timeout: the persistent decode step is not in use");
+    CU(cudaSetDevice(h->device));
+    CU(cudaStreamSynchronize(h->stream));
+    StepParams sp = h->step;
+    sp.wait_ns = (unsigned long long)wait_ms * 1000000ull;
+    sp.stall_cta = 0;  // CTA 0 never arrives at the first grid barrier
+    if (launch_decode_step(sp, h->NQ / h->NKV, h->step_grid, h->stream) != cudaSuccess)
+        return fail(h, QWC_E_CUDA, "qwc_check_step_timeout: launch failed");
+    return check_device_error(h);  // QWC_E_DEVICE: the waits ran out and the step stopped
+}
+
 // ------------------------------------------------------------------ kernel-level API
 static int* kernel_api_err() {
     int* p = nullptr;
@@ -1844,6 +1982,23 @@ extern "C" int qwc_gemv_bf16(const uint16_t* W, const float* x, float* y, int ou
     p.dev_err = kernel_api_err();
     cudaError_t e = launch_gemv(PRO_PLAIN, EPI_STORE, p, gemv_grid(out_dim), (cudaStream_t)stream, false);
     if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gemv_bf16: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+extern "C" int qwc_quantize_q8(const uint16_t* W, int8_t* Wq, float* scales, int out_dim, int in_dim, void* stream) {
+    if (!W || !Wq || !scales || out_dim <= 0 || in_dim <= 0 || in_dim % 128)
+        return fail(nullptr, QWC_E_INVALID, "qwc_quantize_q8: invalid argument (in_dim must be a multiple of 128)");
+    cudaError_t e = launch_quantize_q8(W, Wq, scales, out_dim, in_dim, (cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_quantize_q8: ") + cudaGetErrorString(e));
+    return QWC_OK;
+}
+
+extern "C" int qwc_gemv_q8(const int8_t* Wq, const float* scales, const float* x, float* y, int out_dim, int in_dim,
+                           void* stream) {
+    if (!Wq || !scales || !x || !y || out_dim <= 0 || in_dim <= 0 || in_dim % 512 || in_dim > 8192)
+        return fail(nullptr, QWC_E_INVALID, "qwc_gemv_q8: invalid argument (in_dim a multiple of 512, at most 8192)");
+    cudaError_t e = launch_gemv_q8(Wq, scales, x, y, out_dim, in_dim, (cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(nullptr, QWC_E_CUDA, std::string("qwc_gemv_q8: ") + cudaGetErrorString(e));
     return QWC_OK;
 }
 

@@ -61,11 +61,18 @@ struct GemvParams {
     const float* part_o = nullptr;
     const float* part_ml = nullptr;
     int nsplit = 1, nq = 0, nkv = 0;
+    int min_chunk = 32;             // positions per attention split at least (as the splits)
 };
 
 size_t gemv_smem_bytes(const GemvParams& p);
 cudaError_t launch_gemv(int pro, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl);
 int gemv_grid(int rows, int per_sm = 1);
+
+// Int8-weight GEMV (gemv_q8.cu): codes [rows][in_dim] int8 + fp32 scales [rows][in_dim/128];
+// in_dim a multiple of 512 (<= 8192) for the GEMV, of 128 for the quantiser.
+cudaError_t launch_quantize_q8(const uint16_t* W, int8_t* Wq, float* scales, int rows, int in_dim, cudaStream_t s);
+cudaError_t launch_gemv_q8(const int8_t* W, const float* scales, const float* x, float* y, int rows, int in_dim,
+                           cudaStream_t s);
 
 // ------------------------------------------------------------------ GDN decode
 // One token of the Gated DeltaNet mixer core (qwen_model.cpp:173-207): causal conv over
@@ -111,6 +118,7 @@ struct AttnDecodeParams {
     float eps = 1e-6f;
     int defer_combine = 0;          // every split only publishes its partial; the consumer
                                     // of `out` combines them (PRO_ATTN_COMBINE)
+    int min_chunk = 32;             // positions per split at least
 };
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t s, bool pdl);
 int attn_nsplit_for(int max_ctx, int nkv);
@@ -138,6 +146,8 @@ struct StepParams {
     int* dev_err = nullptr;
     int nslot = 4;                      // ring slots per warp (4 KB each)
     int xs_max = 0;                     // largest GEMV x length (floats)
+    unsigned long long wait_ns = 0;     // limit of every wait of the step (0: kWaitLimitNs)
+    int stall_cta = -1;                 // test only: this CTA withholds its first grid arrival
     long long* trace = nullptr;         // optional [grid][nphases][8] globaltimer stamps / counters
 };
 static_assert(sizeof(StepPhase) % 16 == 0, "staged as int4");

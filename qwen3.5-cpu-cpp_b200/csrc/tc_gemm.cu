@@ -31,6 +31,7 @@
 // Every wait is bounded: on a timeout the kernel posts an error code and all roles stop.
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_util.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -48,49 +49,14 @@ constexpr int kAccCols = 2 * kTN;                // columns of one tile's two ac
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr size_t kTcSmem = (size_t)kTStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
 
-// ---------------------------------------------------------------- PTX wrappers
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-// Shared-memory matrix descriptor of a K-major tile with 128-byte rows in the 128-byte
-// swizzle layout that TMA writes: 8-row groups 1024 bytes apart (SBO), leading offset
-// unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B). Tiles are 1024-aligned.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-           (2ull << 61);
-}
 // Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, M=128, N=128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
-                            ((uint32_t)(kTM >> 4) << 24);
+constexpr uint32_t kIdesc = tc::idesc_bf16(kTM, kTN);
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accum) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(kIdesc), "r"(accum)
-        : "memory");
-}
-// Arrive on `bar` once every tcgen05.mma issued so far by this thread has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 // 16 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    tc::ld16_nowait(taddr, r);
+    tc::ld_wait();
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
@@ -134,13 +100,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
         fence_mbar_init();
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tc::tmem_alloc(tmem_slot, kTmemCols);
     }
-    tc_fence_before();
+    tc::fence_before();
     __syncthreads();
-    tc_fence_after();
+    tc::fence_after();
     const uint32_t tmem = *tmem_slot;
     auto aborted = [&]() { return *reinterpret_cast<volatile int*>(s_abort) != 0; };
     auto abort_with = [&](int code) {
@@ -160,10 +124,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 uint8_t* st = smem + (size_t)s * kStageBytes;
                 mbar_arrive_expect_tx(&full[s], kStageBytes);
                 // rows past M (a partial or empty second weight tile) read as zero
-                tma_load_2d(st, &mapW, kb * kTK, m0, &full[s]);
-                tma_load_2d(st + kTileABytes, &mapW, kb * kTK, m0 + kTM, &full[s]);
-                tma_load_2d(st + 2 * kTileABytes, &mapX, kb * kTK, n0, &full[s]);
-                tma_load_2d(st + 2 * kTileABytes + kTileBBytes, &mapX, p.K + kb * kTK, n0, &full[s]);
+                tc::tma2d(st, &mapW, kb * kTK, m0, &full[s]);
+                tc::tma2d(st + kTileABytes, &mapW, kb * kTK, m0 + kTM, &full[s]);
+                tc::tma2d(st + 2 * kTileABytes, &mapX, kb * kTK, n0, &full[s]);
+                tc::tma2d(st + 2 * kTileABytes + kTileBBytes, &mapX, p.K + kb * kTK, n0, &full[s]);
             }
         }
         // every stage issued has been consumed (its MMAs completed) before the CTA exits
@@ -180,32 +144,32 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const int buf = it & 1;
             const uint32_t use = (uint32_t)(it >> 1);
             if (!mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, p.err, DEV_TC_MMA_TIMEOUT)) { abort_with(DEV_TC_MMA_TIMEOUT); break; }
-            tc_fence_after();
+            tc::fence_after();
             const uint32_t d0 = tmem + (uint32_t)(buf * kAccCols), d1 = d0 + kTN;
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++kc) {
                 const int s = (int)(kc % kTStages);
                 const uint32_t ph = (uint32_t)((kc / kTStages) & 1);
                 if (!mbar_wait_bounded(&full[s], ph, p.err, DEV_TC_MMA_TIMEOUT)) { ok = false; break; }
-                tc_fence_after();
+                tc::fence_after();
                 const uint32_t a0 = sbase + (uint32_t)s * kStageBytes;
-                const uint64_t da0 = sw128_desc(a0), da1 = sw128_desc(a0 + kTileABytes),
-                               dh = sw128_desc(a0 + 2 * kTileABytes), dl = sw128_desc(a0 + 2 * kTileABytes + kTileBBytes);
+                const uint64_t da0 = tc::desc128(a0), da1 = tc::desc128(a0 + kTileABytes),
+                               dh = tc::desc128(a0 + 2 * kTileABytes), dl = tc::desc128(a0 + 2 * kTileABytes + kTileBBytes);
 #pragma unroll
                 for (int ks = 0; ks < kTK / 16; ++ks) {
                     const uint64_t adv = (uint64_t)((ks * 32) >> 4);  // +32 bytes along K
                     const uint32_t first = (kb | ks) != 0 ? 1u : 0u;
-                    umma_bf16(d0, da0 + adv, dh + adv, first);
-                    umma_bf16(d0, da0 + adv, dl + adv, 1u);
-                    umma_bf16(d1, da1 + adv, dh + adv, first);
-                    umma_bf16(d1, da1 + adv, dl + adv, 1u);
+                    tc::mma_ss(d0, da0 + adv, dh + adv, kIdesc, first);
+                    tc::mma_ss(d0, da0 + adv, dl + adv, kIdesc, 1u);
+                    tc::mma_ss(d1, da1 + adv, dh + adv, kIdesc, first);
+                    tc::mma_ss(d1, da1 + adv, dl + adv, kIdesc, 1u);
                 }
-                umma_commit(&empty[s]);  // stage free once these MMAs have read it
+                tc::commit(&empty[s]);  // stage free once these MMAs have read it
             }
             if (!ok) { abort_with(DEV_TC_MMA_TIMEOUT); break; }
-            umma_commit(&acc_full[buf]);  // accumulator complete
+            tc::commit(&acc_full[buf]);  // accumulator complete
         }
-        umma_commit(mma_done);
+        tc::commit(mma_done);
         mbar_wait_bounded(mma_done, 0u, p.err, DEV_TC_DRAIN_TIMEOUT);
     } else if (warp >= 2) {
         // ------------------------------------------------ epilogue
@@ -218,7 +182,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             bool ok = mbar_wait_bounded(&acc_full[buf], use & 1u, p.err, DEV_TC_EPI_TIMEOUT);
             ok = __all_sync(0xffffffffu, ok && !aborted());
             if (!ok) break;
-            tc_fence_after();
+            tc::fence_after();
             const int n0 = (tile % ntn) * kTN;
             for (int c = half * kTN; c < (half + 1) * kTN; c += 16) {
                 // columns [0, 128): features m0 + lane row; [128, 256): the second weight tile
@@ -272,16 +236,16 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                 }
             }
-            tc_fence_before();
+            tc::fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
-    tc_fence_before();
+    tc::fence_before();
     __syncthreads();
     if (warp == 1) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+        tc::fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
     }
 }
 

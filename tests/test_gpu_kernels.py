@@ -219,3 +219,30 @@ def test_gdn_op_configs1_full_length(pkg, oracle):
     assert rel_l2(got[:T], want[:T]) < 1e-4
     assert rel_l2(got[T:], want[T:]) < 1e-4
     assert rel_l2(d_state.cpu().numpy(), st_want) < 1e-4
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 512), (37, 1024), (1024, 1024), (8224, 1024), (1024, 3584),
+                                       (2048, 6144), (151936, 1024)])
+def test_q8_quantize_and_gemv_match_the_format(pkg, oracle, rows, cols):
+    """Int8 weight GEMV: the device quantiser gives the format's codes and scales bit for
+    bit (including an all-zero group and a group with one outlier), and the GEMV matches
+    the dequantised product to fp32 accumulation error."""
+    rng = np.random.default_rng(rows + cols)
+    w = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02).astype(np.float32)
+    w[0, :128] = 0.0                                 # an all-zero group: scale 0, codes 0
+    w[-1, 5] = 3.0                                   # an outlier dominating its group
+    wb = pkg.synth.f32_to_bf16_bits(w)
+    x = rng.standard_normal(cols, dtype=np.float32)
+    q_want, s_want = oracle.q8_quantize(wb)
+    d_w = dev(wb.view(np.int16))
+    d_q = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
+    d_s = torch.empty((rows, cols // 128), dtype=torch.float32, device="cuda")
+    d_x, d_y = dev(x), torch.full((rows,), float("nan"), device="cuda")
+    pkg.abi.quantize_q8(d_w.data_ptr(), d_q.data_ptr(), d_s.data_ptr(), rows, cols)
+    pkg.abi.gemv_q8(d_q.data_ptr(), d_s.data_ptr(), d_x.data_ptr(), d_y.data_ptr(), rows, cols)
+    torch.cuda.synchronize()
+    assert np.array_equal(d_q.cpu().numpy(), q_want)
+    assert np.array_equal(d_s.cpu().numpy(), s_want)
+    y = d_y.cpu().numpy()
+    assert np.isfinite(y).all()
+    assert rel_l2(y, oracle.q8_gemv(q_want, s_want, x)) < TOL

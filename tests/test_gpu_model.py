@@ -4,6 +4,8 @@ restatement of the reference, itself pinned to the reference's own outputs).
 Bar (north star): greedy tokens identical; logits rel_l2 <= 2e-3. The decode path keeps
 fp32 activations and accumulation over bf16 weights like the reference, so the observed
 error is ~1e-6."""
+import os
+
 import numpy as np
 import pytest
 
@@ -105,4 +107,43 @@ def test_measurement_entry_points(pkg, oracle):
         # stamps are ordered within every CTA and phase: start <= barrier <= end
         assert (st[:, :, 1] >= st[:, :, 0]).all() and (st[:, :, 3] >= st[:, :, 1]).all()
         assert m.position() == pos + 2
+    m.close()
+
+
+def test_context_planned_from_free_memory(pkg):
+    """max_context <= 0: the capacity is planned from the device's free memory with the
+    memory equation (capped at the config's native context); decoding is unchanged."""
+    d = model_dir(pkg, "tiny")
+    s = pkg.synth.SHAPES["tiny"]
+    prompt = pkg.synth.random_prompt(s.vocab_size, 6, seed=2)
+    m = pkg.abi.Model(d, max_context=0)
+    cfg = pkg.abi.load_config(os.path.join(d, "config.json"))
+    assert 1024 < m.max_context <= cfg.native_max_context
+    ref = pkg.abi.Model(d, max_context=32)
+    assert ref.max_context == 32
+    for t in prompt:
+        a, _ = m.step(int(t))
+        b, _ = ref.step(int(t))
+        assert np.array_equal(a, b)
+    m.close()
+    ref.close()
+
+
+def test_bounded_wait_expiry_returns_device_error_and_recovers(pkg, oracle):
+    """One CTA withholds its first grid-barrier arrival (qwc_check_step_timeout): the other
+    CTAs' waits run out after 50 ms, the step stops with an error code, the call returns
+    QWC_E_DEVICE; after qwc_reset the handle decodes exactly as before."""
+    d = model_dir(pkg, "small-0.8b-widths")
+    s = pkg.synth.SHAPES["small-0.8b-widths"]
+    prompt = pkg.synth.random_prompt(s.vocab_size, 5, seed=8)
+    m = pkg.abi.Model(d, max_context=32)
+    m.step(int(prompt[0]))
+    assert m.check_step_timeout(50) == -7
+    m.reset()
+    orc = oracle.OracleModel(d, 32)
+    for t in prompt:
+        lg, _ = m.step(int(t))
+        ref = orc.step(int(t))
+        assert rel_l2(lg, ref) < LOGIT_TOL
+    assert m.generate_greedy(prompt, 6).tolist() == orc.generate_greedy(prompt, 6).tolist()
     m.close()

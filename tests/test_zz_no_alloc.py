@@ -33,9 +33,13 @@ def _inputs(pkg, n_ctx, kv_dtype, NQ=8, NKV=2, seed=0):
     return q, gate, torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(), max_ctx
 
 
-def test_noalloc_matches_regular_entry_two_calls(pkg):
-    NQ, NKV = 8, 2
-    for call, (n_ctx, kv_dtype) in enumerate([(4099, 0), (777, 1)]):
+@pytest.mark.parametrize("NQ,NKV,cases", [
+    (8, 2, [(4099, 0), (777, 1)]),   # several splits, then the array's leftovers reused
+    (8, 2, [(20, 0), (32, 1)]),      # one split: the result is written without a combine
+    (8, 1, [(8192, 1), (5000, 0)]),  # GQA group 8 with > 128 splits: the unstaged combine
+])
+def test_noalloc_matches_regular_entry_two_calls(pkg, NQ, NKV, cases):
+    for call, (n_ctx, kv_dtype) in enumerate(cases):
         q, gate, K, V, max_ctx = _inputs(pkg, n_ctx, kv_dtype, NQ, NKV, seed=call)
         want = torch.empty((NQ, 256), device="cuda")
         got = torch.full((NQ, 256), float("nan"), device="cuda")
@@ -62,3 +66,22 @@ def test_noalloc_rejects_workspace_beyond_limit(pkg):
                                          out.data_ptr())
     assert e.value.code == -1
     assert "exceeds" in str(e.value)
+
+
+def test_noalloc_leaves_device_memory_unchanged(pkg):
+    """A warmed-up call allocates nothing: the device's free memory is the same after it
+    (the first call of the process may load the library's device module, which reserves
+    the array; that happens in the warm-up call)."""
+    NQ, NKV, n_ctx = 8, 2, 3000
+    q, gate, K, V, max_ctx = _inputs(pkg, n_ctx, 0, NQ, NKV, seed=9)
+    out = torch.empty((NQ, 256), device="cuda")
+    args = (q.data_ptr(), gate.data_ptr(), K.data_ptr(), V.data_ptr(), 0, NQ, NKV, max_ctx, n_ctx,
+            out.data_ptr())
+    pkg.abi.attention_decode_noalloc(*args)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        pkg.abi.attention_decode_noalloc(*args)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0

@@ -38,6 +38,9 @@ the forward pass (2 x projection parameters per token, causal attention
 4 NQ HD (t+1) per token per attention layer, GDN 7 DK DV per head per token per GDN layer,
 the lm_head for the last token) against the measured bf16 peak.
 
+--workload q8-gemv times the int8-weight GEMV (qwc_gemv_q8, no reference counterpart) on
+the lm_head shape against the bf16 GEMV of the same shape.
+
 --workload gdn-op / attn-op time the mixer ops of configs[1] and configs[2] through the
 kernel-level C ABI on device buffers: the GDN core (16 heads, 128/128, conv K=4; seeded
 N(0,1) inputs rounded to bf16 values, A_log ~ U(0, ln 16)) as a 4096-token chunked prefill
@@ -572,6 +575,75 @@ def run_attn_op(args):
     return 0
 
 
+def run_q8_gemv(args):
+    """Int8-weight decode GEMV (qwc_gemv_q8) on the lm_head shape of the 0.8B-shaped model
+    (151936 x 1024, the largest GEMV of a decode step), against the bf16 GEMV of the same
+    shape: bytes per call, GB/s against the measured copy bandwidth, and the result against
+    the format's dequantised product (oracle.q8_gemv)."""
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    abi = pkg.abi
+    from oracle import bindings
+    rows, cols = 151936, 1024
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02).astype(np.float32)
+    wb = pkg.synth.f32_to_bf16_bits(w)
+    x = rng.standard_normal(cols, dtype=np.float32)
+    d_w = torch.from_numpy(wb.view(np.int16)).cuda()
+    d_q = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
+    d_s = torch.empty((rows, cols // 128), dtype=torch.float32, device="cuda")
+    d_x = torch.from_numpy(x).cuda()
+    d_y, d_yb = torch.empty(rows, device="cuda"), torch.empty(rows, device="cuda")
+    abi.quantize_q8(d_w.data_ptr(), d_q.data_ptr(), d_s.data_ptr(), rows, cols)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > L2 between timed calls
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ms = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms += e0.elapsed_time(e1)
+        return ms / args.steps
+
+    q_ms = timed(lambda: abi.gemv_q8(d_q.data_ptr(), d_s.data_ptr(), d_x.data_ptr(), d_y.data_ptr(), rows, cols))
+    b_ms = timed(lambda: abi.gemv_bf16(d_w.data_ptr(), d_x.data_ptr(), d_yb.data_ptr(), rows, cols))
+    q_bytes = rows * cols + rows * (cols // 128) * 4 + cols * 4 + rows * 4
+    b_bytes = rows * cols * 2 + cols * 4 + rows * 4
+    peak, src = measured_peaks()
+    q, sc = d_q.cpu().numpy(), d_s.cpu().numpy()
+    t0 = time.perf_counter()
+    want = bindings.q8_gemv(q, sc, x)
+    cpu_s = time.perf_counter() - t0
+    got = d_y.cpu().numpy().astype(np.float64)
+    rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    exact = w.astype(np.float64) @ x.astype(np.float64)
+    qerr = float(np.linalg.norm(got - exact) / np.linalg.norm(exact))
+    gbs = q_bytes / (q_ms * 1e6)
+    line = _op_line(args, "int8 GEMV calls/s", 1000.0 / q_ms, "calls/s",
+                    {"workload": "lm_head-shaped int8 GEMV (151936 x 1024), group-128 scales",
+                     "l2": "flushed between timed calls (256 MB write)"},
+                    {"ms_per_step": round(q_ms, 5),
+                     "roofline": {"bound": "hbm", "kernel": "k_gemv_q8", "achieved": round(gbs, 1), "peak": peak,
+                                  "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": src, "traffic": None,
+                                  "bytes_per_step": q_bytes},
+                     "bf16_gemv": {"ms": round(b_ms, 5), "gbs": round(b_bytes / (b_ms * 1e6), 1),
+                                   "speedup_of_int8": round(b_ms / q_ms, 3)},
+                     "e2e": None, "gpu_launches": args.steps, "rel_l2_vs_format": rel,
+                     "rel_l2_vs_bf16_weights": qerr,
+                     "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "calls/s", "cores": 1, "kind": "port",
+                                      "sample": "oracle.q8_gemv (numpy, float64) of one call"}})
+    emit(line)
+    return 0
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -840,7 +912,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("decode", "prefill", "gdn-op", "attn-op"), default=None,
+    ap.add_argument("--workload", choices=("decode", "prefill", "gdn-op", "attn-op", "q8-gemv"), default=None,
                     help="default: decode on one GPU, prefill (tensor parallel) under torchrun")
     ap.add_argument("--seq-len", type=int, default=PREFILL_T, help="prefill workload: prompt length")
     ap.add_argument("--model", default=None, help="prefill workload: synthetic shape name")
@@ -858,6 +930,8 @@ def main():
         return run_gdn_op(args)
     if args.workload == "attn-op":
         return run_attn_op(args)
+    if args.workload == "q8-gemv":
+        return run_q8_gemv(args)
     return run_ours(args)
 
 

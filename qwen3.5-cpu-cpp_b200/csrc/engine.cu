@@ -1142,6 +1142,7 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
         {(void**)&h->n_prompt, 16},
         {(void**)&h->argmax, 16},
         {(void**)&h->dev_err, 16},
+        {(void**)&h->tp_vote, 16},
         // grid-barrier counters on their own 4 KB lines, away from the other counters
         {(void**)&h->step_bar, 4096},
         {(void**)&h->step_done, 4096},

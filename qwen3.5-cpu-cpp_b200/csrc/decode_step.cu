@@ -191,22 +191,33 @@ __device__ __noinline__ void producer(StepShared& S, const StepParams sp, int c,
 
 // Grid barrier: all CTAs finished phase p-1 (acquire of the arrival counter, which every
 // CTA bumps with a release after its CTA barrier). Leaves S.abort CTA-uniform.
+//
+// The poll is the critical path of every phase, so each iteration is one acquire load of
+// the counter and nothing else: the error word is read once, issued together with the
+// first poll (its value is only needed after the wait), and again every 16 iterations of
+// a long wait. An error posted while this barrier is pending stops the CTA at the next one.
 __device__ __noinline__ void grid_wait(StepShared& S, const StepParams sp, int p, int c, int nc) {
     const int tid = threadIdx.x;
-    if (tid == 0 && p > 0) {
-        const unsigned long long target = (unsigned long long)p * nc;
-        if (ld_acquire_u64(sp.bar) < target) {
-            const unsigned long long t0 = globaltimer_ns();
-            while (ld_acquire_u64(sp.bar) < target) {
-                if (step_aborted(sp)) break;
-                if (globaltimer_ns() - t0 > step_wait_ns(sp)) {
-                    post_error(sp.dev_err, DEV_STEP_BARRIER_TIMEOUT);
-                    break;
+    if (tid == 0) {
+        const int err0 = *reinterpret_cast<const volatile int*>(sp.dev_err);  // in flight with the poll
+        int ab = 0;
+        if (p > 0) {
+            const unsigned long long target = (unsigned long long)p * nc;
+            if (ld_acquire_u64(sp.bar) < target) {
+                const unsigned long long t0 = globaltimer_ns();
+                for (unsigned it = 1; ld_acquire_u64(sp.bar) < target; ++it) {
+                    if ((it & 15u) != 0) continue;
+                    if (step_aborted(sp)) { ab = 1; break; }
+                    if (globaltimer_ns() - t0 > step_wait_ns(sp)) {
+                        post_error(sp.dev_err, DEV_STEP_BARRIER_TIMEOUT);
+                        ab = 1;
+                        break;
+                    }
                 }
             }
         }
+        S.abort = (ab || err0 != 0) ? 1 : 0;
     }
-    if (tid == 0) S.abort = step_aborted(sp) ? 1 : 0;
     cta_sync();
     trace_mark(sp, c, p, 1);
 }
@@ -731,17 +742,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1) k_decode_step(const StepPara
     if (tid >= kSThreads) {
         producer(S, sp, c, nc);
     } else {
-        StepPhase* ph = reinterpret_cast<StepPhase*>(smem + plan.phase);
+        // The descriptor of phase p+1 is loaded into registers (one int4 per thread) while
+        // phase p runs and stored to shared memory after it, so no CTA -- in particular not
+        // the last one to arrive at a barrier -- waits for a descriptor load between phases.
+        constexpr int kDesc16 = (int)(sizeof(StepPhase) / 16);
+        static_assert(sizeof(StepPhase) % 16 == 0 && kDesc16 <= kSThreads, "descriptor staging");
+        int4* ph16 = reinterpret_cast<int4*>(smem + plan.phase);
+        const int4* desc = reinterpret_cast<const int4*>(sp.phases);
+        if (tid < kDesc16) ph16[tid] = desc[tid];
         for (int p = 0; p < sp.nphases; ++p) {
             trace_mark(sp, c, p, 0);
-            // stage this phase's descriptor (the previous phase ended with a CTA barrier)
-            {
-                const int4* src = reinterpret_cast<const int4*>(sp.phases + p);
-                int4* dst = reinterpret_cast<int4*>(ph);
-                for (int q = tid; q < (int)(sizeof(StepPhase) / 16); q += kSThreads) dst[q] = src[q];
-            }
-            cta_sync();
-            const int type = ph->type;
+            int4 next_desc = make_int4(0, 0, 0, 0);
+            if (tid < kDesc16 && p + 1 < sp.nphases) next_desc = desc[(size_t)(p + 1) * kDesc16 + tid];
+            cta_sync();  // this phase's descriptor is in shared memory
+            const int type = reinterpret_cast<const StepPhase*>(ph16)->type;
             if (type == PH_GDN) {
                 gdn_phase(S, sp, p, c, nc);
             } else if (type == PH_ATTN) {
@@ -756,6 +770,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) k_decode_step(const StepPara
             // wait then runs out and the step ends with an error, see qwc_check_step_timeout)
             if (p + 1 < sp.nphases && tid == 0 && !(p == 0 && c == sp.stall_cta))
                 red_release_add_u64(sp.bar, 1ull);  // orders this CTA's writes before it
+            if (tid < kDesc16 && p + 1 < sp.nphases) ph16[tid] = next_desc;
         }
     }
     __syncthreads();

@@ -127,6 +127,8 @@ struct qwc_handle {
     // as bf16 pairs, for the positions of one batched pass
     uint16_t* pf_kvs = nullptr;
     size_t pf_kvs_bytes = 0;
+    float* pf_fa_part = nullptr;  // key-split partials of the prefill attention (O, then m / l)
+    size_t pf_fa_part_bytes = 0;
 
     // tensor parallelism: this handle holds `shard` of a tp_world-rank group; the working
     // sizes above (KH, VH, KD, VD, C, NQ, NKV, I) are the shard's, g_* the whole model's
@@ -136,11 +138,12 @@ struct qwc_handle {
     ncclComm_t nccl = nullptr;       // non-blocking communicator (calls are settled, waits bounded)
     int tp_timeout_ms = 300000;      // bound on every wait for the group (env QWC_TP_TIMEOUT_MS)
     bool nccl_aborted = false;       // the communicator was aborted: the handle refuses work
-    // QWC_PF_TIMING=1: per batched pass, the device time of the whole pass and of the
-    // all-reduces (event pairs around each, from a pool reused across passes) on stderr
+    // QWC_PF_TIMING=1: per batched pass, the device time of the whole pass and of its
+    // parts by category (event pairs from a pool reused across passes) on stderr
     bool pf_timing = false;
-    std::vector<cudaEvent_t> pf_ev;
+    std::vector<cudaEvent_t> pf_ev;  // [0] [1]: the pass; then one pair per timed part
     size_t pf_ev_used = 0;
+    std::vector<int> pf_pair_cat;    // category of each pair
     float* pf_part = nullptr;  // prefill: [chunk][H] partial sums to all-reduce
 
     cudaGraphExec_t graph = nullptr;
@@ -898,6 +901,7 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     for (cudaEvent_t e : h->pf_ev) cudaEventDestroy(e);
     cudaFree(h->pf_ws);
     cudaFree(h->pf_kvs);
+    cudaFree(h->pf_fa_part);
     if (h->nccl) {
         // a communicator whose group is incomplete would block ncclCommDestroy: abort it
         ncclResult_t st = ncclSuccess;
@@ -1439,6 +1443,11 @@ static int stream_wait(qwc_handle* h, const char* who) {
     }
 }
 
+// Parts of a batched pass timed under QWC_PF_TIMING.
+enum PfCat { PF_CAT_ALLREDUCE, PF_CAT_GDN, PF_CAT_GDN_STATE, PF_CAT_ATTN, PF_CAT_GEMM, PF_NCAT };
+static const char* const kPfCatName[PF_NCAT] = {"all-reduce + add", "gdn mixer (all kernels)", "gdn state pass",
+                                                "attention", "projections (tc_gemm)"};
+
 // next event of the timing pool (QWC_PF_TIMING)
 static cudaEvent_t pf_event(qwc_handle* h) {
     if (h->pf_ev_used == h->pf_ev.size()) {
@@ -1448,17 +1457,36 @@ static cudaEvent_t pf_event(qwc_handle* h) {
     }
     return h->pf_ev[h->pf_ev_used++];
 }
-// events 0 / 1: the pass; then pairs around each all-reduce (+ the residual add)
+// A timed part: two consecutive events of the pool, recorded by the caller.
+struct PfPair {
+    cudaEvent_t b = nullptr, e = nullptr;
+};
+static PfPair pf_pair(qwc_handle* h, int cat) {
+    PfPair pr;
+    if (!h->pf_timing) return pr;
+    pr.b = pf_event(h);
+    pr.e = pf_event(h);
+    h->pf_pair_cat.push_back(cat);
+    return pr;
+}
+static void pf_rec(qwc_handle* h, cudaEvent_t e) {
+    if (e) cudaEventRecord(e, h->stream);
+}
+// events 0 / 1: the pass; then the pairs, summed by category
 static void pf_timing_report(qwc_handle* h, int T) {
     if (!h->pf_timing || h->pf_ev_used < 2) return;
-    float total = 0.f, ar = 0.f, t = 0.f;
-    cudaEventElapsedTime(&total, h->pf_ev[0], h->pf_ev[h->pf_ev_used - 1]);
-    for (size_t i = 1; i + 2 < h->pf_ev_used; i += 2) {
-        cudaEventElapsedTime(&t, h->pf_ev[i], h->pf_ev[i + 1]);
-        ar += t;
+    float total = 0.f, t = 0.f, cat[PF_NCAT] = {};
+    int calls[PF_NCAT] = {};
+    cudaEventElapsedTime(&total, h->pf_ev[0], h->pf_ev[1]);
+    for (size_t k = 0; k < h->pf_pair_cat.size(); ++k) {
+        if (cudaEventElapsedTime(&t, h->pf_ev[2 + 2 * k], h->pf_ev[3 + 2 * k]) != cudaSuccess) continue;
+        cat[h->pf_pair_cat[k]] += t;
+        ++calls[h->pf_pair_cat[k]];
     }
-    std::fprintf(stderr, "[qwc] prefill T=%d rank %d/%d: %.3f ms device, all-reduce + add %.3f ms (%zu calls)\n", T,
-                 h->tp_rank, h->tp_world, total, ar, (h->pf_ev_used - 2) / 2);
+    std::fprintf(stderr, "[qwc] prefill T=%d rank %d/%d: %.3f ms device", T, h->tp_rank, h->tp_world, total);
+    for (int c = 0; c < PF_NCAT; ++c)
+        if (calls[c]) std::fprintf(stderr, "; %s %.3f ms (%d)", kPfCatName[c], cat[c], calls[c]);
+    std::fprintf(stderr, "\n");
 }
 
 static int pf_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t* xs, long ldxs, int M, int N, int K,
@@ -1469,7 +1497,10 @@ static int pf_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t* xs, lon
     p.N = N;
     p.K = K;
     p.err = h->dev_err;
+    const PfPair pr = pf_pair(h, PF_CAT_GEMM);
+    pf_rec(h, pr.b);
     CU(launch_tc_gemm(mw, mx, p, h->stream));
+    pf_rec(h, pr.e);
     return QWC_OK;
 }
 
@@ -1488,12 +1519,13 @@ static int pf_residual_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t
     g.y = h->pf_part;
     int rc = pf_gemm(h, mw, xs, ldxs, h->H, Tc, K, g);
     if (rc) return rc;
-    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
+    const PfPair ar = pf_pair(h, PF_CAT_ALLREDUCE);
+    pf_rec(h, ar.b);
     rc = nccl_settle(h, ncclAllReduce(h->pf_part, h->pf_part, (size_t)Tc * h->H, ncclFloat32, ncclSum, h->nccl, h->stream),
                      "ncclAllReduce");
     if (rc) return rc;
     CU(pf_add(h->pf_hid, h->pf_part, (size_t)Tc * h->H, h->stream));
-    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
+    pf_rec(h, ar.e);
     return QWC_OK;
 }
 
@@ -1513,7 +1545,12 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
     if (rc) return rc;
     const int H = h->H;
     h->pf_ev_used = 0;
-    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
+    h->pf_pair_cat.clear();
+    if (h->pf_timing) {
+        pf_event(h);  // [0] start, [1] end of the pass
+        pf_event(h);
+        CU(cudaEventRecord(h->pf_ev[0], h->stream));
+    }
     const size_t kv_layer = (size_t)2 * h->NKV * sv.max_ctx * h->HD * h->kv_bytes;
     // tensor-core attention operands for positions [0, p0 + T): K and V^T pairs per layer
     const bool attn_tc = pf_attn_tc() && h->HD == 256 && h->n_attn > 0;
@@ -1530,6 +1567,23 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
         h->pf_kvs_bytes = kvs_layer * 2 * h->n_attn;
         // every entry holds a finite value: positions past the prompt meet zero weights
         CU(cudaMemsetAsync(h->pf_kvs, 0, h->pf_kvs_bytes, h->stream));
+    }
+    // key-split partials: the most splits any chunk of this pass uses (more for later chunks)
+    int fa_splits = 1;
+    if (attn_tc)
+        for (int c0 = 0; c0 < T; c0 += chunk)
+            fa_splits = std::max(fa_splits, pf_fattn_splits(std::min(chunk, T - c0), p0 + c0, h->NQ, h->NKV));
+    const size_t fa_rows = (size_t)std::min(T, chunk) * h->NQ;
+    const size_t fa_bytes = fa_splits > 1 ? (size_t)fa_splits * fa_rows * (h->HD + 2) * 4 : 0;
+    if (fa_bytes > h->pf_fa_part_bytes) {
+        cudaFree(h->pf_fa_part);
+        h->pf_fa_part = nullptr;
+        h->pf_fa_part_bytes = 0;
+        if (cudaMalloc(&h->pf_fa_part, fa_bytes) != cudaSuccess) {
+            h->pf_fa_part = nullptr;
+            return fail(h, QWC_E_OOM, "prefill attention split workspace allocation failed");
+        }
+        h->pf_fa_part_bytes = fa_bytes;
     }
     for (int c0 = 0; c0 < T; c0 += chunk) {
         const int Tc = std::min(chunk, T - c0), pc = p0 + c0;
@@ -1573,13 +1627,19 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 a.xs = h->pf_xa;
                 a.ldxs = h->pf_lda;
                 if (attn_tc) {
+                    a.part_o = h->pf_fa_part;
+                    a.part_ml = h->pf_fa_part ? h->pf_fa_part + (size_t)fa_splits * fa_rows * h->HD : nullptr;
+                    a.part_splits = fa_splits;
                     a.ksplit = h->pf_kvs + kvs_layer * lw.idx;
                     a.vt = a.ksplit + kvs_layer / 2;
                     a.vsplit = h->pf_vsplit;
                     a.ctx_pad = ctx_pad;
                     a.err = h->dev_err;
                 }
+                const PfPair pa = pf_pair(h, PF_CAT_ATTN);
+                pf_rec(h, pa.b);
                 CU(pf_attention(a, h->stream));
+                pf_rec(h, pa.e);
             } else {
                 PfGdnArgs g;
                 g.proj = h->pf_proj;
@@ -1613,9 +1673,14 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
                 g.VH = h->VH;
                 g.C = h->C;
                 g.VD = h->VD;
+                const PfPair pg = pf_pair(h, PF_CAT_GDN), ps = pf_pair(h, PF_CAT_GDN_STATE);
+                g.ev_state0 = ps.b;
+                g.ev_state1 = ps.e;
+                pf_rec(h, pg.b);
                 CU(pf_gdn(g, h->stream));
                 CU(pf_gated_norm_split(h->pf_o, h->VD, h->pf_proj + h->C, h->pf_ldp, lw.gn_w, Tc, h->VH, h->eps,
                                        h->pf_xa, h->pf_lda, h->stream));
+                pf_rec(h, pg.e);
             }
             if ((rc = pf_residual_gemm(h, h->pf_map_out[l], h->pf_xa, h->pf_lda, Tc, lw.out_in))) return rc;
             // FFN: post-attention norm, gate/up + SwiGLU (written as hi/lo for down), down + residual
@@ -1647,7 +1712,7 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
             CU(cudaMemcpyAsync(dst, h->pf_logits, (size_t)gn * h->V * 4, cudaMemcpyDeviceToHost, h->stream));
         }
     }
-    if (h->pf_timing) CU(cudaEventRecord(pf_event(h), h->stream));
+    if (h->pf_timing) CU(cudaEventRecord(h->pf_ev[1], h->stream));
     if ((rc = stream_wait(h, "prefill"))) return rc;
     pf_timing_report(h, T);
     return check_device_error(h);

@@ -27,11 +27,25 @@
 // K and V reach this kernel as bf16 pairs written by the attention prep kernel: K split
 // row-major [kv][pos][hi 256 | lo 256], V split and transposed [kv][hi|lo][256 dims][pos],
 // so that every shared-memory operand is K-major. Every wait is bounded.
+//
+// Key splits. One CTA per (kv head, query block) gives NKV * T / (128 / GRP) CTAs: 256 for
+// a 4096-token chunk of the 2B shape on one GPU, but 32 on each rank of an 8-way tensor-
+// parallel group (one q head per rank), where a long context then runs on a fifth of the
+// SMs. The grid's third dimension therefore splits each CTA's key blocks into `nsplit`
+// contiguous ranges; a split CTA leaves its unnormalised O, running max m (log2 units)
+// and sum l per row in a workspace, and k_pf_fattn_combine merges the splits of a row,
+//   M = max_s m_s,  O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s,
+// before the gate and the bf16-pair split (the split-K combine of the decode attention).
+// Rotated key order (each CTA starting at a different block, to spread L2 reads of a
+// short context) is used only while the layer's K / V operands fit in L2; over a long
+// context every CTA of a kv head walks the same blocks in the same order, so each block
+// is read from HBM once and served from L2 to the others.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_util.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace qwc {
 namespace {
@@ -49,6 +63,8 @@ constexpr uint32_t kIdescS =
 constexpr uint32_t kIdescO =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kHD >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kFattnWaves = 2, kFattnMinBlocks = 32;
+constexpr size_t kFattnRotateBytes = 48ull << 20;
 static_assert(kSmem <= 232448, "shared memory of the attention CTA");
 
 using namespace tc;
@@ -60,8 +76,18 @@ struct FAParams {
     uint16_t* xs;        // output [T][ldxs], K = NQ*HD, hi/lo
     long ldxs;
     int T, p0, NQ, NKV, grp, ctx_pad;
+    int nsplit, rotate;  // key ranges per query block; rotated key order (short contexts)
+    float* part_o;       // nsplit > 1: [nsplit][T][NQ][HD] unnormalised O
+    float* part_ml;      //             [nsplit][T][NQ][2] running max (log2 units), sum
     int* err;
 };
+
+// Key blocks [lo, hi) of split `s` of a query block whose causal range has nkb blocks.
+__host__ __device__ inline void fattn_split_range(int nkb, int nsplit, int s, int& lo, int& hi) {
+    const int len = (nkb + nsplit - 1) / nsplit;
+    lo = s * len;
+    hi = lo + len < nkb ? lo + len : nkb;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     k_pf_fattn(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapVt, const FAParams p) {
@@ -86,12 +112,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qb = gridDim.y - 1 - blockIdx.y;  // longest causal rows first
     const int bqt = kM / p.grp;                 // tokens per CTA
     const int t_last = min((qb + 1) * bqt, p.T) - 1;
-    const int nkb = (p.p0 + t_last) / kN + 1;  // causal: key blocks up to the last query
-    // Each CTA walks its key blocks from a different start (the online softmax does not
-    // depend on the order), so that the CTAs of a kv head do not all read the same block
-    // from L2 at the same time.
-    const int rot = (qb * 13 + kv * 7) % nkb;
-    auto blk = [&](int kb) { return kb + rot < nkb ? kb + rot : kb + rot - nkb; };
+    const int nkb_all = (p.p0 + t_last) / kN + 1;  // causal: key blocks up to the last query
+    int kb_lo, kb_hi;
+    fattn_split_range(nkb_all, p.nsplit, blockIdx.z, kb_lo, kb_hi);
+    const int nkb = kb_hi - kb_lo;
+    if (nkb <= 0) return;  // an empty split (short causal range): the combine skips it
+    // Short contexts: each CTA walks its key blocks from a different start (the online
+    // softmax does not depend on the order), so that the CTAs of a kv head do not all
+    // read the same block from L2 at the same time. Long contexts: the same order for all.
+    const int rot = p.rotate ? (qb * 13 + kv * 7) % nkb : 0;
+    auto blk = [&](int kb) { return kb_lo + (kb + rot < nkb ? kb + rot : kb + rot - nkb); };
 
     if (threadIdx.x == 0) {
         mbar_init(k_full, 1);
@@ -334,7 +364,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, ok && !aborted());
             if (!ok && lane == 0) give_up(DEV_TC_EPI_TIMEOUT);
         }
-        if (ok) {
+        if (ok && p.nsplit > 1) {
+            // partial of this key range: unnormalised O, m, l (combined by k_pf_fattn_combine)
+            fence_after();
+            const size_t prow = ((size_t)blockIdx.z * p.T + (valid ? ti : 0)) * p.NQ + h;
+            float* po = p.part_o + prow * kHD;
+#pragma unroll 1
+            for (int c = 0; c < kHD / 16; ++c) {
+                uint32_t o[16];
+                ld16_nowait(trow + kColO + c * 16, o);
+                ld_wait();
+                if (valid) {
+                    float4* d4 = reinterpret_cast<float4*>(po + c * 16);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        d4[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                            __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+                }
+            }
+            if (valid) *reinterpret_cast<float2*>(p.part_ml + prow * 2) = make_float2(m, l);
+        } else if (ok) {
             fence_after();
             const int K = p.NQ * kHD;
             uint16_t* row = p.xs + (size_t)(valid ? ti : 0) * p.ldxs;
@@ -369,6 +418,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
+}
+
+// Merges the key-range partials of each (token, q head) row: one warp per row, lane l
+// holding dims 8l..8l+7; then O / l * sigmoid(gate) as the bf16 pair o_proj reads.
+__global__ void __launch_bounds__(256) k_pf_fattn_combine(const FAParams p) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= p.T * p.NQ) return;
+    const int ti = row / p.NQ, h = row % p.NQ;
+    const int bqt = kM / p.grp, qb = ti / bqt;
+    const int t_last = min((qb + 1) * bqt, p.T) - 1;
+    const int nkb_all = (p.p0 + t_last) / kN + 1;
+    float M = -INFINITY;
+    int ns = 0;
+    for (int s2 = 0; s2 < p.nsplit; ++s2) {
+        int lo, hi;
+        fattn_split_range(nkb_all, p.nsplit, s2, lo, hi);
+        if (lo >= hi) break;
+        M = fmaxf(M, p.part_ml[(((size_t)s2 * p.T + ti) * p.NQ + h) * 2]);
+        ++ns;
+    }
+    float L = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s2 = 0; s2 < ns; ++s2) {
+        const size_t prow = ((size_t)s2 * p.T + ti) * p.NQ + h;
+        const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + prow * 2);
+        if (ml.x == -INFINITY) continue;  // every key of this range is after the query
+        const float f = exp2f(ml.x - M);
+        L += ml.y * f;
+        const float4* po = reinterpret_cast<const float4*>(p.part_o + prow * kHD + lane * 8);
+        const float4 a = po[0], b = po[1];
+        o[0] += a.x * f; o[1] += a.y * f; o[2] += a.z * f; o[3] += a.w * f;
+        o[4] += b.x * f; o[5] += b.y * f; o[6] += b.z * f; o[7] += b.w * f;
+    }
+    const float inv_l = 1.0f / L;
+    const float* gate = p.proj + (size_t)ti * p.ldp + (size_t)h * 2 * kHD + kHD + lane * 8;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        const float x0 = o[e] * inv_l * sigmoid_f(gate[e]);
+        const float x1 = o[e + 1] * inv_l * sigmoid_f(gate[e + 1]);
+        split2(x0, x1, hw[e / 2], lw[e / 2]);
+    }
+    const int K = p.NQ * kHD;
+    uint16_t* xrow = p.xs + (size_t)ti * p.ldxs;
+    *reinterpret_cast<uint4*>(xrow + h * kHD + lane * 8) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(xrow + K + h * kHD + lane * 8) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
 // V split rows [kv][pos][hi 256 | lo 256] (positions p0..p0+T-1) -> transposed
@@ -419,9 +513,37 @@ cudaError_t pf_fattn(const PfFattnArgs& a, cudaStream_t s) {
     p.grp = grp;
     p.ctx_pad = a.ctx_pad;
     p.err = a.err;
-    dim3 grid(a.NKV, (a.T + (kM / grp) - 1) / (kM / grp));
+    p.nsplit = pf_fattn_splits(a.T, a.p0, a.NQ, a.NKV);
+    p.part_o = a.part_o;
+    p.part_ml = a.part_ml;
+    if (p.nsplit > 1 && (!a.part_o || !a.part_ml || a.part_splits < p.nsplit)) return cudaErrorInvalidValue;
+    // K and V pairs of the layer: NKV * ctx_pad * (1 KB + 1 KB)
+    p.rotate = (size_t)a.NKV * a.ctx_pad * 2048 <= kFattnRotateBytes ? 1 : 0;
+    dim3 grid(a.NKV, (a.T + (kM / grp) - 1) / (kM / grp), p.nsplit);
     k_pf_fattn<<<grid, kThreads, kSmem, s>>>(mk, mv, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || p.nsplit == 1) return e;
+    k_pf_fattn_combine<<<(a.T * a.NQ + 7) / 8, 256, 0, s>>>(p);
     return cudaGetLastError();
+}
+
+// Key splits of one launch. A launch with at least one CTA per SM is not split (measured:
+// splitting the 256 CTAs of a one-GPU 2B chunk made the 131072-token pass 0.8 % slower);
+// one with fewer (a tensor-parallel rank's few q heads) gets enough splits for about
+// kFattnWaves waves, each split at least kFattnMinBlocks key blocks (the query load and
+// the epilogue amortised), at most kFattnMaxSplits. QWC_FATTN_SPLITS=n forces n.
+int pf_fattn_splits(int T, int p0, int NQ, int NKV) {
+    const char* env = std::getenv("QWC_FATTN_SPLITS");  // read per call, like the other prefill switches
+    const int forced = env ? std::max(0, std::atoi(env)) : 0;
+    if (T <= 0 || NKV <= 0 || NQ % NKV) return 1;
+    const int grp = NQ / NKV, bqt = kM / grp;
+    const int base = NKV * ((T + bqt - 1) / bqt);
+    const int nkb_max = (p0 + T - 1) / kN + 1;
+    if (forced > 0) return std::min(forced, kFattnMaxSplits);
+    if (base >= num_sms()) return 1;
+    int n = (kFattnWaves * num_sms() + base - 1) / base;
+    n = std::min(n, std::max(1, nkb_max / kFattnMinBlocks));
+    return std::max(1, std::min(n, kFattnMaxSplits));
 }
 
 }  // namespace qwc

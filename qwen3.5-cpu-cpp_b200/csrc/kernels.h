@@ -213,6 +213,7 @@ struct PfGdnArgs {
     uint16_t* ST = nullptr;       // scratch [VH][ceil(T/64)][2][128][128] bf16 pairs
     uint16_t* ET = nullptr;       // scratch [VH][ceil(T/64)][2][128][64] bf16 pairs
     int* err = nullptr;           // device error word of the tensor-core kernel
+    cudaEvent_t ev_state0 = nullptr, ev_state1 = nullptr;  // optional: recorded around the state pass
     float* state = nullptr;       // [VH][DK][DV], read then updated
     float* out = nullptr;         // [T][VD]
     int T = 0, p0 = 0, KH = 0, VH = 0, C = 0, VD = 0;
@@ -243,6 +244,9 @@ struct PfAttnArgs {
     uint16_t* vt = nullptr;
     uint16_t* vsplit = nullptr;
     int ctx_pad = 0;
+    float* part_o = nullptr;      // key-split partials of the tensor-core attention
+    float* part_ml = nullptr;
+    int part_splits = 0;
     int* err = nullptr;
 };
 cudaError_t pf_attention(const PfAttnArgs& a, cudaStream_t s);
@@ -256,9 +260,16 @@ struct PfFattnArgs {
     uint16_t* vt = nullptr;
     const uint16_t* vsplit = nullptr;
     int T = 0, p0 = 0, NQ = 0, NKV = 0, ctx_pad = 0;
+    // key-split partials (pf_fattn_splits(...) > 1): [splits][T][NQ][HD] and [splits][T][NQ][2]
+    float* part_o = nullptr;
+    float* part_ml = nullptr;
+    int part_splits = 0;
     int* err = nullptr;
 };
 cudaError_t pf_fattn(const PfFattnArgs& a, cudaStream_t s);
+// Key splits pf_fattn uses for a chunk of T queries at positions p0.. (grows with p0).
+int pf_fattn_splits(int T, int p0, int NQ, int NKV);
+constexpr int kFattnMaxSplits = 16;
 cudaError_t pf_add(float* y, const float* x, size_t n, cudaStream_t s);  // y += x (16-byte aligned)
 
 // Records a handle-less failure message (what qwc_last_error(NULL) returns).

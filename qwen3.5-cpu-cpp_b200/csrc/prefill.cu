@@ -1112,7 +1112,9 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
         tc_make_map_box(&mET, a.ET, pl * 128, kGC, kGC, 128) || tc_make_map_box(&mP, a.P, pl * kGC, kGC, kGC, 64))
         return cudaErrorInvalidValue;
     k_pf_gdn_chunk_a_tc<<<dim3(nch, a.VH), 128, kGdnATcSmem, s>>>(ck, a.err);
+    if (a.ev_state0) cudaEventRecord(a.ev_state0, s);
     k_pf_gdn_state<<<a.VH * (128 / kGS1), 256, kGdnB1Smem, s>>>(ck);
+    if (a.ev_state1) cudaEventRecord(a.ev_state1, s);
     k_pf_gdn_out_tc<<<dim3(nch, a.VH), 128, kGdnOutSmem, s>>>(mST, mQG, mET, mP, ck, a.err);
     return cudaGetLastError();
 }
@@ -1193,6 +1195,9 @@ cudaError_t pf_attention(const PfAttnArgs& a, cudaStream_t s) {
         f.NQ = a.NQ;
         f.NKV = a.NKV;
         f.ctx_pad = a.ctx_pad;
+        f.part_o = a.part_o;
+        f.part_ml = a.part_ml;
+        f.part_splits = a.part_splits;
         f.err = a.err;
         return pf_fattn(f, s);
     }

@@ -127,6 +127,47 @@ def test_tensor_core_attention_matches_simt_and_oracle(pkg, oracle, chunk, attn_
     assert (got.argmax(1) == simt.argmax(1)).mean() > 0.99
 
 
+@pytest.fixture
+def fattn_splits():
+    """Force the number of key ranges each query block of the tcgen05 attention is split
+    into (QWC_FATTN_SPLITS, read per call); restores the environment afterwards."""
+    old = os.environ.get("QWC_FATTN_SPLITS")
+
+    def use(n):
+        os.environ["QWC_FATTN_SPLITS"] = str(n)
+
+    yield use
+    if old is None:
+        os.environ.pop("QWC_FATTN_SPLITS", None)
+    else:
+        os.environ["QWC_FATTN_SPLITS"] = old
+
+
+@pytest.mark.parametrize("chunk", [128, 4096], indirect=True)
+@pytest.mark.parametrize("shape,T", [("tiny", 333), ("tiny-rep", 64), ("small-0.8b-widths", 203)])
+def test_tensor_core_attention_key_splits_match_unsplit_and_oracle(pkg, oracle, chunk, fattn_splits, shape, T):
+    """Key-range splits of the tcgen05 attention (partials of O, m, l per range merged by
+    the combine kernel): 2 and 3 ranges, and 16 -- more ranges than a short causal range
+    has key blocks, so some splits are empty and some rows see only masked keys in a
+    range -- against the unsplit kernel and the oracle."""
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=37)
+    last = s.vocab_size > 4096
+    m = pkg.abi.Model(d, max_context=T + 8)
+    fattn_splits(1)
+    base = m.forward_logits(ids, last_only=last).reshape(-1, s.vocab_size)
+    want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=last).reshape(-1, s.vocab_size)
+    for n in (2, 3, 16):
+        fattn_splits(n)
+        got = m.forward_logits(ids, last_only=last).reshape(-1, s.vocab_size)
+        for i in range(got.shape[0]):
+            assert rel_l2(got[i], base[i]) < 1e-4, (n, i)
+            assert rel_l2(got[i], want[i]) < LOGIT_TOL, (n, i)
+        assert (got.argmax(1) == base.argmax(1)).mean() > 0.99
+    m.close()
+
+
 @pytest.mark.parametrize("chunk", [96, 4096], indirect=True)
 @pytest.mark.parametrize("shape,T", [("tiny", 200), ("small-0.8b-widths", 150)])
 def test_per_layer_hidden_states_match_oracle(pkg, oracle, chunk, shape, T):

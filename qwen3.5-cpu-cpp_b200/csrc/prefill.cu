@@ -14,6 +14,8 @@
 #include "tc_util.cuh"
 #include "kernels.h"
 
+#include <cstdlib>
+
 namespace qwc {
 
 constexpr int kPT = 256;  // threads of the token-parallel kernels
@@ -491,34 +493,47 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
 }
 
 // Kernel B1: the state recurrence across chunks, S_{c+1} = gamma_C S_c + Kd^T (U - W S_c).
-// Columns of S evolve independently, so each CTA owns a (value head, 16-column slice) and
+// Columns of S evolve independently, so each CTA owns a (value head, WS-column slice) and
 // walks the chunks in order; the next chunk's W, Kd and U slice are fetched (cp.async)
 // while the current one is applied. For the output kernel B2 it writes the state entering
 // every chunk and E = U - W S_c, both transposed (value dims as rows) as bf16 pairs; then
 // the final state.
-constexpr int kGS1 = 16;             // columns of S per CTA
-constexpr int kGS1P = kGS1 + 4;      // padded stride of [.][16] tiles
+//
+// The walk is sequential, so a launch takes (chunks x per-chunk time) however few CTAs
+// it has. The arithmetic per chunk is proportional to WS and the fetch is not: with many
+// value heads (one GPU) 16-column slices fill the SMs; a tensor-parallel rank holds VH / N
+// heads, and narrower slices (8, 4 columns) give it as many CTAs and a shorter chunk step.
 constexpr int kWtP = kGC + 4;         // padded stride of the W^T rows
-constexpr int kB1Buf = 128 * kWtP + kGC * kGP + kGC * kGS1P;  // floats per chunk buffer: W^T, Kd, U slice
-constexpr size_t kGdnB1Smem = (size_t)(2 * kB1Buf + 128 * kGS1P + kGC * kGS1P) * 4;
+template <int WS>
+struct GdnStateCfg {
+    static constexpr int P = WS + 4;                                // padded stride of [.][WS] tiles
+    static constexpr int Buf = 128 * kWtP + kGC * kGP + kGC * P;    // floats per chunk buffer: W^T, Kd, U slice
+    static constexpr size_t Smem = (size_t)(2 * Buf + 128 * P + kGC * P) * 4;
+    static constexpr int KS = 64 / WS;   // E = U - W S: lanes sharing one 4 x 4 tile (key-dim split)
+    static constexpr int KH = 32 / WS;   // S update: lanes sharing one 4 x 4 tile (token split)
+    static_assert(WS == 4 || WS == 8 || WS == 16, "state slice width");
+};
 __device__ __forceinline__ void cp16(float* dst, const float* src, bool pred) {
     const uint32_t d = smem_u32(dst);
     const int n = pred ? 16 : 0;  // 0: zero fill
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
 }
+template <int WS>
 __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
+    using C = GdnStateCfg<WS>;
+    constexpr int P = C::P, KS = C::KS, KH = C::KH, Q4 = WS / 4;
     extern __shared__ __align__(16) float sb[];
-    float* Ssm = sb + 2 * kB1Buf;        // [128][20]
-    float* Esm = Ssm + 128 * kGS1P;      // [64][20]
-    const int vh = blockIdx.x / (128 / kGS1), sl = blockIdx.x % (128 / kGS1), tid = threadIdx.x;
+    float* Ssm = sb + 2 * C::Buf;        // [128][P]
+    float* Esm = Ssm + 128 * P;          // [64][P]
+    const int vh = blockIdx.x / (128 / WS), sl = blockIdx.x % (128 / WS), tid = threadIdx.x;
     const int nch = (p.T + kGC - 1) / kGC;
-    float* Sg = p.state + (size_t)vh * 128 * 128 + sl * kGS1;
-    for (int e = tid; e < 128 * (kGS1 / 4); e += 256) {
-        const int r = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
-        *reinterpret_cast<float4*>(Ssm + r * kGS1P + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
+    float* Sg = p.state + (size_t)vh * 128 * 128 + sl * WS;
+    for (int e = tid; e < 128 * Q4; e += 256) {
+        const int r = e / Q4, c4 = (e % Q4) * 4;
+        *reinterpret_cast<float4*>(Ssm + r * P + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
     }
     auto fetch = [&](int c) {
-        float* B = sb + (c & 1) * kB1Buf;
+        float* B = sb + (c & 1) * C::Buf;
         const int t0 = c * kGC, n = min(kGC, p.T - t0);
         const size_t hrow = ((size_t)vh * p.T + t0) * 128;
         const float* wt = p.W + ((size_t)vh * nch + c) * 128 * kGC;
@@ -532,18 +547,18 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             const size_t off = hrow + (size_t)(i < n ? i : 0) * 128 + c4;
             cp16(Bk + i * kGP + c4, p.KD + off, i < n);
         }
-        for (int e = tid; e < kGC * (kGS1 / 4); e += 256) {
-            const int i = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
-            cp16(Bk + kGC * kGP + i * kGS1P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * kGS1 + c4, i < n);
+        for (int e = tid; e < kGC * Q4; e += 256) {
+            const int i = e / Q4, c4 = (e % Q4) * 4;
+            cp16(Bk + kGC * kGP + i * P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * WS + c4, i < n);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     fetch(0);
-    // E: 4 x 4 tile (rows ei.., columns ec..) over every 4th key dim (kq = lane % 4), the four
-    // partial tiles summed across lanes; state update: 4 x 4 tile (key dims sr.., columns
-    // sc..) over every 2nd token (kh = lane % 2), summed across the lane pair
-    const int kq = tid & 3, et = tid >> 2, ei = (et >> 2) * 4, ec = (et & 3) * 4;
-    const int kh = tid & 1, stl = tid >> 1, sr = (stl >> 2) * 4, sc = (stl & 3) * 4;
+    // E: 4 x 4 tile (rows ei.., columns ec..) over every KS-th key dim (kq = lane % KS), the
+    // KS partial tiles summed across lanes; state update: 4 x 4 tile (key dims sr.., columns
+    // sc..) over every KH-th token (kh = lane % KH), summed across the KH lanes
+    const int kq = tid % KS, et = tid / KS, ei = (et / Q4) * 4, ec = (et % Q4) * 4;
+    const int kh = tid % KH, stl = tid / KH, sr = (stl / Q4) * 4, sc = (stl % Q4) * 4;
     for (int c = 0; c < nch; ++c) {
         if (c + 1 < nch) {
             fetch(c + 1);
@@ -552,22 +567,20 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();  // chunk c's operands and the state are visible to every thread
-        const float* Wts = sb + (c & 1) * kB1Buf;  // W^T [128][68]
+        const float* Wts = sb + (c & 1) * C::Buf;  // W^T [128][68]
         const float* Ksm = Wts + 128 * kWtP;         // Kd [64][132]
-        const float* Usm = Ksm + kGC * kGP;          // U slice [64][20]
+        const float* Usm = Ksm + kGC * kGP;          // U slice [64][P]
         // the state entering chunk c, transposed (rows = value dims) as bf16 pairs, for the
-        // output kernel: thread -> key dim k = tid % 128 and value dims 8 (tid / 128) .. +7 of the
-        // slice (row reads of S; a warp's stores cover 32 consecutive key dims)
+        // output kernel: thread -> key dim k = tid % 128 and WS / 2 value dims from
+        // (tid / 128) WS / 2 (a warp's stores cover 32 consecutive key dims)
         {
-            const int k = tid & 127, d0 = (tid >> 7) * 8;
-            const float4 a4 = *reinterpret_cast<const float4*>(Ssm + k * kGS1P + d0);
-            const float4 b4 = *reinterpret_cast<const float4*>(Ssm + k * kGS1P + d0 + 4);
-            const float v8[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
-            uint16_t* st = p.ST + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + d0) * 128 + k;
+            constexpr int V = WS / 2;
+            const int k = tid & 127, d0 = (tid >> 7) * V;
+            uint16_t* st = p.ST + (((size_t)vh * nch + c) * 2 * 128 + sl * WS + d0) * 128 + k;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < V; ++u) {
                 uint16_t hi, lo;
-                split_bf16(v8[u], hi, lo);
+                split_bf16(Ssm[k * P + d0 + u], hi, lo);
                 st[u * 128] = hi;
                 st[128 * 128 + u * 128] = lo;
             }
@@ -580,10 +593,10 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
 #pragma unroll
                 for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
 #pragma unroll 4
-            for (int it = 0; it < 32; ++it) {
-                const int r = it * 4 + kq;
+            for (int it = 0; it < 128 / KS; ++it) {
+                const int r = it * KS + kq;
                 const float4 w4 = *reinterpret_cast<const float4*>(Wts + r * kWtP + ei);
-                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + ec);
+                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * P + ec);
                 const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
                 for (int x = 0; x < 4; ++x)
@@ -593,36 +606,36 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
 #pragma unroll
             for (int x = 0; x < 4; ++x)
 #pragma unroll
-                for (int y = 0; y < 4; ++y) {
-                    acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], 1);
-                    acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], 2);
-                }
-            // lane kq of the quad stores row ei + kq of the tile
-            const float4 u4 = *reinterpret_cast<const float4*>(Usm + (ei + kq) * kGS1P + ec);
-            float rowv[4];
+                for (int y = 0; y < 4; ++y)
 #pragma unroll
-            for (int y = 0; y < 4; ++y)
-                rowv[y] = kq == 0 ? acc[0][y] : (kq == 1 ? acc[1][y] : (kq == 2 ? acc[2][y] : acc[3][y]));
-            *reinterpret_cast<float4*>(Esm + (ei + kq) * kGS1P + ec) =
-                make_float4(u4.x - rowv[0], u4.y - rowv[1], u4.z - rowv[2], u4.w - rowv[3]);
+                    for (int o = 1; o < KS; o <<= 1) acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], o);
+            // lane kq < 4 of the group stores row ei + kq of the tile
+            if (kq < 4) {
+                const float4 u4 = *reinterpret_cast<const float4*>(Usm + (ei + kq) * P + ec);
+                float rowv[4];
+#pragma unroll
+                for (int y = 0; y < 4; ++y)
+                    rowv[y] = kq == 0 ? acc[0][y] : (kq == 1 ? acc[1][y] : (kq == 2 ? acc[2][y] : acc[3][y]));
+                *reinterpret_cast<float4*>(Esm + (ei + kq) * P + ec) =
+                    make_float4(u4.x - rowv[0], u4.y - rowv[1], u4.z - rowv[2], u4.w - rowv[3]);
+            }
         }
         __syncthreads();  // E complete; every read of S for E done
         // E^T of the slice as bf16 pairs (rows = value dims, 64 token columns; rows past the
-        // chunk's tokens are zero): thread -> token j = tid % 64 and value dims 4 (tid / 64) .. +3
+        // chunk's tokens are zero): thread -> token j = tid % 64 and WS / 4 value dims from
+        // (tid / 64) WS / 4
         {
-            const int j = tid & 63, d0 = (tid >> 6) * 4;
-            const float4 e4 = *reinterpret_cast<const float4*>(Esm + j * kGS1P + d0);
-            const float v4[4] = {e4.x, e4.y, e4.z, e4.w};
-            uint16_t* et = p.ET + (((size_t)vh * nch + c) * 2 * 128 + sl * kGS1 + d0) * kGC + j;
+            const int j = tid & 63, d0 = (tid >> 6) * Q4;
+            uint16_t* et = p.ET + (((size_t)vh * nch + c) * 2 * 128 + sl * WS + d0) * kGC + j;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < Q4; ++u) {
                 uint16_t hi, lo;
-                split_bf16(v4[u], hi, lo);
+                split_bf16(Esm[j * P + d0 + u], hi, lo);
                 et[u * kGC] = hi;
                 et[128 * kGC + u * kGC] = lo;
             }
         }
-        // S = gamma_C S + Kd^T E (each lane pair reads and writes only its own S tile here)
+        // S = gamma_C S + Kd^T E (each lane group reads and writes only its own S tile here)
         {
             const float gC = p.gC[(size_t)vh * nch + c];
             float acc[4][4];
@@ -631,10 +644,10 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
 #pragma unroll
                 for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
 #pragma unroll 4
-            for (int it = 0; it < kGC / 2; ++it) {  // rows past the chunk's tokens are zero
-                const int i = it * 2 + kh;
+            for (int it = 0; it < kGC / KH; ++it) {  // rows past the chunk's tokens are zero
+                const int i = it * KH + kh;
                 const float4 k4 = *reinterpret_cast<const float4*>(Ksm + i * kGP + sr);
-                const float4 e4 = *reinterpret_cast<const float4*>(Esm + i * kGS1P + sc);
+                const float4 e4 = *reinterpret_cast<const float4*>(Esm + i * P + sc);
                 const float kv4[4] = {k4.x, k4.y, k4.z, k4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
                 for (int x = 0; x < 4; ++x)
@@ -644,25 +657,44 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
 #pragma unroll
             for (int x = 0; x < 4; ++x)
 #pragma unroll
-                for (int y = 0; y < 4; ++y) acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], 1);
-            // lane kh of the pair updates rows sr + 2 kh and sr + 2 kh + 1 of the tile
+                for (int y = 0; y < 4; ++y)
 #pragma unroll
-            for (int x2 = 0; x2 < 2; ++x2) {
-                const int x = 2 * kh + x2;
-                float* srow = Ssm + (sr + x) * kGS1P + sc;
-                const float4 s4 = *reinterpret_cast<const float4*>(srow);
-                const float a0 = kh ? acc[2 + x2][0] : acc[x2][0], a1 = kh ? acc[2 + x2][1] : acc[x2][1];
-                const float a2 = kh ? acc[2 + x2][2] : acc[x2][2], a3 = kh ? acc[2 + x2][3] : acc[x2][3];
-                *reinterpret_cast<float4*>(srow) =
-                    make_float4(gC * s4.x + a0, gC * s4.y + a1, gC * s4.z + a2, gC * s4.w + a3);
+                    for (int o = 1; o < KH; o <<= 1) acc[x][y] += __shfl_xor_sync(0xffffffffu, acc[x][y], o);
+            // the tile's 4 rows over the KH lanes of the group: RPL rows each (lanes past the
+            // 4 rows idle)
+            constexpr int RPL = KH >= 4 ? 1 : 4 / KH;
+#pragma unroll
+            for (int x2 = 0; x2 < RPL; ++x2) {
+                const int x = kh * RPL + x2;
+                if (x < 4) {
+                    float* srow = Ssm + (sr + x) * P + sc;
+                    const float4 s4 = *reinterpret_cast<const float4*>(srow);
+                    float a[4];
+#pragma unroll
+                    for (int y = 0; y < 4; ++y)
+                        a[y] = x == 0 ? acc[0][y] : (x == 1 ? acc[1][y] : (x == 2 ? acc[2][y] : acc[3][y]));
+                    *reinterpret_cast<float4*>(srow) =
+                        make_float4(gC * s4.x + a[0], gC * s4.y + a[1], gC * s4.z + a[2], gC * s4.w + a[3]);
+                }
             }
         }
         __syncthreads();  // new S visible; chunk c's buffer free for the fetch of chunk c + 2
     }
-    for (int e = tid; e < 128 * (kGS1 / 4); e += 256) {
-        const int r = e / (kGS1 / 4), c4 = (e % (kGS1 / 4)) * 4;
-        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * kGS1P + c4);
+    for (int e = tid; e < 128 * Q4; e += 256) {
+        const int r = e / Q4, c4 = (e % Q4) * 4;
+        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * P + c4);
     }
+}
+
+// Column-slice width of the state pass: the narrowest of 16 / 8 / 4 that keeps about a
+// wave of CTAs (QWC_GDN_STATE_COLS forces one).
+static int gdn_state_cols(int VH) {
+    const char* e = std::getenv("QWC_GDN_STATE_COLS");
+    const int forced = e ? std::atoi(e) : 0;
+    if (forced == 4 || forced == 8 || forced == 16) return forced;
+    int cols = 16;
+    while (cols > 4 && VH * (128 / cols) * 2 <= num_sms()) cols /= 2;
+    return cols;
 }
 
 // Kernel B2 on the tensor cores: per (chunk, value head) the outputs, transposed,
@@ -1100,7 +1132,14 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
     {
         cudaError_t e = cudaFuncSetAttribute(k_pf_gdn_chunk_a_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnATcSmem);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_pf_gdn_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnB1Smem);
+            e = cudaFuncSetAttribute(k_pf_gdn_state<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)GdnStateCfg<16>::Smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_pf_gdn_state<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)GdnStateCfg<8>::Smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_pf_gdn_state<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)GdnStateCfg<4>::Smem);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_pf_gdn_out_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdnOutSmem);
         if (e != cudaSuccess) return e;
@@ -1113,7 +1152,11 @@ cudaError_t pf_gdn(const PfGdnArgs& a, cudaStream_t s) {
         return cudaErrorInvalidValue;
     k_pf_gdn_chunk_a_tc<<<dim3(nch, a.VH), 128, kGdnATcSmem, s>>>(ck, a.err);
     if (a.ev_state0) cudaEventRecord(a.ev_state0, s);
-    k_pf_gdn_state<<<a.VH * (128 / kGS1), 256, kGdnB1Smem, s>>>(ck);
+    switch (gdn_state_cols(a.VH)) {
+        case 4: k_pf_gdn_state<4><<<a.VH * 32, 256, GdnStateCfg<4>::Smem, s>>>(ck); break;
+        case 8: k_pf_gdn_state<8><<<a.VH * 16, 256, GdnStateCfg<8>::Smem, s>>>(ck); break;
+        default: k_pf_gdn_state<16><<<a.VH * 8, 256, GdnStateCfg<16>::Smem, s>>>(ck); break;
+    }
     if (a.ev_state1) cudaEventRecord(a.ev_state1, s);
     k_pf_gdn_out_tc<<<dim3(nch, a.VH), 128, kGdnOutSmem, s>>>(mST, mQG, mET, mP, ck, a.err);
     return cudaGetLastError();

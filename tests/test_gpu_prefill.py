@@ -168,6 +168,51 @@ def test_tensor_core_attention_key_splits_match_unsplit_and_oracle(pkg, oracle, 
     m.close()
 
 
+@pytest.fixture
+def gdn_state_cols():
+    """Force the column-slice width of the GDN state pass (QWC_GDN_STATE_COLS, read per
+    call); restores the environment afterwards."""
+    old = os.environ.get("QWC_GDN_STATE_COLS")
+
+    def use(n):
+        os.environ["QWC_GDN_STATE_COLS"] = str(n)
+
+    yield use
+    if old is None:
+        os.environ.pop("QWC_GDN_STATE_COLS", None)
+    else:
+        os.environ["QWC_GDN_STATE_COLS"] = old
+
+
+@pytest.mark.parametrize("chunk", [96, 4096], indirect=True)
+@pytest.mark.parametrize("shape,T", [("tiny", 300), ("small-0.8b-widths", 203)])
+def test_gdn_state_pass_slice_widths_match(pkg, oracle, chunk, gdn_state_cols, shape, T):
+    """The GDN state pass with 8- and 4-column state slices (the tensor-parallel launch
+    shapes: the key-dim and token sums split over more lanes) against 16-column slices and
+    the oracle, across chunk boundaries; the decode state it leaves behind as well."""
+    d = model_dir(pkg, shape)
+    s = pkg.synth.SHAPES[shape]
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=43)
+    last = s.vocab_size > 4096
+    m = pkg.abi.Model(d, max_context=T + 8)
+    gdn_state_cols(16)
+    base = m.forward_logits(ids, last_only=last).reshape(-1, s.vocab_size)
+    base_next = m.prefill(ids)
+    base_step, _ = m.step(int(np.argmax(base_next)))
+    want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=last).reshape(-1, s.vocab_size)
+    for n in (8, 4):
+        gdn_state_cols(n)
+        got = m.forward_logits(ids, last_only=last).reshape(-1, s.vocab_size)
+        for i in range(got.shape[0]):
+            assert rel_l2(got[i], base[i]) < 1e-4, (n, i)
+            assert rel_l2(got[i], want[i]) < LOGIT_TOL, (n, i)
+        nxt = m.prefill(ids)
+        assert int(np.argmax(nxt)) == int(np.argmax(base_next))
+        step, _ = m.step(int(np.argmax(nxt)))
+        assert rel_l2(step, base_step) < 1e-4, n
+    m.close()
+
+
 @pytest.mark.parametrize("chunk", [96, 4096], indirect=True)
 @pytest.mark.parametrize("shape,T", [("tiny", 200), ("small-0.8b-widths", 150)])
 def test_per_layer_hidden_states_match_oracle(pkg, oracle, chunk, shape, T):

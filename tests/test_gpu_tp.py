@@ -49,22 +49,34 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("shape,world", [("tiny", 2), ("small-0.8b-widths", 2), ("small-0.8b-widths", 4),
-                                         ("small-0.8b-widths", 8)])
-def test_tp_prefill_matches_single_gpu_and_oracle(pkg, oracle, tmp_path, shape, world):
+@pytest.mark.parametrize("shape,world,fsplits", [("tiny", 2, None), ("small-0.8b-widths", 2, None),
+                                                 ("small-0.8b-widths", 2, 3), ("small-0.8b-widths", 4, None),
+                                                 ("small-0.8b-widths", 8, None)])
+def test_tp_prefill_matches_single_gpu_and_oracle(pkg, oracle, tmp_path, shape, world, fsplits):
+    """fsplits: the attention's key ranges forced (QWC_FATTN_SPLITS, inherited by the rank
+    processes) -- at T = 200 a rank's launch is otherwise too short to be split."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     d = model_dir(pkg, shape)
     s = pkg.synth.SHAPES[shape]
     T = 200
     ids = pkg.synth.random_prompt(s.vocab_size, T, seed=17)
-    mp.start_processes(_rank_main, args=(world, _free_port(), d, ids, T + 8, str(tmp_path)), nprocs=world,
-                       start_method="spawn")
+    old = os.environ.get("QWC_FATTN_SPLITS")
+    if fsplits:
+        os.environ["QWC_FATTN_SPLITS"] = str(fsplits)
+    try:
+        mp.start_processes(_rank_main, args=(world, _free_port(), d, ids, T + 8, str(tmp_path)), nprocs=world,
+                           start_method="spawn")
+        one = pkg.abi.Model(d, max_context=T + 8)
+        want1 = one.forward_logits(ids)
+        one.close()
+    finally:
+        if old is None:
+            os.environ.pop("QWC_FATTN_SPLITS", None)
+        else:
+            os.environ["QWC_FATTN_SPLITS"] = old
     got = np.load(tmp_path / "all.npy")
     last = np.load(tmp_path / "last.npy")
-    one = pkg.abi.Model(d, max_context=T + 8)
-    want1 = one.forward_logits(ids)
-    one.close()
     per_row = np.array([rel_l2(got[i], want1[i]) for i in range(T)])
     assert per_row.max() < 1e-4, per_row.max()  # same arithmetic, partial sums reordered
     assert rel_l2(last, got[-1]) < 1e-5

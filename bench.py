@@ -359,6 +359,9 @@ def run_prefill(args):
             "data": "synthetic", "config": prefill_config(name, T, WORLD, params),
             "roofline": f["roofline"], "e2e": f["e2e"], "gpu_launches": f["gpu_launches"], "clocks": clk,
             "last_argmax": int(np.argmax(lg))}
+    if WORLD > 1:  # which all-reduce combined the ranks' residual partials
+        line["config"]["allreduce"] = {1: "peer-memory (NVLink loads/stores)", 0: "nccl"}.get(m.tp_allreduce_path(),
+                                                                                          "undecided")
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = ref_prefill_sample(d, ids)
     m.close()

@@ -279,6 +279,14 @@ int qwc_create_from_dir_tp(const char* model_dir, int max_context, int kv_dtype,
  * counterpart (the reference runs on one CPU). */
 int qwc_tp_set_timeout(qwc_handle* h, int ms);
 
+/* Which all-reduce a tensor-parallel handle's batched passes use after the residual
+ * projections: 1 = the library's peer-memory all-reduce (every rank's residual buffer
+ * mapped into the others' address space over NVLink), 0 = NCCL's all-reduce
+ * (QWC_TP_ALLREDUCE=nccl, or the group could not set the peer mappings up), 2 = not
+ * decided yet (the first batched pass decides, collectively). QWC_E_INVALID for a
+ * single-GPU handle. */
+int qwc_tp_allreduce_path(qwc_handle* h);
+
 /* After qwc_prefill on a tensor-parallel group: gathers every rank's shard of the decode
  * state (GDN state and conv ring of its heads, KV of its kv heads for the T prefilled
  * positions) into `full`, a single-GPU handle of the same model on rank 0's device, over

@@ -29,7 +29,7 @@ EXPORTS = ("qwc_load_config", "qwc_default_config", "qwc_compute_budget", "qwc_s
            "qwc_enqueue_greedy", "qwc_read_tokens", "qwc_profile_step", "qwc_trace_step",
            "qwc_gemv_bf16", "qwc_gemm_bf16", "qwc_quantize_q8", "qwc_gemv_q8",
            "qwc_tp_shard_of", "qwc_tp_unique_id", "qwc_create_tp", "qwc_create_from_dir_tp",
-           "qwc_tp_gather_state", "qwc_max_context", "qwc_check_step_timeout", "qwc_tp_set_timeout",
+           "qwc_tp_gather_state", "qwc_max_context", "qwc_check_step_timeout", "qwc_tp_set_timeout", "qwc_tp_allreduce_path",
            "qwc_gdn_decode_step", "qwc_gdn_prefill", "qwc_gdn_prefill_workspace",
            "qwc_attention_decode")
 KERNEL_KINDS = {0: "mix_in", 1: "gdn", 2: "attn", 3: "mix_out", 4: "gate_up", 5: "down",
@@ -300,6 +300,14 @@ class Model:
         fn = lib().qwc_tp_set_timeout
         fn.argtypes = [C.c_void_p, C.c_int]
         check(fn(self._h, int(ms)), self._h)
+
+    def tp_allreduce_path(self) -> int:
+        """qwc_tp_allreduce_path: 1 peer-memory all-reduce, 0 NCCL, 2 not decided yet."""
+        fn = lib().qwc_tp_allreduce_path
+        fn.argtypes = [C.c_void_p]
+        r = int(fn(self._h))
+        check(min(r, 0), self._h)
+        return r
 
     def tp_gather_state(self, full: "Model | None"):
         """qwc_tp_gather_state: collective over the tensor-parallel group; rank 0 passes

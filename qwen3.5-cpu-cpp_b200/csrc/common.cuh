@@ -22,6 +22,7 @@ enum DevError : int {
     DEV_TC_MMA_TIMEOUT = 9,       // tensor-core GEMM: MMA issuer waited for operands
     DEV_TC_EPI_TIMEOUT = 10,      // tensor-core GEMM: epilogue waited for an accumulator
     DEV_TC_DRAIN_TIMEOUT = 11,    // tensor-core GEMM: in-flight copies / MMAs at exit
+    DEV_TP_BARRIER_TIMEOUT = 12,  // peer-memory all-reduce: a rank did not reach a barrier
 };
 
 __device__ __forceinline__ void post_error(int* flag, int code) {

@@ -8,6 +8,7 @@
 // graph (zero allocation per token), with token id, position and the greedy argmax
 // kept on the device.
 #include "qwen_cuda.h"
+#include "common.cuh"
 #include "kernels.h"
 
 #include <nccl.h>
@@ -138,6 +139,13 @@ struct qwc_handle {
     ncclComm_t nccl = nullptr;       // non-blocking communicator (calls are settled, waits bounded)
     int tp_timeout_ms = 300000;      // bound on every wait for the group (env QWC_TP_TIMEOUT_MS)
     bool nccl_aborted = false;       // the communicator was aborted: the handle refuses work
+    // peer-memory all-reduce of the residual stream (tp_p2p.cu); off after a failed setup
+    // vote or with QWC_TP_ALLREDUCE=nccl, in which case NCCL's all-reduce is used
+    P2pGroup* p2p = nullptr;
+    bool p2p_off = false;
+    int p2p_gen = 0;
+    unsigned long long p2p_epoch = 0;
+    uint64_t tp_group = 0;           // hash of the group's NCCL id: names the exchange sockets
     // QWC_PF_TIMING=1: per batched pass, the device time of the whole pass and of its
     // parts by category (event pairs from a pool reused across passes) on stderr
     bool pf_timing = false;
@@ -901,6 +909,7 @@ extern "C" void qwc_destroy(qwc_handle* h) {
     cudaFree(h->pf_ws);
     cudaFree(h->pf_kvs);
     cudaFree(h->pf_fa_part);
+    p2p_destroy(h->p2p);
     if (h->nccl) {
         // a communicator whose group is incomplete would block ncclCommDestroy: abort it
         ncclResult_t st = ncclSuccess;
@@ -1171,6 +1180,9 @@ static int create_impl(const qwc_config* cfg, const qwc_tensor* tensors, int n_t
         if (const char* e = std::getenv("QWC_TP_TIMEOUT_MS")) h->tp_timeout_ms = std::max(1, std::atoi(e));
         ncclUniqueId id;
         std::memcpy(&id, unique_id, sizeof(id));
+        uint64_t hsh = 1469598103934665603ull;  // FNV-1a of the id: the same on every rank
+        for (size_t i = 0; i < sizeof(id); ++i) hsh = (hsh ^ (uint8_t)id.internal[i]) * 1099511628211ull;
+        h->tp_group = hsh;
         ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
         ncfg.blocking = 0;  // every wait for the group is bounded (nccl_settle, stream_wait)
         const ncclResult_t r = ncclCommInitRankConfig(&h->nccl, world, id, rank, &ncfg);
@@ -1526,10 +1538,60 @@ static int pf_residual_gemm(qwc_handle* h, const CUtensorMap& mw, const uint16_t
     if (rc) return rc;
     const PfPair ar = pf_pair(h, PF_CAT_ALLREDUCE);
     pf_rec(h, ar.b);
-    rc = nccl_settle(h, ncclAllReduce(h->pf_hid, h->pf_hid, (size_t)Tc * h->H, ncclFloat32, ncclSum, h->nccl, h->stream),
-                     "ncclAllReduce");
-    if (rc) return rc;
+    if (h->p2p) {
+        const unsigned long long wait_ns = (unsigned long long)std::min(h->tp_timeout_ms, 60000) * 1000000ull;
+        CU(p2p_allreduce(h->p2p, (size_t)Tc * h->H, h->p2p_epoch, wait_ns, h->dev_err, h->stream));
+    } else {
+        rc = nccl_settle(h, ncclAllReduce(h->pf_hid, h->pf_hid, (size_t)Tc * h->H, ncclFloat32, ncclSum, h->nccl,
+                                          h->stream),
+                         "ncclAllReduce");
+        if (rc) return rc;
+    }
     pf_rec(h, ar.e);
+    return QWC_OK;
+}
+
+// Collective: the peer-memory all-reduce buffers for `floats` residual values per rank.
+// Every rank sets up (or declines: QWC_TP_ALLREDUCE=nccl) and the group votes; unless
+// every rank succeeded, all of them stay on NCCL's all-reduce for the handle's lifetime.
+static int p2p_ensure(qwc_handle* h, size_t floats) {
+    if (h->p2p_off || (h->p2p && p2p_capacity_floats(h->p2p) >= floats)) return QWC_OK;
+    int rc = stream_wait(h, "peer-memory setup");  // nothing of this rank in flight
+    if (rc) return rc;
+    p2p_destroy(h->p2p);  // the peers no longer use it: the last pass ended with a group barrier
+    h->p2p = nullptr;
+    P2pGroup* g = nullptr;
+    const char* e = std::getenv("QWC_TP_ALLREDUCE");
+    int mine = (e && std::strcmp(e, "nccl") == 0) ? 0 : 1;
+    if (mine) {
+        std::string why;
+        const int tmo = std::min(h->tp_timeout_ms, 60000);
+        if (p2p_setup(&g, h->tp_rank, h->tp_world, h->device, h->tp_group, ++h->p2p_gen, floats * sizeof(float), tmo,
+                      why) != 0) {
+            std::fprintf(stderr, "[qwc] rank %d: peer-memory all-reduce unavailable (%s); using NCCL\n", h->tp_rank,
+                         why.c_str());
+            mine = 0;
+        }
+    }
+    h->h_pin[5] = mine;
+    CU(cudaMemcpyAsync(h->tp_vote, &h->h_pin[5], sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    rc = nccl_settle(h, ncclAllReduce(h->tp_vote, h->tp_vote, 1, ncclInt32, ncclMin, h->nccl, h->stream),
+                     "peer-memory setup: vote");
+    if (rc) {
+        p2p_destroy(g);
+        return rc;
+    }
+    CU(cudaMemcpyAsync(&h->h_pin[5], h->tp_vote, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    if ((rc = stream_wait(h, "peer-memory setup"))) {
+        p2p_destroy(g);
+        return rc;
+    }
+    if (h->h_pin[5] == 1) {
+        h->p2p = g;
+    } else {
+        p2p_destroy(g);
+        h->p2p_off = true;
+    }
     return QWC_OK;
 }
 
@@ -1547,6 +1609,10 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
     const int chunk = pf_chunk(h);
     rc = pf_workspace(h, std::min(T, chunk));
     if (rc) return rc;
+    if (h->tp_world > 1) {  // the residual stream lives in the peer-mapped buffer when there is one
+        if ((rc = p2p_ensure(h, (size_t)std::min(T, chunk) * h->H))) return rc;
+        if (h->p2p) h->pf_hid = p2p_local_data(h->p2p);
+    }
     const int H = h->H;
     h->pf_ev_used = 0;
     h->pf_pair_cat.clear();
@@ -1719,7 +1785,15 @@ static int pf_run(qwc_handle* h, const StateView& sv, const int* ids, int T, int
     if (h->pf_timing) CU(cudaEventRecord(h->pf_ev[1], h->stream));
     if ((rc = stream_wait(h, "prefill"))) return rc;
     pf_timing_report(h, T);
-    return check_device_error(h);
+    rc = check_device_error(h);
+    if (rc && h->p2p && h->h_pin[8] == DEV_TP_BARRIER_TIMEOUT) {
+        // a peer-memory barrier may have run out: the group's epochs no longer agree
+        p2p_destroy(h->p2p);
+        h->p2p = nullptr;
+        h->p2p_off = true;
+        return tp_abort(h, h->err + " (tensor-parallel pass)");
+    }
+    return rc;
 }
 
 extern "C" int qwc_prefill(qwc_handle* h, const int* ids, int T, float* logits_out, int last_only) {
@@ -1752,6 +1826,12 @@ extern "C" int qwc_tp_set_timeout(qwc_handle* h, int ms) {
     if (!h || h->tp_world < 2 || ms <= 0) return fail(h, QWC_E_INVALID, "qwc_tp_set_timeout: needs a tensor-parallel handle and ms > 0");
     h->tp_timeout_ms = ms;
     return QWC_OK;
+}
+
+extern "C" int qwc_tp_allreduce_path(qwc_handle* h) {
+    if (!h || h->tp_world < 2) return fail(h, QWC_E_INVALID, "qwc_tp_allreduce_path: needs a tensor-parallel handle");
+    if (h->p2p) return 1;
+    return h->p2p_off ? 0 : 2;
 }
 
 extern "C" int qwc_tp_gather_state(qwc_handle* tp, qwc_handle* full) {

@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <string>
+
 namespace qwc {
 
 // ------------------------------------------------------------------ GEMV family
@@ -271,6 +273,27 @@ cudaError_t pf_fattn(const PfFattnArgs& a, cudaStream_t s);
 int pf_fattn_splits(int T, int p0, int NQ, int NKV);
 constexpr int kFattnMaxSplits = 16;
 cudaError_t pf_add(float* y, const float* x, size_t n, cudaStream_t s);  // y += x (16-byte aligned)
+
+// Peer-memory all-reduce of the tensor-parallel residual stream (tp_p2p.cu).
+constexpr int kP2pMaxRanks = 8;
+struct P2pPtrs {
+    unsigned long long* flags[kP2pMaxRanks];  // every rank's barrier flags, as mapped here
+    float* data[kP2pMaxRanks];                // every rank's residual buffer, as mapped here
+    int world, rank;
+};
+struct P2pGroup;
+// Collective over the group: every rank allocates an exportable buffer of data_bytes,
+// exchanges it with the others (abstract Unix sockets named by `group` and `gen`, bounded
+// by timeout_ms) and maps theirs. Returns 0, or -1 with `why` (nothing left allocated).
+int p2p_setup(P2pGroup** out, int rank, int world, int device, uint64_t group, int gen, size_t data_bytes,
+              int timeout_ms, std::string& why);
+void p2p_destroy(P2pGroup* g);
+float* p2p_local_data(P2pGroup* g);
+size_t p2p_capacity_floats(const P2pGroup* g);
+// In-place sum of n floats over the group's buffers (barrier, reduce, barrier); `epoch`
+// advances by 2 and must advance identically on every rank.
+cudaError_t p2p_allreduce(P2pGroup* g, size_t n, unsigned long long& epoch, unsigned long long wait_ns, int* err,
+                          cudaStream_t s);
 
 // Records a handle-less failure message (what qwc_last_error(NULL) returns).
 void set_api_error(const char* msg);

@@ -34,6 +34,7 @@ def _rank_main(rank, world, port, d, ids, max_ctx, out_dir):
         if rank == 0:
             np.save(os.path.join(out_dir, "all.npy"), all_rows)
             np.save(os.path.join(out_dir, "last.npy"), last)
+            np.save(os.path.join(out_dir, "path.npy"), np.array([m.tp_allreduce_path()]))
         dist.barrier()
         m.close()
     finally:
@@ -82,6 +83,44 @@ def test_tp_prefill_matches_single_gpu_and_oracle(pkg, oracle, tmp_path, shape, 
     assert rel_l2(last, got[-1]) < 1e-5
     want = oracle.OracleModel(d, T + 8).prefill(ids, last_only=True)
     assert rel_l2(got[-1], want.reshape(-1)[-s.vocab_size:]) < 2e-3
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_peer_memory_allreduce_matches_nccl(pkg, tmp_path, world):
+    """The library's peer-memory all-reduce (ranks' residual buffers mapped over NVLink,
+    summed in rank order) against NCCL's all-reduce of the same partials: on two ranks the
+    sums are the same two terms, so the logits are identical; on more ranks the summation
+    order differs, within rel_l2 1e-5. The handle reports which path it took."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    d = model_dir(pkg, "small-0.8b-widths")
+    s = pkg.synth.SHAPES["small-0.8b-widths"]
+    T = 200
+    ids = pkg.synth.random_prompt(s.vocab_size, T, seed=19)
+    got = {}
+    for mode in ("peer", "nccl"):
+        out = tmp_path / mode
+        out.mkdir()
+        old = os.environ.get("QWC_TP_ALLREDUCE")
+        if mode == "nccl":
+            os.environ["QWC_TP_ALLREDUCE"] = "nccl"
+        else:
+            os.environ.pop("QWC_TP_ALLREDUCE", None)
+        try:
+            mp.start_processes(_rank_main, args=(world, _free_port(), d, ids, T + 8, str(out)), nprocs=world,
+                               start_method="spawn")
+        finally:
+            if old is None:
+                os.environ.pop("QWC_TP_ALLREDUCE", None)
+            else:
+                os.environ["QWC_TP_ALLREDUCE"] = old
+        got[mode] = (np.load(out / "all.npy"), int(np.load(out / "path.npy")[0]))
+    assert got["peer"][1] == 1 and got["nccl"][1] == 0
+    a, b = got["peer"][0], got["nccl"][0]
+    if world == 2:
+        assert np.array_equal(a, b)
+    per_row = np.array([rel_l2(a[i], b[i]) for i in range(T)])
+    assert per_row.max() < 1e-5, per_row.max()
 
 
 def _gather_main(rank, world, port, d, ids, n_new, max_ctx, out_dir):

@@ -377,29 +377,41 @@ __device__ __forceinline__ void st_cg4(float* p, float4 v) {
 }
 
 // Slice `rank` of n floats (n % 4 == 0): sum over the ranks' buffers in rank order, the
-// sum stored into every rank's buffer. Skipped entirely after a barrier error.
+// sum stored into every rank's buffer. Skipped entirely after a barrier error. Each thread
+// takes two elements a grid stride apart with all their loads issued first (peer loads
+// cross NVLink: more of them in flight).
 __global__ void __launch_bounds__(256) k_p2p_reduce(const P2pPtrs P, long long n4, const int* err) {
     if (*reinterpret_cast<const volatile int*>(err) != 0) return;
     const long long per = (n4 + P.world - 1) / P.world;
     const long long a = (long long)P.rank * per, b = a + per < n4 ? a + per : n4;
     const long long stride = (long long)gridDim.x * blockDim.x;
-    for (long long i = a + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < b; i += stride) {
-        float4 v[kP2pMaxRanks];
+    for (long long i = a + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < b; i += 2 * stride) {
+        const long long i2 = i + stride;
+        const bool two = i2 < b;
+        float4 v[2][kP2pMaxRanks];
 #pragma unroll
         for (int q = 0; q < kP2pMaxRanks; ++q)
-            if (q < P.world) v[q] = ld_cg4(P.data[q] + 4 * i);
-        float4 s = v[0];
-#pragma unroll
-        for (int q = 1; q < kP2pMaxRanks; ++q)
             if (q < P.world) {
-                s.x += v[q].x;
-                s.y += v[q].y;
-                s.z += v[q].z;
-                s.w += v[q].w;
+                v[0][q] = ld_cg4(P.data[q] + 4 * i);
+                if (two) v[1][q] = ld_cg4(P.data[q] + 4 * i2);
             }
 #pragma unroll
-        for (int q = 0; q < kP2pMaxRanks; ++q)
-            if (q < P.world) st_cg4(P.data[q] + 4 * i, s);
+        for (int u = 0; u < 2; ++u) {
+            if (u == 1 && !two) break;
+            float4 s = v[u][0];
+#pragma unroll
+            for (int q = 1; q < kP2pMaxRanks; ++q)
+                if (q < P.world) {
+                    s.x += v[u][q].x;
+                    s.y += v[u][q].y;
+                    s.z += v[u][q].z;
+                    s.w += v[u][q].w;
+                }
+            const long long e = u == 0 ? i : i2;
+#pragma unroll
+            for (int q = 0; q < kP2pMaxRanks; ++q)
+                if (q < P.world) st_cg4(P.data[q] + 4 * e, s);
+        }
     }
 }
 

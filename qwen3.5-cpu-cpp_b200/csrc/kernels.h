@@ -272,7 +272,6 @@ cudaError_t pf_fattn(const PfFattnArgs& a, cudaStream_t s);
 // Key splits pf_fattn uses for a chunk of T queries at positions p0.. (grows with p0).
 int pf_fattn_splits(int T, int p0, int NQ, int NKV);
 constexpr int kFattnMaxSplits = 16;
-cudaError_t pf_add(float* y, const float* x, size_t n, cudaStream_t s);  // y += x (16-byte aligned)
 
 // Peer-memory all-reduce of the tensor-parallel residual stream (tp_p2p.cu).
 constexpr int kP2pMaxRanks = 8;

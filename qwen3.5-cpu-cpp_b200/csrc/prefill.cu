@@ -1091,25 +1091,7 @@ __global__ void __launch_bounds__(256, 1) k_pf_attn(const PfAttn p) {
     }
 }
 
-// ---------------------------------------------------------------- y += x
-__global__ void k_pf_add(float* y, const float* x, size_t n) {
-    const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (i + 3 < n) {
-        float4 a = *reinterpret_cast<float4*>(y + i);
-        const float4 b = *reinterpret_cast<const float4*>(x + i);
-        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-        *reinterpret_cast<float4*>(y + i) = a;
-    } else {
-        for (size_t j = i; j < n; ++j) y[j] += x[j];
-    }
-}
-
 // ---------------------------------------------------------------- launchers
-cudaError_t pf_add(float* y, const float* x, size_t n, cudaStream_t s) {
-    const size_t threads = (n + 3) / 4;
-    k_pf_add<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(y, x, n);
-    return cudaGetLastError();
-}
 cudaError_t pf_embed(const int* ids, int T, const uint16_t* embed, int H, int V, float* hid, int* err,
                      cudaStream_t s) {
     k_pf_embed<<<T, kPT, 0, s>>>(ids, embed, H, V, hid, err);

@@ -352,11 +352,15 @@ __global__ void k_p2p_barrier(const P2pPtrs P, unsigned long long epoch, unsigne
         unsigned long long* slot = P.flags[lane] + P.rank;
         asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(epoch) : "memory");
         const unsigned long long* f = P.flags[P.rank] + lane;
+        const volatile int* e = err;
         const unsigned long long t0 = globaltimer_ns();
-        for (;;) {
+        for (unsigned it = 0;; ++it) {
             unsigned long long v;
             asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
             if (v >= epoch) break;
+            // an earlier barrier of this pass ran out: the group is already lost, do not
+            // wait again (every later barrier of the pass returns at once)
+            if ((it & 63u) == 0 && *e != 0) break;
             if (globaltimer_ns() - t0 > wait_ns) {
                 post_error(err, DEV_TP_BARRIER_TIMEOUT);
                 break;

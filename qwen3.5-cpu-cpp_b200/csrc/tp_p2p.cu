@@ -127,11 +127,12 @@ bool recv_fd(int sock, Msg& m, int& fd) {
     h.msg_iovlen = 1;
     h.msg_control = cbuf;
     h.msg_controllen = sizeof(cbuf);
-    if (recvmsg(sock, &h, 0) != (ssize_t)sizeof(m)) return false;
-    cmsghdr* c = CMSG_FIRSTHDR(&h);
-    if (!c || c->cmsg_level != SOL_SOCKET || c->cmsg_type != SCM_RIGHTS) return false;
-    std::memcpy(&fd, CMSG_DATA(c), sizeof(int));
-    return m.magic == kP2pMagic;
+    const ssize_t n = recvmsg(sock, &h, 0);
+    // a descriptor that arrived is taken (and closed by the caller on failure) even when
+    // the message around it is short, so none stays open unnoticed
+    cmsghdr* c = n > 0 ? CMSG_FIRSTHDR(&h) : nullptr;
+    if (c && c->cmsg_level == SOL_SOCKET && c->cmsg_type == SCM_RIGHTS) std::memcpy(&fd, CMSG_DATA(c), sizeof(int));
+    return n == (ssize_t)sizeof(m) && fd >= 0 && m.magic == kP2pMagic;
 }
 
 struct Mapping {

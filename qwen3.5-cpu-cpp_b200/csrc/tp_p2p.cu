@@ -149,29 +149,29 @@ void unmap(Mapping& m) {
     if (m.handle) d.release(m.handle);
     m = Mapping();
 }
+// Maps allocation `h` into a fresh address range with read/write access for `device`. On
+// failure nothing stays reserved or mapped, `m` is left empty and the caller still owns `h`.
 bool map_handle(Mapping& m, CUmemGenericAllocationHandle h, size_t size, int device) {
     const DriverFns& d = drv();
-    m.handle = h;
-    m.size = size;
-    if (d.reserve(&m.va, size, 0, 0, 0) != CUDA_SUCCESS) {
-        m.va = 0;
-        return false;
-    }
-    if (d.map(m.va, size, 0, h, 0) != CUDA_SUCCESS) {
-        d.addr_free(m.va, size);
-        m.va = 0;
+    m = Mapping();
+    CUdeviceptr va = 0;
+    if (d.reserve(&va, size, 0, 0, 0) != CUDA_SUCCESS) return false;
+    if (d.map(va, size, 0, h, 0) != CUDA_SUCCESS) {
+        d.addr_free(va, size);
         return false;
     }
     CUmemAccessDesc acc{};
     acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
     acc.location.id = device;
     acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-    if (d.set_access(m.va, size, &acc, 1) != CUDA_SUCCESS) {
-        d.unmap(m.va, size);
-        d.addr_free(m.va, size);
-        m.va = 0;
+    if (d.set_access(va, size, &acc, 1) != CUDA_SUCCESS) {
+        d.unmap(va, size);
+        d.addr_free(va, size);
         return false;
     }
+    m.handle = h;
+    m.va = va;
+    m.size = size;
     return true;
 }
 

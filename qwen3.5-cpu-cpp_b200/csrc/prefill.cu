@@ -503,12 +503,22 @@ __global__ void __launch_bounds__(128, 1) k_pf_gdn_chunk_a_tc(const PfGdnChunk p
 // it has. The arithmetic per chunk is proportional to WS and the fetch is not: with many
 // value heads (one GPU) 16-column slices fill the SMs; a tensor-parallel rank holds VH / N
 // heads, and narrower slices (8, 4 columns) give it as many CTAs and a shorter chunk step.
-constexpr int kWtP = kGC + 4;         // padded stride of the W^T rows
+// Shared-memory strides (floats), chosen so that the float4 reads of the two products take
+// the fewest wavefronts: in E = U - W S a warp reads W^T rows kq (the key-dim split) x 2
+// token quads and S rows kq x the slice's column quads; in the update, Kd rows kh x 4
+// key-dim quads and E rows kh x the column quads. A W^T stride = 8 (mod 32) banks, a Kd
+// stride = 16 (mod 32) and unpadded S rows put those sets on distinct bank groups (with the
+// earlier strides 68 / 132 / WS + 4, 39 % of the shared-memory wavefronts of a launch were
+// bank conflicts and short-scoreboard stalls were 45 % of the samples). E and U keep WS + 4:
+// E is also read transposed (one token per lane) for its bf16-pair copy.
+constexpr int kWtP = kGC + 8;          // W^T rows
+constexpr int kKdP = 128 + 16;         // Kd rows
 template <int WS>
 struct GdnStateCfg {
-    static constexpr int P = WS + 4;                                // padded stride of [.][WS] tiles
-    static constexpr int Buf = 128 * kWtP + kGC * kGP + kGC * P;    // floats per chunk buffer: W^T, Kd, U slice
-    static constexpr size_t Smem = (size_t)(2 * Buf + 128 * P + kGC * P) * 4;
+    static constexpr int P = WS + 4;                                // stride of the E and U tiles
+    static constexpr int PS = WS;                                   // stride of the S tile
+    static constexpr int Buf = 128 * kWtP + kGC * kKdP + kGC * P;   // floats per chunk buffer: W^T, Kd, U slice
+    static constexpr size_t Smem = (size_t)(2 * Buf + 128 * PS + kGC * P) * 4;
     static constexpr int KS = 64 / WS;   // E = U - W S: lanes sharing one 4 x 4 tile (key-dim split)
     static constexpr int KH = 32 / WS;   // S update: lanes sharing one 4 x 4 tile (token split)
     static_assert(WS == 4 || WS == 8 || WS == 16, "state slice width");
@@ -521,16 +531,16 @@ __device__ __forceinline__ void cp16(float* dst, const float* src, bool pred) {
 template <int WS>
 __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
     using C = GdnStateCfg<WS>;
-    constexpr int P = C::P, KS = C::KS, KH = C::KH, Q4 = WS / 4;
+    constexpr int P = C::P, PS = C::PS, KS = C::KS, KH = C::KH, Q4 = WS / 4;
     extern __shared__ __align__(16) float sb[];
-    float* Ssm = sb + 2 * C::Buf;        // [128][P]
-    float* Esm = Ssm + 128 * P;          // [64][P]
+    float* Ssm = sb + 2 * C::Buf;        // [128][PS]
+    float* Esm = Ssm + 128 * PS;         // [64][P]
     const int vh = blockIdx.x / (128 / WS), sl = blockIdx.x % (128 / WS), tid = threadIdx.x;
     const int nch = (p.T + kGC - 1) / kGC;
     float* Sg = p.state + (size_t)vh * 128 * 128 + sl * WS;
     for (int e = tid; e < 128 * Q4; e += 256) {
         const int r = e / Q4, c4 = (e % Q4) * 4;
-        *reinterpret_cast<float4*>(Ssm + r * P + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
+        *reinterpret_cast<float4*>(Ssm + r * PS + c4) = *reinterpret_cast<const float4*>(Sg + (size_t)r * 128 + c4);
     }
     auto fetch = [&](int c) {
         float* B = sb + (c & 1) * C::Buf;
@@ -545,11 +555,11 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
         for (int e = tid; e < kGC * 32; e += 256) {
             const int i = e >> 5, c4 = (e & 31) * 4;
             const size_t off = hrow + (size_t)(i < n ? i : 0) * 128 + c4;
-            cp16(Bk + i * kGP + c4, p.KD + off, i < n);
+            cp16(Bk + i * kKdP + c4, p.KD + off, i < n);
         }
         for (int e = tid; e < kGC * Q4; e += 256) {
             const int i = e / Q4, c4 = (e % Q4) * 4;
-            cp16(Bk + kGC * kGP + i * P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * WS + c4, i < n);
+            cp16(Bk + kGC * kKdP + i * P + c4, p.U + hrow + (size_t)(i < n ? i : 0) * 128 + sl * WS + c4, i < n);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -567,9 +577,9 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();  // chunk c's operands and the state are visible to every thread
-        const float* Wts = sb + (c & 1) * C::Buf;  // W^T [128][68]
-        const float* Ksm = Wts + 128 * kWtP;         // Kd [64][132]
-        const float* Usm = Ksm + kGC * kGP;          // U slice [64][P]
+        const float* Wts = sb + (c & 1) * C::Buf;  // W^T [128][kWtP]
+        const float* Ksm = Wts + 128 * kWtP;         // Kd [64][kKdP]
+        const float* Usm = Ksm + kGC * kKdP;          // U slice [64][P]
         // the state entering chunk c, transposed (rows = value dims) as bf16 pairs, for the
         // output kernel: thread -> key dim k = tid % 128 and WS / 2 value dims from
         // (tid / 128) WS / 2 (a warp's stores cover 32 consecutive key dims)
@@ -577,10 +587,21 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             constexpr int V = WS / 2;
             const int k = tid & 127, d0 = (tid >> 7) * V;
             uint16_t* st = p.ST + (((size_t)vh * nch + c) * 2 * 128 + sl * WS + d0) * 128 + k;
+            float v[V];
+            if constexpr (V % 4 == 0) {  // vector reads of the row (fewer wavefronts than scalars)
+#pragma unroll
+                for (int q = 0; q < V / 4; ++q) {
+                    const float4 f = *reinterpret_cast<const float4*>(Ssm + k * PS + d0 + 4 * q);
+                    v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < V; ++u) v[u] = Ssm[k * PS + d0 + u];
+            }
 #pragma unroll
             for (int u = 0; u < V; ++u) {
                 uint16_t hi, lo;
-                split_bf16(Ssm[k * P + d0 + u], hi, lo);
+                split_bf16(v[u], hi, lo);
                 st[u * 128] = hi;
                 st[128 * 128 + u * 128] = lo;
             }
@@ -596,7 +617,7 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             for (int it = 0; it < 128 / KS; ++it) {
                 const int r = it * KS + kq;
                 const float4 w4 = *reinterpret_cast<const float4*>(Wts + r * kWtP + ei);
-                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * P + ec);
+                const float4 s4 = *reinterpret_cast<const float4*>(Ssm + r * PS + ec);
                 const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
                 for (int x = 0; x < 4; ++x)
@@ -646,7 +667,7 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
 #pragma unroll 4
             for (int it = 0; it < kGC / KH; ++it) {  // rows past the chunk's tokens are zero
                 const int i = it * KH + kh;
-                const float4 k4 = *reinterpret_cast<const float4*>(Ksm + i * kGP + sr);
+                const float4 k4 = *reinterpret_cast<const float4*>(Ksm + i * kKdP + sr);
                 const float4 e4 = *reinterpret_cast<const float4*>(Esm + i * P + sc);
                 const float kv4[4] = {k4.x, k4.y, k4.z, k4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
@@ -667,7 +688,7 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
             for (int x2 = 0; x2 < RPL; ++x2) {
                 const int x = kh * RPL + x2;
                 if (x < 4) {
-                    float* srow = Ssm + (sr + x) * P + sc;
+                    float* srow = Ssm + (sr + x) * PS + sc;
                     const float4 s4 = *reinterpret_cast<const float4*>(srow);
                     float a[4];
 #pragma unroll
@@ -682,7 +703,7 @@ __global__ void __launch_bounds__(256) k_pf_gdn_state(const PfGdnChunk p) {
     }
     for (int e = tid; e < 128 * Q4; e += 256) {
         const int r = e / Q4, c4 = (e % Q4) * 4;
-        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * P + c4);
+        *reinterpret_cast<float4*>(Sg + (size_t)r * 128 + c4) = *reinterpret_cast<const float4*>(Ssm + r * PS + c4);
     }
 }
 

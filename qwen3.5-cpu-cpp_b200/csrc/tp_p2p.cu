@@ -14,7 +14,8 @@
 //
 // Memory: each buffer is a driver virtual-memory allocation exported as a POSIX file
 // descriptor; the descriptors travel to the other ranks over abstract Unix sockets named
-// after the group's NCCL id, and every rank imports and maps the others. An imported
+// after the group's NCCL id (exchange_fds, host/src/fd_exchange.cpp), and every rank
+// imports and maps the others. An imported
 // allocation stays alive while it is mapped, so a rank that exits does not unmap the
 // others' view of its memory. No multicast object is created. Before use, every rank
 // reads a token each peer wrote into its buffer through the mapping (a host-driven copy),
@@ -27,27 +28,21 @@
 // the error word and touches no peer memory, and the host aborts the group.
 #include "common.cuh"
 #include "kernels.h"
+#include "../host/src/fd_exchange.h"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
-#include <poll.h>
-#include <sys/socket.h>
-#include <sys/un.h>
 #include <unistd.h>
 
-#include <algorithm>
-#include <cerrno>
-#include <chrono>
-#include <cstdio>
 #include <cstring>
-#include <thread>
 
 namespace qwc {
 
 namespace {
 
 constexpr size_t kP2pHeader = 256;  // [0, 64): flags[8] (epochs); [128, 136): the setup token
-constexpr uint32_t kP2pMagic = 0x71776332u;
+constexpr uint32_t kP2pMagic = 0x71776332u;  // in the setup token
+static_assert(kP2pMaxRanks <= kFdExchangeMaxRanks, "descriptor exchange group size");
 
 struct DriverFns {
     PFN_cuMemCreate_v10020 create = nullptr;
@@ -83,56 +78,6 @@ const DriverFns& drv() {
         return x;
     }();
     return d;
-}
-
-double now_ms() {
-    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
-}
-
-// abstract socket address of (group, generation, rank)
-socklen_t sock_addr(sockaddr_un& a, uint64_t group, int gen, int rank) {
-    std::memset(&a, 0, sizeof(a));
-    a.sun_family = AF_UNIX;
-    const int n = std::snprintf(a.sun_path + 1, sizeof(a.sun_path) - 1, "qwc-p2p-%016llx-%d-%d",
-                                (unsigned long long)group, gen, rank);
-    return (socklen_t)(offsetof(sockaddr_un, sun_path) + 1 + n);
-}
-
-struct Msg {
-    uint32_t magic, rank;
-    uint64_t bytes;
-};
-
-bool send_fd(int sock, const Msg& m, int fd) {
-    iovec iov{const_cast<Msg*>(&m), sizeof(m)};
-    alignas(cmsghdr) char cbuf[CMSG_SPACE(sizeof(int))];
-    std::memset(cbuf, 0, sizeof(cbuf));
-    msghdr h{};
-    h.msg_iov = &iov;
-    h.msg_iovlen = 1;
-    h.msg_control = cbuf;
-    h.msg_controllen = sizeof(cbuf);
-    cmsghdr* c = CMSG_FIRSTHDR(&h);
-    c->cmsg_level = SOL_SOCKET;
-    c->cmsg_type = SCM_RIGHTS;
-    c->cmsg_len = CMSG_LEN(sizeof(int));
-    std::memcpy(CMSG_DATA(c), &fd, sizeof(int));
-    return sendmsg(sock, &h, MSG_NOSIGNAL) == (ssize_t)sizeof(m);
-}
-bool recv_fd(int sock, Msg& m, int& fd) {
-    iovec iov{&m, sizeof(m)};
-    alignas(cmsghdr) char cbuf[CMSG_SPACE(sizeof(int))];
-    msghdr h{};
-    h.msg_iov = &iov;
-    h.msg_iovlen = 1;
-    h.msg_control = cbuf;
-    h.msg_controllen = sizeof(cbuf);
-    const ssize_t n = recvmsg(sock, &h, 0);
-    // a descriptor that arrived is taken (and closed by the caller on failure) even when
-    // the message around it is short, so none stays open unnoticed
-    cmsghdr* c = n > 0 ? CMSG_FIRSTHDR(&h) : nullptr;
-    if (c && c->cmsg_level == SOL_SOCKET && c->cmsg_type == SCM_RIGHTS) std::memcpy(&fd, CMSG_DATA(c), sizeof(int));
-    return n == (ssize_t)sizeof(m) && fd >= 0 && m.magic == kP2pMagic;
 }
 
 struct Mapping {
@@ -239,71 +184,13 @@ int p2p_setup(P2pGroup** out, int rank, int world, int device, uint64_t group, i
     int fd = -1;
     if (d.export_h(&fd, own, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0) != CUDA_SUCCESS || fd < 0)
         return bail("cuMemExportToShareableHandle failed");
-    // ---- exchange descriptors: listen, send ours to every peer, receive every peer's
-    const int lsock = socket(AF_UNIX, SOCK_STREAM | SOCK_CLOEXEC, 0);
-    if (lsock < 0) {
-        close(fd);
-        return bail("socket failed");
-    }
-    sockaddr_un la;
-    const socklen_t llen = sock_addr(la, group, gen, rank);
-    if (bind(lsock, reinterpret_cast<sockaddr*>(&la), llen) != 0 || listen(lsock, kP2pMaxRanks) != 0) {
-        close(lsock);
-        close(fd);
-        return bail(std::string("bind/listen: ") + std::strerror(errno));
-    }
-    const double t0 = now_ms();
-    bool ok = true;
-    for (int q = 0; q < world && ok; ++q) {
-        if (q == rank) continue;
-        sockaddr_un pa;
-        const socklen_t plen = sock_addr(pa, group, gen, q);
-        for (;;) {
-            const int s = socket(AF_UNIX, SOCK_STREAM | SOCK_CLOEXEC, 0);
-            if (s >= 0 && connect(s, reinterpret_cast<sockaddr*>(&pa), plen) == 0) {
-                const Msg m{kP2pMagic, (uint32_t)rank, (uint64_t)g->bytes};
-                ok = send_fd(s, m, fd);
-                close(s);
-                if (!ok) why = "sending the descriptor failed";
-                break;
-            }
-            if (s >= 0) close(s);
-            if (now_ms() - t0 > timeout_ms) {
-                ok = false;
-                why = "rank " + std::to_string(q) + " did not open its exchange socket in time";
-                break;
-            }
-            std::this_thread::sleep_for(std::chrono::milliseconds(2));
-        }
-    }
-    close(fd);
+    // ---- exchange descriptors with the other ranks (bounded by timeout_ms)
     int fds[kP2pMaxRanks];
-    uint64_t sizes[kP2pMaxRanks] = {};
-    for (int q = 0; q < kP2pMaxRanks; ++q) fds[q] = -1;
-    for (int got = 0; ok && got < world - 1;) {
-        pollfd p{lsock, POLLIN, 0};
-        const int left = (int)std::max(1.0, timeout_ms - (now_ms() - t0));
-        if (poll(&p, 1, left) <= 0) {
-            ok = false;
-            why = "a rank's descriptor did not arrive in time";
-            break;
-        }
-        const int s = accept4(lsock, nullptr, nullptr, SOCK_CLOEXEC);
-        if (s < 0) continue;
-        timeval tv{5, 0};
-        setsockopt(s, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
-        Msg m{};
-        int rfd = -1;
-        if (recv_fd(s, m, rfd) && (int)m.rank < world && (int)m.rank != rank && fds[m.rank] < 0) {
-            fds[m.rank] = rfd;
-            sizes[m.rank] = m.bytes;
-            ++got;
-        } else if (rfd >= 0) {
-            close(rfd);
-        }
-        close(s);
-    }
-    close(lsock);
+    uint64_t sizes[kP2pMaxRanks];
+    const bool ok_x = exchange_fds(group, gen, rank, world, fd, (uint64_t)g->bytes, timeout_ms, fds, sizes, why);
+    close(fd);
+    if (!ok_x) return bail(why);
+    bool ok = true;
     // ---- import and map every peer's allocation
     for (int q = 0; q < world && ok; ++q) {
         if (q == rank) continue;
@@ -320,7 +207,7 @@ int p2p_setup(P2pGroup** out, int rank, int world, int device, uint64_t group, i
             why = "mapping rank " + std::to_string(q) + "'s allocation failed";
         }
     }
-    for (int q = 0; q < kP2pMaxRanks; ++q)
+    for (int q = 0; q < world; ++q)
         if (fds[q] >= 0) close(fds[q]);
     if (!ok) return bail(why);
     // ---- every peer's token through the mapping
